@@ -1,0 +1,257 @@
+"""Drop-in replacement for the reference's ``gaussian_rasterizer`` torch extension.
+
+Exports the ten entry points of gaussian_splatting/rasterizer/bindings.cpp:4-43 with the same
+argument order, tensor layouts, return tuples and error messages, implemented on libhds_b200.so.
+Outputs are allocated with torch's caching allocator on the inputs' device and all work is queued
+on the current CUDA stream.  Two additive entry points serve this package's own autograd layer:
+``rasterize_with_features`` (one walk producing RGB and features) and ``eval_sh_backward`` (plain
+SH gradients, for data-parallel training that all-reduces them).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from .native import check, lib, ptr, stream_of
+
+TILE = 16
+_F32 = torch.float32
+_I32 = torch.int32
+
+
+def _check(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+
+
+def _tiles(width: int, height: int) -> int:
+    return ((width + TILE - 1) // TILE) * ((height + TILE - 1) // TILE)
+
+
+def _bin(means2D, depths, radii, conics, colors, opacities, width, height, keep_keys=False):
+    """forward.cu:262-404: pack, count, scan, (host read), emit, sort, ranges.
+
+    Returns (conic [N,4], color_opacity [N,4], values_sorted, tile_ranges [T,2], keys_sorted or None)."""
+    n = means2D.shape[0]
+    dev = means2D.device
+    stream = stream_of(dev)
+    conic = torch.empty(n, 4, dtype=_F32, device=dev)
+    color_opacity = torch.empty(n, 4, dtype=_F32, device=dev)
+    prep = torch.empty(lib.hds_rasterize_prepare_scratch_bytes(n), dtype=torch.uint8, device=dev)
+    total = ctypes.c_int64(0)
+    check(lib.hds_rasterize_prepare(n, ptr(means2D), ptr(depths), ptr(radii), ptr(conics), ptr(colors), ptr(opacities),
+                                    width, height, ptr(conic), ptr(color_opacity), ptr(prep), prep.numel(),
+                                    ctypes.byref(total), stream))
+    dups = total.value
+    tiles = _tiles(width, height)
+    if dups == 0:
+        return conic, color_opacity, torch.empty(0, dtype=_I32, device=dev), \
+            torch.zeros(tiles, 2, dtype=_I32, device=dev), (torch.empty(0, dtype=torch.int64, device=dev) if keep_keys else None)
+    values = torch.empty(dups, dtype=_I32, device=dev)
+    ranges = torch.empty(tiles, 2, dtype=_I32, device=dev)
+    keys = torch.empty(dups, dtype=torch.int64, device=dev) if keep_keys else None
+    scratch = torch.empty(lib.hds_rasterize_sort_scratch_bytes(n, dups, width, height), dtype=torch.uint8, device=dev)
+    check(lib.hds_rasterize_sort(n, dups, width, height, ptr(prep), ptr(scratch), scratch.numel(), ptr(values),
+                                 ptr(ranges), ptr(keys), stream))
+    return conic, color_opacity, values, ranges, keys
+
+
+def rasterize(means2D, depths, radii, conics, colors, opacities, background, image_width: int, image_height: int):
+    """forward.cu:239-435.  Returns (image [H,W,3] view of [H,W,4], final_T [H,W], n_contrib [H,W],
+    values_sorted [Dups], tile_ranges [T,2], conic [N,4], color_opacity [N,4])."""
+    for t, name in ((means2D, "means2D"), (depths, "depths"), (radii, "radii"), (conics, "conics"),
+                    (colors, "colors"), (opacities, "opacities"), (background, "background")):
+        _check(t, name)
+    width, height = int(image_width), int(image_height)
+    dev = means2D.device
+    conic, color_opacity, values, ranges, _ = _bin(means2D, depths, radii, conics, colors, opacities, width, height)
+    if values.numel() == 0:
+        return (background.reshape(1, 1, 3).expand(height, width, 3).contiguous(),
+                torch.ones(height, width, dtype=_F32, device=dev), torch.zeros(height, width, dtype=_I32, device=dev),
+                values, ranges, conic, color_opacity)
+    out = torch.empty(height, width, 4, dtype=_F32, device=dev)
+    final_T = torch.empty(height, width, dtype=_F32, device=dev)
+    n_contrib = torch.empty(height, width, dtype=_I32, device=dev)
+    check(lib.hds_render_forward(width, height, ptr(ranges), ptr(values), ptr(means2D), ptr(conic), ptr(color_opacity),
+                                 ptr(background), ptr(out), ptr(final_T), ptr(n_contrib), stream_of(dev)))
+    return out[..., :3], final_T, n_contrib, values, ranges, conic, color_opacity
+
+
+def rasterize_with_features(means2D, depths, radii, conics, colors, opacities, background, features,
+                            image_width: int, image_height: int):
+    """rasterize + rasterize_features in one walk of the sorted lists (the RGB image is a by-product of
+    the feature pass).  Returns (image, feature_image, final_T, n_contrib, values_sorted, tile_ranges,
+    conic, color_opacity); final_T / n_contrib serve both images' backward passes."""
+    for t, name in ((means2D, "means2D"), (depths, "depths"), (radii, "radii"), (conics, "conics"),
+                    (colors, "colors"), (opacities, "opacities"), (background, "background")):
+        _check(t, name)
+    if not (features.is_cuda and features.is_contiguous() and features.dtype == _F32):
+        raise RuntimeError("features must be a contiguous float32 CUDA tensor")
+    width, height = int(image_width), int(image_height)
+    dev = means2D.device
+    n, d = features.shape
+    conic, color_opacity, values, ranges, _ = _bin(means2D, depths, radii, conics, colors, opacities, width, height)
+    out = torch.empty(height, width, 4, dtype=_F32, device=dev)
+    feature_image = torch.empty(height, width, d, dtype=_F32, device=dev)
+    final_T = torch.empty(height, width, dtype=_F32, device=dev)
+    n_contrib = torch.empty(height, width, dtype=_I32, device=dev)
+    check(lib.hds_render_features_forward(n, d, width, height, ptr(ranges), ptr(values), ptr(means2D), ptr(conic),
+                                          ptr(color_opacity), ptr(features), ptr(background), ptr(feature_image),
+                                          ptr(final_T), ptr(n_contrib), ptr(out), stream_of(dev)))
+    return out[..., :3], feature_image, final_T, n_contrib, values, ranges, conic, color_opacity
+
+
+def rasterize_backward(grad_image, means2D, conic, color_opacity, values_sorted, tile_ranges, final_transmittance,
+                       n_contrib, background, image_width: int, image_height: int):
+    """backward.cu:166-226.  Returns (dL/dmeans2D [N,2], dL/dconics [N,3], dL/dcolors [N,3], dL/dopacities [N,1])."""
+    for t, name in ((grad_image, "grad_image"), (means2D, "means2D"), (conic, "conic"),
+                    (color_opacity, "color_opacity"), (values_sorted, "values_sorted"), (tile_ranges, "tile_ranges"),
+                    (final_transmittance, "final_transmittance"), (n_contrib, "n_contrib"), (background, "background")):
+        _check(t, name)
+    n = means2D.shape[0]
+    dev = means2D.device
+    gm = torch.empty(n, 2, dtype=_F32, device=dev)
+    gc = torch.empty(n, 3, dtype=_F32, device=dev)
+    gcol = torch.empty(n, 3, dtype=_F32, device=dev)
+    go = torch.empty(n, 1, dtype=_F32, device=dev)
+    check(lib.hds_render_backward(n, int(image_width), int(image_height), ptr(grad_image), ptr(means2D), ptr(conic),
+                                  ptr(color_opacity), ptr(values_sorted), ptr(tile_ranges), ptr(final_transmittance),
+                                  ptr(n_contrib), ptr(background), ptr(gm), ptr(gc), ptr(gcol), ptr(go),
+                                  stream_of(dev)))
+    return gm, gc, gcol, go
+
+
+def rasterize_features(features, means2D, conic, color_opacity, values_sorted, tile_ranges, image_width: int,
+                       image_height: int):
+    """features.cu:299-346.  Returns (feature_image [H,W,D], final_T [H,W], n_contrib [H,W])."""
+    if not (features.is_cuda and features.is_contiguous() and features.dtype == _F32):
+        raise RuntimeError("features must be a contiguous float32 CUDA tensor")
+    width, height = int(image_width), int(image_height)
+    dev = features.device
+    n, d = features.shape
+    out = torch.empty(height, width, d, dtype=_F32, device=dev)
+    final_T = torch.empty(height, width, dtype=_F32, device=dev)
+    n_contrib = torch.empty(height, width, dtype=_I32, device=dev)
+    check(lib.hds_render_features_forward(n, d, width, height, ptr(tile_ranges), ptr(values_sorted), ptr(means2D),
+                                          ptr(conic), ptr(color_opacity), ptr(features), None, ptr(out), ptr(final_T),
+                                          ptr(n_contrib), None, stream_of(dev)))
+    return out, final_T, n_contrib
+
+
+def rasterize_features_backward(grad_output, features, means2D, conic, color_opacity, values_sorted, tile_ranges,
+                                final_transmittance, n_contrib, image_width: int, image_height: int, slice_width: int):
+    """features.cu:561-616.  Returns (dL/dfeatures [N,D], dL/dmeans2D [N,2], dL/dconics [N,3], dL/dopacities [N,1])."""
+    if not (grad_output.is_cuda and grad_output.is_contiguous()):
+        raise RuntimeError("grad_output must be a contiguous CUDA tensor")
+    n, d = features.shape
+    dev = features.device
+    gf = torch.empty(n, d, dtype=_F32, device=dev)
+    gm = torch.empty(n, 2, dtype=_F32, device=dev)
+    gc = torch.empty(n, 3, dtype=_F32, device=dev)
+    go = torch.empty(n, 1, dtype=_F32, device=dev)
+    check(lib.hds_render_features_backward(n, d, int(slice_width), int(image_width), int(image_height), ptr(grad_output),
+                                           ptr(features), ptr(means2D), ptr(conic), ptr(color_opacity),
+                                           ptr(values_sorted), ptr(tile_ranges), ptr(final_transmittance),
+                                           ptr(n_contrib), ptr(gf), ptr(gm), ptr(gc), ptr(go), stream_of(dev)))
+    return gf, gm, gc, go
+
+
+def eval_sh(sh_dc, sh_rest, dirs, degree: int, radii):
+    """sh.cu:157-168.  Returns rgb [N,3]."""
+    n = sh_dc.shape[0]
+    rgb = torch.empty(n, 3, dtype=_F32, device=sh_dc.device)
+    check(lib.hds_eval_sh_forward(n, int(degree), ptr(sh_dc), ptr(sh_rest), ptr(dirs), ptr(radii), ptr(rgb),
+                                  stream_of(sh_dc.device)))
+    return rgb
+
+
+def eval_sh_backward_adam(grad_rgb, sh_dc, sh_rest, dirs, degree: int, radii, m_dc, v_dc, m_rest, v_rest, step_dc,
+                          step_rest, lr_dc: float, lr_rest: float, beta1: float, beta2: float, eps: float):
+    """sh.cu:171-190: steps sh_dc / sh_rest and their Adam moments in place, returns dL/ddirs [N,3]."""
+    n = sh_dc.shape[0]
+    grad_dirs = torch.empty_like(dirs)
+    check(lib.hds_eval_sh_backward_adam(n, int(degree), ptr(grad_rgb), ptr(sh_dc), ptr(sh_rest), ptr(dirs), ptr(radii),
+                                        ptr(m_dc), ptr(v_dc), ptr(m_rest), ptr(v_rest), ptr(step_dc), ptr(step_rest),
+                                        float(lr_dc), float(lr_rest), float(beta1), float(beta2), float(1.0 - beta1),
+                                        float(1.0 - beta2), float(eps), ptr(grad_dirs), stream_of(sh_dc.device)))
+    return grad_dirs
+
+
+def eval_sh_backward(grad_rgb, sh_dc, sh_rest, dirs, degree: int, radii):
+    """Plain SH backward: returns (dL/dsh_dc [N,1,3], dL/dsh_rest [N,15,3], dL/ddirs [N,3])."""
+    n = sh_dc.shape[0]
+    gdc = torch.empty_like(sh_dc)
+    grest = torch.empty_like(sh_rest)
+    gd = torch.empty_like(dirs)
+    check(lib.hds_eval_sh_backward(n, int(degree), ptr(grad_rgb), ptr(sh_dc), ptr(sh_rest), ptr(dirs), ptr(radii),
+                                   ptr(gdc), ptr(grest), ptr(gd), stream_of(sh_dc.device)))
+    return gdc, grest, gd
+
+
+def project_gaussians(means, scales, quats, opacities, world_to_camera, fx: float, fy: float, cx: float, cy: float,
+                      width: int, height: int, near_plane: float, low_pass: float, fov_scale: float):
+    """projection.cu:210-231.  Returns (means2D [N,2], depths [N], radii [N], conics [N,3])."""
+    n = means.shape[0]
+    dev = means.device
+    pose = world_to_camera.contiguous()
+    opac = opacities.contiguous()
+    means2D = torch.empty(n, 2, dtype=_F32, device=dev)
+    depths = torch.empty(n, dtype=_F32, device=dev)
+    radii = torch.empty(n, dtype=_F32, device=dev)
+    conics = torch.empty(n, 3, dtype=_F32, device=dev)
+    check(lib.hds_project_forward(n, ptr(means), ptr(scales), ptr(quats), ptr(opac), ptr(pose), float(fx), float(fy),
+                                  float(cx), float(cy), int(width), int(height), float(near_plane), float(low_pass),
+                                  float(fov_scale), ptr(means2D), ptr(depths), ptr(radii), ptr(conics), stream_of(dev)))
+    return means2D, depths, radii, conics
+
+
+def project_gaussians_backward(grad_means2D, grad_conics, means, scales, quats, world_to_camera, fx: float, fy: float,
+                               cx: float, cy: float, width: int, height: int, near_plane: float, low_pass: float,
+                               fov_scale: float):
+    """projection.cu:234-253.  Returns (dL/dmeans [N,3], dL/dscales [N,3], dL/dquats [N,4])."""
+    n = means.shape[0]
+    dev = means.device
+    pose = world_to_camera.contiguous()
+    gm = torch.empty_like(means)
+    gs = torch.empty_like(scales)
+    gq = torch.empty_like(quats)
+    check(lib.hds_project_backward(n, ptr(grad_means2D), ptr(grad_conics), ptr(means), ptr(scales), ptr(quats), ptr(pose),
+                                   float(fx), float(fy), float(cx), float(cy), int(width), int(height),
+                                   float(near_plane), float(low_pass), float(fov_scale), ptr(gm), ptr(gs), ptr(gq),
+                                   stream_of(dev)))
+    return gm, gs, gq
+
+
+def ssim_forward(rendered, gt):
+    """ssim.cu:306-338.  Returns (ssim_map, d_mu, d_aa, d_ab), each [H,W,3]."""
+    if not (rendered.is_cuda and gt.is_cuda):
+        raise RuntimeError("ssim inputs must be CUDA tensors")
+    if not (rendered.is_contiguous() and gt.is_contiguous()):
+        raise RuntimeError("ssim inputs must be contiguous")
+    if not (rendered.dim() == 3 and rendered.shape[2] == 3 and rendered.shape == gt.shape):
+        raise RuntimeError("ssim inputs must both be [H, W, 3]")
+    h, w = rendered.shape[:2]
+    outs = [torch.empty_like(rendered) for _ in range(4)]
+    check(lib.hds_ssim_forward(h, w, ptr(rendered), ptr(gt), *map(ptr, outs), stream_of(rendered.device)))
+    return tuple(outs)
+
+
+def ssim_backward(grad_mean, rendered, gt, d_mu, d_aa, d_ab):
+    """ssim.cu:340-367.  Returns dL/drendered [H,W,3]."""
+    h, w = rendered.shape[:2]
+    grad = torch.empty_like(rendered)
+    check(lib.hds_ssim_backward(h, w, ptr(grad_mean), ptr(rendered), ptr(gt), ptr(d_mu), ptr(d_aa), ptr(d_ab), ptr(grad),
+                                stream_of(rendered.device)))
+    return grad
+
+
+def bin_gaussians(means2D, depths, radii, conics, opacities, image_width: int, image_height: int):
+    """The binning stage alone, with the sorted keys (for bit-exact checks against the oracle).
+    Returns (keys_sorted int64 [Dups], values_sorted [Dups], tile_ranges [T,2])."""
+    colors = torch.zeros(means2D.shape[0], 3, dtype=_F32, device=means2D.device)
+    _, _, values, ranges, keys = _bin(means2D, depths, radii, conics, colors, opacities, int(image_width),
+                                      int(image_height), keep_keys=True)
+    return keys, values, ranges

@@ -1,0 +1,96 @@
+"""Autograd layer over the blend: mirrors gaussian_splatting/rasterizer/__init__.py of the reference.
+
+``_get_rasterizer()`` returns this package's ``gaussian_rasterizer`` module (the reference returns
+its JIT-built extension), so a training loop written against the reference runs unchanged.
+"""
+from __future__ import annotations
+
+from types import ModuleType
+
+import torch
+
+from . import gaussian_rasterizer as _ext
+
+# Channels each feature backward block owns; None takes the widest slice, at most 128
+# (the reference's __init__.py:11-12, 158).
+FEATURE_SLICE_WIDTH: int | None = None
+
+
+def _get_rasterizer() -> ModuleType:
+    """The extension module with the reference's ten entry points (see gaussian_rasterizer.py)."""
+    return _ext
+
+
+class RasterizeGaussians(torch.autograd.Function):
+    """Autograd node for tile binning and the alpha blend (the reference's __init__.py:57-165).
+
+    With features, one walk of the sorted lists renders both images (the reference renders them in
+    two passes); their shared transmittance and contributor counts feed both backward passes."""
+
+    @staticmethod
+    def forward(ctx, means2D, depths, radii, conics, colors, opacities, background, features, image_width,
+                image_height):
+        ext = _get_rasterizer()
+        width, height = int(image_width), int(image_height)
+        ctx.image_size = (width, height)
+        args = (means2D.contiguous(), depths.contiguous(), radii.contiguous(), conics.contiguous(),
+                colors.contiguous(), opacities.contiguous(), background.contiguous())
+        if features is None:
+            image, final_T, n_contrib, values, ranges, conic, color_opacity = ext.rasterize(*args, width, height)
+            ctx.save_for_backward(means2D, conic, color_opacity, values, ranges, final_T, n_contrib, background, None,
+                                  None, None)
+            return image
+        features = features.contiguous()
+        image, feature_image, final_T, n_contrib, values, ranges, conic, color_opacity = ext.rasterize_with_features(
+            *args, features, width, height)
+        ctx.save_for_backward(means2D, conic, color_opacity, values, ranges, final_T, n_contrib, background, features,
+                              final_T, n_contrib)
+        return image, feature_image
+
+    @staticmethod
+    def backward(ctx, grad_image, grad_features=None):
+        (means2D, conic, color_opacity, values, ranges, final_T, n_contrib, background, features, feature_T,
+         feature_contrib) = ctx.saved_tensors
+        width, height = ctx.image_size
+        ext = _get_rasterizer()
+        means2D = means2D.contiguous()
+        if grad_image is None:
+            grad_image = torch.zeros(height, width, 3, device=means2D.device)
+        with torch.cuda.nvtx.range("rasterize_backward"):
+            grad_means2D, grad_conics, grad_colors, grad_opacities = ext.rasterize_backward(
+                grad_image.contiguous(), means2D, conic, color_opacity, values, ranges, final_T, n_contrib,
+                background, width, height)
+        grad_feats = None
+        # Frozen features still shape the geometry gradients (the reference's __init__.py:150-153).
+        if features is not None and grad_features is not None and any(ctx.needs_input_grad[i] for i in (0, 3, 5, 7)):
+            with torch.cuda.nvtx.range("rasterize_features_backward"):
+                grad_feats, f_means2D, f_conics, f_opacities = ext.rasterize_features_backward(
+                    grad_features.contiguous(), features, means2D, conic, color_opacity, values, ranges, feature_T,
+                    feature_contrib, width, height, FEATURE_SLICE_WIDTH or min(features.shape[1], 128))
+            grad_means2D += f_means2D
+            grad_conics += f_conics
+            grad_opacities += f_opacities
+            if not ctx.needs_input_grad[7]:
+                grad_feats = None
+        return grad_means2D, None, None, grad_conics, grad_colors, grad_opacities, None, grad_feats, None, None
+
+
+def rasterize(means2D: torch.Tensor, depths: torch.Tensor, radii: torch.Tensor, conics: torch.Tensor,
+              colors: torch.Tensor, opacities: torch.Tensor, image_width: int, image_height: int,
+              background: torch.Tensor | None = None, features: torch.Tensor | None = None):
+    """Alpha-blends projected gaussians into an image, front to back, on 16x16 tiles
+    (the reference's __init__.py:168-211).
+
+    Returns the [H, W, 3] image, or (image, [H, W, D] feature image) when features ([N, D], D one of
+    32, 64, 128, 256 or 512) are given."""
+    n = means2D.shape[0]
+    assert means2D.shape == (n, 2)
+    assert depths.shape == (n,) and radii.shape == (n,)
+    assert conics.shape == (n, 3) and colors.shape == (n, 3)
+    assert opacities.shape == (n, 1)
+    if background is None:
+        background = torch.zeros(3, device=means2D.device, dtype=means2D.dtype)
+    assert background.shape == (3,)
+    assert features is None or (features.ndim == 2 and features.shape[0] == n)
+    return RasterizeGaussians.apply(means2D, depths, radii, conics, colors, opacities, background, features,
+                                    image_width, image_height)

@@ -1,0 +1,177 @@
+/*
+ * hds_b200.h -- C ABI of the B200 (sm_100a) high-dimensional gaussian splatting rasterizer.
+ *
+ * The library (libhds_b200.so) implements the hot path of alexkato29/high-dimensional-splatting:
+ * EWA projection, SH colour, tile binning with a device radix sort, the RGB and C-channel
+ * feature blends (feature contraction on tcgen05 TF32 tensor cores), their backward passes, and
+ * fused SSIM.  Each entry point below replaces one entry point of the reference's torch extension
+ * (gaussian_splatting/rasterizer/api.h, bound in bindings.cpp:4-43); the comment on each names the
+ * reference function and its file:line.
+ *
+ * Conventions
+ *  - Every pointer is a CUDA device pointer to contiguous row-major fp32 (or int32 / uint64 where
+ *    typed) memory on the current device, laid out exactly as the reference's tensors.
+ *  - Nothing here allocates device memory.  Where a step needs scratch, a *_scratch_bytes()
+ *    query gives the size and the caller passes the buffer (256-byte aligned).
+ *  - All work is queued on `stream` (a cudaStream_t; NULL is the legacy default stream) and is
+ *    asynchronous, except hds_rasterize_prepare, which synchronises `stream` to read the number
+ *    of (tile, gaussian) pairs -- the same host read as the reference (forward.cu:318-325).
+ *  - Return value: HDS_OK (0) or an HDS_ERR_* code; hds_last_error() then describes the failure
+ *    (thread-local; message texts match the reference's TORCH_CHECK wording where it has one).
+ *  - Outputs are fully overwritten; gradient outputs are zero-filled by the call itself.
+ */
+#ifndef HDS_B200_H
+#define HDS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* hds_stream_t; /* cudaStream_t */
+
+enum {
+    HDS_OK = 0,
+    HDS_ERR_INVALID = 1,     /* bad size, null pointer or misaligned buffer */
+    HDS_ERR_UNSUPPORTED = 2, /* channel count / slice width outside the supported set */
+    HDS_ERR_CUDA = 3,        /* a CUDA runtime call or kernel launch failed */
+    HDS_ERR_SCRATCH = 4,     /* scratch buffer smaller than the *_scratch_bytes() query */
+    HDS_ERR_TOO_LARGE = 5,   /* sizes beyond the int32 indexing of the reference's layouts */
+    HDS_ERR_DEVICE = 6       /* a kernel recorded a device-side failure (bounded wait ran out) */
+};
+
+/* Thread-local description of the last failure on this thread ("" after success). */
+const char* hds_last_error(void);
+
+/* ABI version of this header (bumped on any signature change). */
+int hds_abi_version(void);
+#define HDS_ABI_VERSION 1
+
+/* ---------------------------------------------------------------------------------------------
+ * Projection.  Replaces project_gaussians (projection.cu:210-231; autograd glue projection.py:25-96).
+ * means/scales [n,3], quats [n,4] (w,x,y,z), opacities [n] (the [n,1] tensor), world_to_camera
+ * [4,4] row-major on the device.  Outputs means2D [n,2], depths [n], radii [n] (0 = culled),
+ * conics [n,3] (inverse 2-D covariance xx, xy, yy).
+ * ------------------------------------------------------------------------------------------- */
+int hds_project_forward(int n, const float* means, const float* scales, const float* quats, const float* opacities,
+                        const float* world_to_camera, float fx, float fy, float cx, float cy, int width, int height,
+                        float near_plane, float low_pass, float fov_scale, float* means2D, float* depths,
+                        float* radii, float* conics, hds_stream_t stream);
+
+/* Replaces project_gaussians_backward (projection.cu:234-253). */
+int hds_project_backward(int n, const float* grad_means2D, const float* grad_conics, const float* means,
+                         const float* scales, const float* quats, const float* world_to_camera, float fx, float fy,
+                         float cx, float cy, int width, int height, float near_plane, float low_pass,
+                         float fov_scale, float* grad_means, float* grad_scales, float* grad_quats,
+                         hds_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Spherical harmonics.  Replaces eval_sh (sh.cu:157-168; glue utils/sh.py:26-59).
+ * sh_dc [n,1,3], sh_rest [n,15,3], dirs [n,3] unit vectors, radii [n]; rgb [n,3].
+ * ------------------------------------------------------------------------------------------- */
+int hds_eval_sh_forward(int n, int degree, const float* sh_dc, const float* sh_rest, const float* dirs,
+                        const float* radii, float* rgb, hds_stream_t stream);
+
+/* Replaces eval_sh_backward_adam (sh.cu:171-190; glue utils/sh.py:62-109): SH gradient kept on chip
+ * and consumed by an in-place Adam step of sh_dc/sh_rest and their moments; returns dL/ddirs.
+ * step_dc/step_rest are device scalars already incremented for this step (torch state["step"]).
+ * one_minus_beta1/2 are 1 - beta formed in double by the caller, as torch does. */
+int hds_eval_sh_backward_adam(int n, int degree, const float* grad_rgb, float* sh_dc, float* sh_rest,
+                              const float* dirs, const float* radii, float* m_dc, float* v_dc, float* m_rest,
+                              float* v_rest, const float* step_dc, const float* step_rest, float lr_dc, float lr_rest,
+                              float beta1, float beta2, float one_minus_beta1, float one_minus_beta2, float eps,
+                              float* grad_dirs, hds_stream_t stream);
+
+/* Plain SH backward returning dL/dsh_dc [n,1,3], dL/dsh_rest [n,15,3] and dL/ddirs [n,3].  No
+ * counterpart in the reference (which only has the fused-Adam form); data-parallel training needs
+ * SH gradients it can all-reduce before any optimizer step. */
+int hds_eval_sh_backward(int n, int degree, const float* grad_rgb, const float* sh_dc, const float* sh_rest,
+                         const float* dirs, const float* radii, float* grad_sh_dc, float* grad_sh_rest,
+                         float* grad_dirs, hds_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Binning + RGB blend.  Together these three calls replace rasterize (forward.cu:239-435).
+ *
+ * 1. hds_rasterize_prepare (forward.cu:284-326): culls, packs conic4 [n,4] = (a, b, c, 0) and
+ *    color_opacity [n,4] = (r, g, b, opacity), counts the tiles each gaussian touches, prefix-sums
+ *    the counts and writes the total number of (tile, gaussian) pairs to *num_duplicates (host).
+ *    It synchronises `stream`.  scratch: hds_rasterize_prepare_scratch_bytes(n) bytes, which must
+ *    stay untouched until hds_rasterize_sort has been queued.
+ * 2. hds_rasterize_sort (forward.cu:340-404): emits keys tile << 32 | depth bits, radix-sorts them
+ *    stably on 32 + ceil(log2 tiles) bits, and writes values_sorted [num_duplicates] (gaussian ids)
+ *    and tile_ranges [tiles,2] ([start, end), empty tiles 0, 0).  keys_sorted may be NULL; when
+ *    given it receives the sorted keys (bit-exactness checks).
+ * 3. hds_render_forward (forward.cu:406-434): front-to-back FP32 blend.  image4 [H,W,4] (the
+ *    reference's padded layout; channel 3 written 0), final_T [H,W], n_contrib [H,W] (1-based
+ *    index of the last blended list entry).
+ * ------------------------------------------------------------------------------------------- */
+size_t hds_rasterize_prepare_scratch_bytes(int n);
+int hds_rasterize_prepare(int n, const float* means2D, const float* depths, const float* radii, const float* conics,
+                          const float* colors, const float* opacities, int width, int height, float* conic4,
+                          float* color_opacity, void* scratch, size_t scratch_bytes, int64_t* num_duplicates,
+                          hds_stream_t stream);
+
+size_t hds_rasterize_sort_scratch_bytes(int n, int64_t num_duplicates, int width, int height);
+int hds_rasterize_sort(int n, int64_t num_duplicates, int width, int height, const void* prepare_scratch,
+                       void* scratch, size_t scratch_bytes, int32_t* values_sorted, int32_t* tile_ranges,
+                       uint64_t* keys_sorted, hds_stream_t stream);
+
+int hds_render_forward(int width, int height, const int32_t* tile_ranges, const int32_t* values_sorted,
+                       const float* means2D, const float* conic4, const float* color_opacity,
+                       const float* background, float* image4, float* final_T, int32_t* n_contrib,
+                       hds_stream_t stream);
+
+/* Replaces rasterize_backward (backward.cu:166-226).  grad_image [H,W,3]; outputs dL/dmeans2D [n,2],
+ * dL/dconics [n,3], dL/dcolors [n,3], dL/dopacities [n]. */
+int hds_render_backward(int n, int width, int height, const float* grad_image, const float* means2D,
+                        const float* conic4, const float* color_opacity, const int32_t* values_sorted,
+                        const int32_t* tile_ranges, const float* final_T, const int32_t* n_contrib,
+                        const float* background, float* grad_means2D, float* grad_conics, float* grad_colors,
+                        float* grad_opacities, hds_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Feature blend.  Replaces rasterize_features (features.cu:299-346): features [n,C] with
+ * C in {32, 64, 128, 256, 512} blended over a zero background into feature_image [H,W,C], plus its
+ * own final_T and n_contrib.  The contraction runs on tcgen05 TF32 tensor cores (weights and
+ * features rounded to nearest TF32).  When image4 is non-NULL the same walk also writes the RGB
+ * image (colours from color_opacity, over `background`), which the reference computes in a second
+ * pass; that is an addition, NULL reproduces the reference call.
+ * ------------------------------------------------------------------------------------------- */
+int hds_render_features_forward(int n, int channels, int width, int height, const int32_t* tile_ranges,
+                                const int32_t* values_sorted, const float* means2D, const float* conic4,
+                                const float* color_opacity, const float* features, const float* background,
+                                float* feature_image, float* final_T, int32_t* n_contrib, float* image4,
+                                hds_stream_t stream);
+
+/* Replaces rasterize_features_backward (features.cu:561-616).  slice_width is the channel slice one
+ * block owns, one of the reference's pairs (features.cu:601-612); any other pair is rejected.
+ * Outputs dL/dfeatures [n,C], dL/dmeans2D [n,2], dL/dconics [n,3], dL/dopacities [n]. */
+int hds_render_features_backward(int n, int channels, int slice_width, int width, int height,
+                                 const float* grad_output, const float* features, const float* means2D,
+                                 const float* conic4, const float* color_opacity, const int32_t* values_sorted,
+                                 const int32_t* tile_ranges, const float* final_T, const int32_t* n_contrib,
+                                 float* grad_features, float* grad_means2D, float* grad_conics,
+                                 float* grad_opacities, hds_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * SSIM (11x11 gaussian window, sigma 1.5).  Replace ssim_forward (ssim.cu:306-338) and
+ * ssim_backward (ssim.cu:340-367); glue utils/loss.py:57-90.  Images [H,W,3]; grad_mean is a
+ * device scalar (dL/d mean SSIM).
+ * ------------------------------------------------------------------------------------------- */
+int hds_ssim_forward(int height, int width, const float* rendered, const float* gt, float* ssim_map, float* d_mu,
+                     float* d_aa, float* d_ab, hds_stream_t stream);
+int hds_ssim_backward(int height, int width, const float* grad_mean, const float* rendered, const float* gt,
+                      const float* d_mu, const float* d_aa, const float* d_ab, float* grad_rendered,
+                      hds_stream_t stream);
+
+/* Reads and clears the device-side failure word that kernels with bounded waits set (0 = none).
+ * Synchronises `stream`. */
+int hds_device_status(int* status, hds_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HDS_B200_H */

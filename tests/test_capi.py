@@ -1,0 +1,61 @@
+"""CPU checks of the C ABI: the library loads, exports every function include/*.h declares, and the
+host-side argument checks reject bad calls before any device work (no GPU needed)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+REPO = Path(__file__).resolve().parent.parent
+
+
+def declared_functions():
+    names = []
+    for header in (REPO / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.S)
+        names += re.findall(r"^\s*(?:const\s+)?[A-Za-z_][A-Za-z0-9_]*\s*\*?\s*(hds_[a-z0-9_]+)\s*\(", text, flags=re.M)
+    return sorted(set(names))
+
+
+def test_header_declares_the_entry_points():
+    names = declared_functions()
+    for required in ("hds_project_forward", "hds_project_backward", "hds_eval_sh_forward", "hds_eval_sh_backward_adam",
+                     "hds_rasterize_prepare", "hds_rasterize_sort", "hds_render_forward", "hds_render_backward",
+                     "hds_render_features_forward", "hds_render_features_backward", "hds_ssim_forward",
+                     "hds_ssim_backward"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol():
+    from hds_b200 import native
+
+    for name in declared_functions():
+        assert hasattr(native.lib, name), f"{name} declared in include/ but not exported"
+        assert name in native.SIGNATURES, f"{name} has no ctypes signature in native.py"
+
+
+def test_abi_version_and_scratch_queries():
+    from hds_b200 import native
+
+    assert native.lib.hds_abi_version() == native.ABI_VERSION
+    small = native.lib.hds_rasterize_prepare_scratch_bytes(10)
+    big = native.lib.hds_rasterize_prepare_scratch_bytes(1_000_000)
+    assert 0 < small < big and big % 256 == 0
+    assert native.lib.hds_rasterize_sort_scratch_bytes(10, 2_000_000, 979, 546) > 2_000_000 * 20
+
+
+def test_bad_arguments_are_rejected_on_the_host():
+    from hds_b200 import native
+
+    rc = native.lib.hds_render_features_forward(10, 24, 16, 16, None, None, None, None, None, None, None, None, None,
+                                                None, None, None)
+    assert rc == 2 and b"32, 64, 128, 256 or 512" in native.lib.hds_last_error()
+    rc = native.lib.hds_render_features_backward(10, 256, 32, 16, 16, *([None] * 14))
+    assert rc == 2 and b"no feature backward for 256 channels in slices of 32" in native.lib.hds_last_error()
+    rc = native.lib.hds_eval_sh_forward(10, 4, None, None, None, None, None, None)
+    assert rc == 1 and b"degree" in native.lib.hds_last_error()
+    out = ctypes.c_int64(0)
+    rc = native.lib.hds_rasterize_prepare(10, *([None] * 6), 16, 16, None, None, None, 0, ctypes.byref(out), None)
+    assert rc == 4 and b"scratch" in native.lib.hds_last_error()
+    with pytest.raises(RuntimeError, match="scratch"):
+        native.check(rc)

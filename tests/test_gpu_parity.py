@@ -1,0 +1,258 @@
+"""Stage-by-stage parity of the CUDA path (called through the C ABI) with the CPU oracle.
+
+Bit-exact (np.array_equal): projection, SH colour and SH gradients, tile keys, sort order, tile
+ranges, the RGB image, final transmittance, contributor counts, and SSIM (map, partials, gradient).
+The forward kernels are compiled with --fmad=false and use the oracle's exact operation order.
+
+Within tolerance:
+  * feature images: TF32 tensor cores.  Against the oracle with the same TF32 rounding of weights
+    and features (exact products, double sums) within 1e-5 * max(1, max|f|); against the exact
+    FP32 oracle within the north star's 1e-3 * max(1, max|f|).
+  * gradients: accumulated with float atomics in any order; within 1e-4 of the largest gradient
+    (helpers.assert_grads_close) against the oracle's double sums.
+"""
+import numpy as np
+import pytest
+
+import oracle
+from helpers import FEATURE_ATOL, assert_close_abs, assert_grads_close
+from scenes_np import GOLDEN_FLAT_CASES, SIZE_EXAMPLES, config_scene, golden_case, reference_scene
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+CASES = ["raster_ref_scene", "raster_config0", *GOLDEN_FLAT_CASES, *[f"size{i}" for i in range(len(SIZE_EXAMPLES))],
+         "config1_20k"]
+BACKGROUND = np.array([0.3, 0.5, 0.7], np.float32)
+_cache = {}
+
+
+@pytest.fixture(scope="module")
+def ext():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    from hds_b200 import gaussian_rasterizer
+
+    return gaussian_rasterizer
+
+
+def cuda(*arrays):
+    return [torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in arrays]
+
+
+def host(t):
+    return t.detach().cpu().numpy()
+
+
+def case(name, golden):
+    if name in _cache:
+        return _cache[name]
+    if name.startswith("size"):
+        seed, n, w, h = SIZE_EXAMPLES[int(name[4:])]
+        out = (reference_scene(seed, n, w, h), w, h)
+    elif name == "config1_20k":
+        from hds_b200 import scenes
+
+        inputs, cam = config_scene(scenes.config1(0, n=20_000, channels=0))
+        out = (inputs, cam.width, cam.height)
+    else:
+        inputs, w, h, _ = golden_case(golden, name)
+        out = (inputs, w, h)
+    _cache[name] = out
+    return out
+
+
+def features_for(n, channels, seed=0):
+    return np.random.default_rng(1000 + channels + seed).random((n, channels), dtype=np.float32)
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_binning_bit_exact(ext, golden, name):
+    (m2, dep, rad, con, col, opac), w, h = case(name, golden)
+    _, keys, values, ranges = oracle.bin_gaussians(m2, dep, rad, con, opac, w, h)
+    g_keys, g_values, g_ranges = ext.bin_gaussians(*cuda(m2, dep, rad, con, opac), w, h)
+    assert np.array_equal(host(g_keys).view(np.uint64), keys), "tile keys differ"
+    assert np.array_equal(host(g_values), values), "sort order differs"
+    assert np.array_equal(host(g_ranges), ranges), "tile ranges differ"
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_rgb_forward_bit_exact(ext, golden, name):
+    inputs, w, h = case(name, golden)
+    m2, dep, rad, con, col, opac = inputs
+    want = oracle.rasterize(*inputs, w, h, background=BACKGROUND)
+    image, final_T, n_contrib, values, ranges, conic, co = ext.rasterize(*cuda(*inputs, BACKGROUND), w, h)
+    assert np.array_equal(host(image), want["image"]), "image differs"
+    assert np.array_equal(host(final_T), want["final_T"]), "final_T differs"
+    assert np.array_equal(host(n_contrib), want["n_contrib"]), "n_contrib differs"
+
+
+@pytest.mark.parametrize("channels", [32, 64, 128, 256, 512])
+@pytest.mark.parametrize("name", ["raster_ref_scene", "raster_config0", "dense_tile", "t_floor", "size3", "size4",
+                                  "config1_20k"])
+def test_feature_forward(ext, golden, name, channels):
+    inputs, w, h = case(name, golden)
+    m2, dep, rad, con, col, opac = inputs
+    feats = features_for(len(dep), channels)
+    want = oracle.rasterize(*inputs, w, h, background=BACKGROUND, features=feats)
+    want_tf32 = oracle.render_forward(want["ranges"], want["values"], m2, con, None, opac, w, h, features=feats,
+                                      tf32_round=True)[3]
+    t_in = cuda(*inputs, BACKGROUND)
+    f = cuda(feats)[0]
+    image, fimg, final_T, n_contrib, *_ = ext.rasterize_with_features(*t_in, f, w, h)
+    assert np.array_equal(host(image), want["image"]), "fused RGB differs"
+    assert np.array_equal(host(final_T), want["final_T"]), "final_T differs"
+    assert np.array_equal(host(n_contrib), want["n_contrib"]), "n_contrib differs"
+    scale = max(1.0, float(np.abs(feats).max())) if feats.size else 1.0
+    assert_close_abs(host(fimg), want_tf32, 1e-5 * scale, "feature image vs TF32 oracle")
+    assert_close_abs(host(fimg), want["features"], FEATURE_ATOL * scale, "feature image vs FP32 oracle")
+    # The reference's two-pass API (rasterize then rasterize_features) gives the same image.
+    _, _, _, values, ranges, conic, co = ext.rasterize(*t_in, w, h)
+    fimg2, t2, c2 = ext.rasterize_features(f, t_in[0], conic, co, values, ranges, w, h)
+    assert torch.equal(fimg2, fimg) and torch.equal(t2, final_T) and torch.equal(c2, n_contrib)
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_rgb_backward(ext, golden, name):
+    inputs, w, h = case(name, golden)
+    m2, dep, rad, con, col, opac = inputs
+    want = oracle.rasterize(*inputs, w, h, background=BACKGROUND)
+    grad_image = np.random.default_rng(5).random((h, w, 3), dtype=np.float32)
+    gm, gc, gcol, go, _ = oracle.render_backward(want["ranges"], want["values"], m2, con, col, opac, w, h,
+                                                 want["final_T"], want["n_contrib"], grad_image=grad_image,
+                                                 background=BACKGROUND)
+    t_in = cuda(*inputs, BACKGROUND)
+    _, final_T, n_contrib, values, ranges, conic, co = ext.rasterize(*t_in, w, h)
+    got = ext.rasterize_backward(cuda(grad_image)[0], t_in[0], conic, co, values, ranges, final_T, n_contrib,
+                                 t_in[6], w, h)
+    for nm, g, wv in zip(("means2D", "conics", "colors", "opacities"), got, (gm, gc, gcol, go)):
+        assert_grads_close(host(g), wv, nm)
+
+
+@pytest.mark.parametrize("channels, slice_width", [(32, 32), (64, 64), (64, 32), (128, 128), (128, 64), (128, 32),
+                                                   (256, 128), (256, 64), (512, 128), (512, 64)])
+@pytest.mark.parametrize("name", ["raster_ref_scene", "raster_config0", "dense_tile", "size3", "config1_20k"])
+def test_feature_backward(ext, golden, name, channels, slice_width):
+    inputs, w, h = case(name, golden)
+    m2, dep, rad, con, col, opac = inputs
+    feats = features_for(len(dep), channels)
+    grad_f = np.random.default_rng(9).random((h, w, channels), dtype=np.float32)
+    want = oracle.rasterize(*inputs, w, h, background=BACKGROUND)
+    gm, gc, _, go, gf = oracle.render_backward(want["ranges"], want["values"], m2, con, None, opac, w, h,
+                                               want["final_T"], want["n_contrib"], features=feats,
+                                               grad_features=grad_f)
+    t_in = cuda(*inputs, BACKGROUND)
+    _, final_T, n_contrib, values, ranges, conic, co = ext.rasterize(*t_in, w, h)
+    got = ext.rasterize_features_backward(cuda(grad_f)[0], cuda(feats)[0], t_in[0], conic, co, values, ranges,
+                                          final_T, n_contrib, w, h, slice_width)
+    for nm, g, wv in zip(("features", "means2D", "conics", "opacities"), got, (gf, gm, gc, go)):
+        assert_grads_close(host(g), wv, nm)
+
+
+def test_unsupported_widths_are_rejected(ext, golden):
+    inputs, w, h = case("raster_ref_scene", golden)
+    t_in = cuda(*inputs, BACKGROUND)
+    _, final_T, n_contrib, values, ranges, conic, co = ext.rasterize(*t_in, w, h)
+    with pytest.raises(RuntimeError, match="32, 64, 128, 256 or 512"):
+        ext.rasterize_features(torch.rand(len(inputs[1]), 24, device="cuda"), t_in[0], conic, co, values, ranges, w, h)
+    f = torch.rand(len(inputs[1]), 256, device="cuda")
+    with pytest.raises(RuntimeError, match="no feature backward for 256 channels in slices of 32"):
+        ext.rasterize_features_backward(torch.rand(h, w, 256, device="cuda"), f, t_in[0], conic, co, values, ranges,
+                                        final_T, n_contrib, w, h, 32)
+
+
+@pytest.mark.parametrize("which", ["config0", "reference", "config1"])
+def test_projection_bit_exact(ext, which):
+    from hds_b200 import scenes
+
+    if which == "config0":
+        s = scenes.config0(0, channels=0)
+        means, sc, q, op, cam = s.means, s.scales, s.quats, s.opacities, s.cameras[0]
+    elif which == "config1":
+        s = scenes.config1(1, n=50_000, channels=0)
+        means, sc, q, op, cam = s.means, s.scales, s.quats, s.opacities, s.cameras[0]
+    else:
+        g = scenes.reference_test_scene(3, 5000)
+        means, sc, q, op = g["means"], g["scales"], g["quats"], g["opacities"]
+        cam = scenes.identity_camera(160, 120)
+    args = (cam.fx, cam.fy, cam.cx, cam.cy, cam.width, cam.height)
+    want = oracle.project_forward(means.numpy(), sc.numpy(), q.numpy(), op.numpy(), cam.world_to_camera.numpy(), *args)
+    got = ext.project_gaussians(*cuda(means.numpy(), sc.numpy(), q.numpy(), op.numpy(), cam.world_to_camera.numpy()),
+                                *args, oracle.NEAR_PLANE, oracle.LOW_PASS, oracle.FOV_SCALE)
+    for nm, g, wv in zip(("means2D", "depths", "radii", "conics"), got, want):
+        assert np.array_equal(host(g), wv), f"{nm} differs"
+    rng = np.random.default_rng(4)
+    gm2 = rng.standard_normal((means.shape[0], 2)).astype(np.float32)
+    gcon = rng.standard_normal((means.shape[0], 3)).astype(np.float32)
+    want = oracle.project_backward(gm2, gcon, means.numpy(), sc.numpy(), q.numpy(), cam.world_to_camera.numpy(), *args)
+    got = ext.project_gaussians_backward(*cuda(gm2, gcon, means.numpy(), sc.numpy(), q.numpy(),
+                                               cam.world_to_camera.numpy()), *args, oracle.NEAR_PLANE, oracle.LOW_PASS,
+                                         oracle.FOV_SCALE)
+    for nm, g, wv in zip(("grad_means", "grad_scales", "grad_quats"), got, want):
+        assert np.array_equal(host(g), wv), f"{nm} differs"
+
+
+@pytest.mark.parametrize("degree", [0, 1, 2, 3])
+def test_sh_bit_exact(ext, golden, degree):
+    g = golden("sh.npz")
+    sh, dirs, radii, grad_rgb = g["sh"], g["dirs"], g["radii"], g["grad_rgb"]
+    dc, rest = np.ascontiguousarray(sh[:, :1]), np.ascontiguousarray(sh[:, 1:])
+    t_dc, t_rest, t_dirs, t_radii, t_grad = cuda(dc, rest, dirs, radii, grad_rgb)
+    assert np.array_equal(host(ext.eval_sh(t_dc, t_rest, t_dirs, degree, t_radii)),
+                          oracle.eval_sh(dc, rest, dirs, degree, radii))
+    got = ext.eval_sh_backward(t_grad, t_dc, t_rest, t_dirs, degree, t_radii)
+    want = oracle.eval_sh_backward(grad_rgb, dc, rest, dirs, degree, radii)
+    for nm, a, b in zip(("dc", "rest", "dirs"), got, want):
+        assert np.array_equal(host(a), b), f"grad {nm} differs"
+
+
+def test_sh_adam_matches_oracle_and_torch(ext, golden):
+    g = golden("sh.npz")
+    sh, dirs, radii = g["sh"], g["dirs"], g["radii"]
+    dc, rest = np.ascontiguousarray(sh[:, :1]), np.ascontiguousarray(sh[:, 1:])
+    t_dc, t_rest, t_dirs, t_radii = cuda(dc, rest, dirs, radii)
+    m_dc, v_dc, m_rest, v_rest = (torch.zeros_like(t) for t in (t_dc, t_dc, t_rest, t_rest))
+    step = torch.zeros((), device="cuda")
+    o_state = {"dc": (np.zeros_like(dc), np.zeros_like(dc)), "rest": (np.zeros_like(rest), np.zeros_like(rest))}
+    for k, grad_rgb in enumerate(g["adam_grad_rgb"], start=1):
+        step += 1
+        ext.eval_sh_backward_adam(cuda(grad_rgb)[0], t_dc, t_rest, t_dirs, 3, t_radii, m_dc, v_dc, m_rest, v_rest, step,
+                                  step, 0.0025, 0.0025 / 20, 0.9, 0.999, 1e-15)
+        gdc, grest, _ = oracle.eval_sh_backward(grad_rgb, dc, rest, dirs, 3, radii)
+        dc, m, v = oracle.adam(dc, *o_state["dc"], gdc, k, 0.0025, 0.9, 0.999, 1e-15)
+        o_state["dc"] = (m, v)
+        rest, m, v = oracle.adam(rest, *o_state["rest"], grest, k, 0.0025 / 20, 0.9, 0.999, 1e-15)
+        o_state["rest"] = (m, v)
+    np.testing.assert_allclose(host(t_dc), dc, rtol=1e-6, atol=1e-7)
+    np.testing.assert_allclose(host(t_rest), rest, rtol=1e-6, atol=1e-7)
+    np.testing.assert_allclose(host(t_dc), g["adam_dc"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(host(t_rest), g["adam_rest"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(host(m_rest), g["adam_m_rest"], rtol=1e-5, atol=1e-7)
+    np.testing.assert_allclose(host(v_rest), g["adam_v_rest"], rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("size", ["64x64", "37x53", "11x11", "546x979"])
+def test_ssim_bit_exact(ext, golden, size):
+    if size == "546x979":
+        rng = np.random.default_rng(0)
+        b = rng.random((546, 979, 3), dtype=np.float32)
+        a = np.clip(b + 0.1 * rng.standard_normal(b.shape).astype(np.float32), 0, 1).astype(np.float32)
+    else:
+        g = golden("ssim.npz")
+        a, b = g[f"{size}_rendered"], g[f"{size}_gt"]
+    want = oracle.ssim_forward(a, b)
+    ta, tb = cuda(a, b)
+    got = ext.ssim_forward(ta, tb)
+    for nm, x, y in zip(("map", "d_mu", "d_aa", "d_ab"), got, want):
+        assert np.array_equal(host(x), y), f"ssim {nm} differs"
+    grad_mean = torch.full((1,), 0.37, device="cuda")
+    got = ext.ssim_backward(grad_mean, ta, tb, *got[1:])
+    assert np.array_equal(host(got), oracle.ssim_backward(np.float32(0.37), a, b, *want[1:]))
+    if size != "546x979":
+        np.testing.assert_allclose(host(ext.ssim_forward(ta, tb)[0]).astype(np.float64).mean(),
+                                   golden("ssim.npz")[f"{size}_ssim"], rtol=1e-5, atol=1e-6)
+
+
+def test_no_device_side_failures(ext):
+    from hds_b200.native import device_status
+
+    assert device_status() == 0
