@@ -6,8 +6,8 @@
 //
 // Blackwell design.  A block owns half a 16x16 tile: 128 pixels, one per thread and one per TMEM
 // lane.  The tile's list is consumed in chunks of 32 gaussians.  Per chunk:
-//   * every thread starts cp.async copies of its share of the chunk's feature rows into the B
-//     operand buffer (no registers held while they fly),
+//   * every thread starts cp.async gathers of its share of the chunk's feature rows into the B
+//     operand buffer, transposed to the K-major core-matrix layout (no registers held while they fly),
 //   * walks the 32 gaussians for its pixel (FP32, the oracle's exact arithmetic), and writes the
 //     TF32-rounded weights as four float4s of the A operand (K-major, conflict-free),
 //   * rounds the landed feature rows to TF32 in place (cvt.rna; the tensor core would otherwise
@@ -43,14 +43,15 @@ struct FwdCfg {
     static constexpr int A_BYTES = PIX * KC * 4;
     static constexpr int B_BYTES = KC * C * 4;
     static constexpr int A_LBO = (PIX / 8) * 128;  // between K-quads: all 16 row groups of 8 rows x 16 B
-    static constexpr int B_LBO = (C / 4) * 128;    // between K-groups of 8 rows: all C/4 column chunks
+    static constexpr int B_LBO = (C / 8) * 128;    // between K-quads: all C/8 groups of 8 channel rows x 16 B
     static constexpr int SMEM = 2 * (A_BYTES + B_BYTES) + 1024;
-    static constexpr uint32_t IDESC = tc::idesc_tf32(128, N_MMA, false, true);
+    // Both operands K-major: tf32 in MN-major layout is only readable with the 128B/32B-atom swizzle.
+    static constexpr uint32_t IDESC = tc::idesc_tf32(128, N_MMA, false, false);
     static_assert(C == 32 || C == 64 || C == 128 || C == 256 || C == 512, "unsupported channel count");
 };
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
@@ -125,17 +126,22 @@ __global__ void __launch_bounds__(128, 1) feature_forward_kernel(
         }
         __syncthreads();
 
-        // B operand (MN-major, no swizzle): element (k, n) at (k/8)*B_LBO + (n/4)*128 + (k%8)*16 + (n%4)*4.
-        // Item i -> k%8 = i%8 so eight consecutive threads fill one contiguous 128-byte row group.
+        // B operand (K-major, no swizzle): element (k, n) at (k/4)*B_LBO + (n/8)*128 + (n%8)*16 + (k%4)*4,
+        // so one 16-byte slot holds four consecutive gaussians of one channel.  Item i = (quad kq,
+        // channel n = i % C): a warp fills 512 contiguous bytes, and each of its four 4-byte gathers
+        // reads 128 contiguous bytes of one gaussian's feature row.
         const uint32_t b_stage = b_base + s * Cfg::B_BYTES;
         for (int i = tid; i < 8 * C; i += Cfg::THREADS) {
-            const int klo = i & 7, rest = i >> 3, q = rest % (C / 4), khi = rest / (C / 4);
-            const int k = khi * 8 + klo;
-            const uint32_t dst = b_stage + khi * Cfg::B_LBO + q * 128 + klo * 16;
-            if (k < valid)
-                cp_async16(dst, features + (size_t)s_id[s][k] * C + 4 * q);
-            else
-                asm volatile("st.shared.v4.f32 [%0], {%1, %1, %1, %1};" ::"r"(dst), "f"(0.0f) : "memory");
+            const int n = i % C, kq = i / C;
+            const uint32_t dst = b_stage + kq * Cfg::B_LBO + (n >> 3) * 128 + (n & 7) * 16;
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int k = kq * 4 + e;
+                if (k < valid)
+                    cp_async4(dst + 4 * e, features + (size_t)s_id[s][k] * C + n);
+                else
+                    asm volatile("st.shared.f32 [%0], %1;" ::"r"(dst + 4 * e), "f"(0.0f) : "memory");
+            }
         }
         cp_async_commit();
 
@@ -175,13 +181,12 @@ __global__ void __launch_bounds__(128, 1) feature_forward_kernel(
             *reinterpret_cast<float4*>(a_row + qd * (Cfg::A_LBO / 4)) = make_float4(w4[0], w4[1], w4[2], w4[3]);
         }
 
-        // Round this thread's landed feature chunks to TF32 in place.
+        // Round this thread's landed feature slots to TF32 in place.
         cp_async_wait_all();
         for (int i = tid; i < 8 * C; i += Cfg::THREADS) {
-            const int klo = i & 7, rest = i >> 3, q = rest % (C / 4), khi = rest / (C / 4);
-            if (khi * 8 + klo >= valid) continue;
-            float4* p = reinterpret_cast<float4*>(smem + 2 * Cfg::A_BYTES + s * Cfg::B_BYTES + khi * Cfg::B_LBO + q * 128 +
-                                                  klo * 16);
+            const int n = i % C, kq = i / C;
+            float4* p = reinterpret_cast<float4*>(smem + 2 * Cfg::A_BYTES + s * Cfg::B_BYTES + kq * Cfg::B_LBO +
+                                                  (n >> 3) * 128 + (n & 7) * 16);
             float4 v = *p;
             *p = make_float4(tc::to_tf32(v.x), tc::to_tf32(v.y), tc::to_tf32(v.z), tc::to_tf32(v.w));
         }
@@ -196,7 +201,8 @@ __global__ void __launch_bounds__(128, 1) feature_forward_kernel(
 #pragma unroll
                 for (int nb = 0; nb < Cfg::N_BLOCKS; nb++) {
                     uint64_t ad = tc::smem_desc(a_stage + ks * 2 * Cfg::A_LBO, Cfg::A_LBO, 128);
-                    uint64_t bd = tc::smem_desc(b_stage + ks * Cfg::B_LBO + nb * (Cfg::N_MMA / 4) * 128, Cfg::B_LBO, 128);
+                    uint64_t bd =
+                        tc::smem_desc(b_stage + ks * 2 * Cfg::B_LBO + nb * (Cfg::N_MMA / 8) * 128, Cfg::B_LBO, 128);
                     tc::mma_tf32(tmem + nb * Cfg::N_MMA, ad, bd, Cfg::IDESC, (c > 0 || ks > 0) ? 1u : 0u);
                 }
             }
