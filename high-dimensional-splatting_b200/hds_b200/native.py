@@ -37,6 +37,8 @@ SIGNATURES = {
     "hds_ssim_forward": [c_int, c_int, P, P, P, P, P, P, S],
     "hds_ssim_backward": [c_int, c_int, P, P, P, P, P, P, P, S],
     "hds_device_status": [ctypes.POINTER(c_int), S],
+    "hds_rasterize_bin_noalloc": [c_int, P, P, P, P, P, P, c_int, c_int, P, P, P, c_int64, P,
+                                  ctypes.POINTER(c_int64), S],
     "hds_last_error": [],
     "hds_abi_version": [],
 }

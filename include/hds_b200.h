@@ -170,6 +170,34 @@ int hds_ssim_backward(int height, int width, const float* grad_mean, const float
  * Synchronises `stream`. */
 int hds_device_status(int* status, hds_stream_t stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * Binning without any allocation.  No counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory where they bin a frame.  Examples: a renderer
+ * inside an application whose GPU memory belongs to another allocator, a real-time loop that must
+ * not call cudaMalloc (it can synchronise the device), or an FFI host that only hands over
+ * finished buffers.  Runs hds_rasterize_prepare followed by hds_rasterize_sort with their scratch
+ * in a fixed file-scope device array of HDS_NOALLOC_SCRATCH_BYTES, so the caller passes only
+ * inputs and outputs.
+ *  - Outputs: conic4 [n,4], color_opacity [n,4], values_sorted (room for values_capacity entries),
+ *    tile_ranges [tiles,2] and *num_duplicates (host).
+ *  - Limits: sizes whose scratch would exceed the array (roughly 500K gaussians with 2M pairs)
+ *    and pair counts above values_capacity are rejected with HDS_ERR_TOO_LARGE before any sort.
+ *  - Memory: the array is 64 MiB per GPU that has called this function, held until the process
+ *    exits.
+ *  - Set-up: the first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress) with that device current.  Make that first call before any stream
+ *    capture.
+ *  - Sharing: every call reuses the same array, so calls that overlap on the GPU (other streams,
+ *    other host threads) race and must be serialised by the caller.
+ *  - Like hds_rasterize_prepare, it synchronises `stream` to read the pair count.
+ * ------------------------------------------------------------------------------------------- */
+#define HDS_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)
+int hds_rasterize_bin_noalloc(int n, const float* means2D, const float* depths, const float* radii,
+                              const float* conics, const float* colors, const float* opacities, int width, int height,
+                              float* conic4, float* color_opacity, int32_t* values_sorted, int64_t values_capacity,
+                              int32_t* tile_ranges, int64_t* num_duplicates, hds_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
