@@ -119,7 +119,8 @@ class CallTimer:
         self.active = False
         self.events = defaultdict(list)
         for name in list(native.SIGNATURES):
-            if name.endswith("_bytes") or name in ("hds_last_error", "hds_abi_version", "hds_device_status"):
+            if name.endswith("_bytes") or name in ("hds_last_error", "hds_abi_version", "hds_device_status",
+                                                   "hds_launch_count"):
                 continue
             fn = getattr(native.lib, name)
             setattr(native.lib, name, self._wrap(name, fn))
@@ -149,11 +150,13 @@ class CallTimer:
 def make_workload(args, device, rank, world):
     import torch
 
-    from hds_b200 import scenes
+    from hds_b200 import parallel, scenes
 
     scene = scenes.config1(0, n=args.gaussians, channels=args.channels)
     cams = scenes.orbit(64)
-    views = [(rank + world * i) % len(cams) for i in range(args.views)]
+    # Round-robin over the orbit; each rank takes args.views views per step (weak scaling).
+    views = parallel.shard_views(len(cams) * args.views * world, rank, world)[:args.views]
+    views = [v % len(cams) for v in views]
     gen = torch.Generator().manual_seed(100 + rank)
     h, w = cams[0].height, cams[0].width
     gt_host = [torch.randint(0, 256, (h, w, 3), dtype=torch.uint8, generator=gen).pin_memory() for _ in views]
@@ -161,7 +164,8 @@ def make_workload(args, device, rank, world):
     feat_grad = torch.rand(h, w, args.channels, generator=gen).to(device) / (h * w)
     leaves = {k: getattr(scene, k).to(device).contiguous().requires_grad_(True)
               for k in ("means", "scales", "quats", "opacities", "sh_dc", "sh_rest", "features")}
-    return {"scene": scene, "cams": cams, "views": views, "gt_host": gt_host, "pose_host": pose_host,
+    bucket = parallel.GradBucket(list(leaves.values()))
+    return {"bucket": bucket, "scene": scene, "cams": cams, "views": views, "gt_host": gt_host, "pose_host": pose_host,
             "gt_dev": [g.to(device) for g in gt_host], "pose_dev": [p.to(device) for p in pose_host],
             "feat_grad": feat_grad, "leaves": leaves, "bg": torch.zeros(3, device=device)}
 
@@ -202,9 +206,7 @@ def run_step(wl, dist, e2e: bool):
             pose, gt = wl["pose_dev"][i], wl["gt_dev"][i]
         losses.append(render_view(wl, i, pose, gt))
     if dist is not None:
-        handles = [dist.all_reduce(p.grad, async_op=True) for p in wl["leaves"].values()]
-        for h in handles:
-            h.wait()
+        wl["bucket"].all_reduce()  # one NCCL all-reduce of every per-gaussian gradient
     loss = torch.stack(losses).sum()
     if e2e:
         return loss.item()  # device -> host read of the step's result
@@ -212,8 +214,7 @@ def run_step(wl, dist, e2e: bool):
 
 
 def zero_grads(wl):
-    for p in wl["leaves"].values():
-        p.grad = None
+    wl["bucket"].zero()
 
 
 def tile_stats(wl, device):
@@ -354,6 +355,7 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
         timer.active = record_calls
+        launches0 = native.lib.hds_launch_count()
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
         start.record()
@@ -363,6 +365,7 @@ def main():
         end.record()
         torch.cuda.synchronize()
         timer.active = False
+        timed.launches = native.lib.hds_launch_count() - launches0
         ms = start.elapsed_time(end)
         if dist is not None:
             t = torch.tensor([ms], device=device)
@@ -373,6 +376,7 @@ def main():
     clocks = ClockSampler(local)
     clocks.start()
     ms = timed(e2e=False, record_calls=True)
+    launches = timed.launches
     clock_info = clocks.stop()
     calls = timer.totals_ms()
     counts = timer.counts()
@@ -396,9 +400,6 @@ def main():
     dominant = max(kernel_calls, key=kernel_calls.get)
     per_launch = kernel_calls[dominant] / max(1, counts[dominant])
     roof = roofline(dominant, per_launch, stats, args, peaks, n)
-    launches = 0
-    for name, cnt in counts.items():
-        launches += cnt
     line = {
         "metric": METRIC, "value": value, "unit": "views/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "ms_per_view": ms / (args.steps * args.views),

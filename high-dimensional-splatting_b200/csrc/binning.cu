@@ -125,6 +125,7 @@ int exclusive_scan(const T* in, T* out, int64_t n, T* block_sums, T* total_out, 
     scan_reduce_kernel<T><<<(unsigned)nb, SCAN_THREADS, 0, stream>>>(in, n, block_sums);
     scan_block_sums_kernel<T><<<1, SCAN_THREADS, 0, stream>>>(block_sums, (int)nb, total_out);
     scan_apply_kernel<T><<<(unsigned)nb, SCAN_THREADS, 0, stream>>>(in, n, block_sums, out);
+    note_launches(2);  // the reduce and block-sum launches; HDS_CHECK_LAUNCH counts the third
     HDS_CHECK_LAUNCH("exclusive_scan");
     return HDS_OK;
 }

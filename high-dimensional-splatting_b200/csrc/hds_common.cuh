@@ -104,11 +104,32 @@ __device__ __forceinline__ PairAlpha pair_alpha(float px, float py, float mx, fl
     return r;
 }
 
+// Conservative half-widths of the box where alpha can reach MIN_ALPHA: the binning extent widened
+// by 0.1% + 0.01 px so rounding never culls a pair the walk would blend (the reference's
+// features.cu:8-17).  Opacity <= MIN_ALPHA never blends (negative extent: hits nothing); a
+// degenerate conic (NaN extent) hits everything.
+__device__ __forceinline__ float2 cull_extent(float a, float b, float c, float opacity) {
+    if (!(opacity > MIN_ALPHA)) return make_float2(-1e30f, -1e30f);
+    float k = sqrtf(2.0f * logf_det(opacity / MIN_ALPHA));
+    float det = a * c - b * b;
+    float ex = k * sqrtf(c / det) * 1.001f + 0.01f;
+    float ey = k * sqrtf(a / det) * 1.001f + 0.01f;
+    if (!(ex >= 0.0f)) ex = 1e30f;
+    if (!(ey >= 0.0f)) ey = 1e30f;
+    return make_float2(ex, ey);
+}
+
+// Does the box mean +- extent touch the pixel-centre rectangle [x0, x1] x [y0, y1]?
+__device__ __forceinline__ bool box_hits(float2 m, float2 e, float x0, float x1, float y0, float y1) {
+    return m.x + e.x >= x0 && m.x - e.x <= x1 && m.y + e.y >= y0 && m.y - e.y <= y1;
+}
+
 // ---------------------------------------------------------------------------------------------
 // host-side error plumbing
 // ---------------------------------------------------------------------------------------------
 void set_error(const char* fmt, ...);
 void clear_error();
+void note_launches(int n);  // counts kernel launches for hds_launch_count()
 
 inline int cuda_fail(cudaError_t err, const char* what) {
     set_error("CUDA error in %s: %s", what, cudaGetErrorString(err));
@@ -117,8 +138,10 @@ inline int cuda_fail(cudaError_t err, const char* what) {
 
 }  // namespace hds
 
+// After exactly one kernel launch: counts it and turns a launch error into HDS_ERR_CUDA.
 #define HDS_CHECK_LAUNCH(name)                                   \
     do {                                                         \
+        hds::note_launches(1);                                   \
         cudaError_t err__ = cudaGetLastError();                  \
         if (err__ != cudaSuccess) return hds::cuda_fail(err__, name); \
     } while (0)

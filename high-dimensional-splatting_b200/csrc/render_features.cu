@@ -5,7 +5,10 @@
 // pass, and the feature image is out[p, c] = sum_j w[p, j] f[j, c] with w = alpha * T.
 //
 // Blackwell design.  A block owns half a 16x16 tile: 128 pixels, one per thread and one per TMEM
-// lane.  The tile's list is consumed in chunks of 32 gaussians.  Per chunk:
+// lane.  The tile's list is consumed in chunks of 32 gaussians; a chunk holds only entries whose
+// opacity-aware box touches the half tile (warp 0 compacts them, keeping each list position for
+// the contributor count), and each warp skips the entries whose box misses its 8 x 4 pixels.
+// Per chunk:
 //   * every thread starts cp.async gathers of its share of the chunk's feature rows into the B
 //     operand buffer, transposed to the K-major core-matrix layout (no registers held while they fly),
 //   * walks the 32 gaussians for its pixel (FP32, the oracle's exact arithmetic), and writes the
@@ -56,6 +59,12 @@ __device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
+// Lane of the (n+1)-th set bit of mask (n >= 0, fewer than popc(mask)).
+__device__ __forceinline__ int nth_set_bit(unsigned mask, int n) {
+    for (int i = 0; i < n; i++) mask &= mask - 1;
+    return __ffs(mask) - 1;
+}
+
 template <int C>
 __global__ void __launch_bounds__(128, 1) feature_forward_kernel(
     int width, int height, int tiles_x, const int2* __restrict__ ranges, const int32_t* __restrict__ values,
@@ -68,6 +77,9 @@ __global__ void __launch_bounds__(128, 1) feature_forward_kernel(
     __shared__ float2 s_mean[2][32];
     __shared__ float4 s_conic[2][32];
     __shared__ float4 s_col[2][32];
+    __shared__ float2 s_ext[2][32];
+    __shared__ int s_pos[2][32];
+    __shared__ int s_filled, s_cursor;
     __shared__ uint64_t s_bar[2];
     __shared__ uint32_t s_tmem;
     __shared__ int s_fail;
@@ -102,34 +114,74 @@ __global__ void __launch_bounds__(128, 1) feature_forward_kernel(
 
     const int2 range = ranges[tile];
     const int count = range.y - range.x;
-    const int chunks = (count + Cfg::KC - 1) / Cfg::KC;
     const bool rgb = image4 != nullptr;
+    // Pixel-centre rectangles of this block's half tile and of this warp's 8 x 4 pixel block.
+    const float hx0 = (float)x0 + 0.5f, hx1 = hx0 + 15.0f, hy0 = (float)y0 + 0.5f, hy1 = hy0 + 7.0f;
+    const float wx0 = (float)(x0 + (warp & 1) * 8) + 0.5f, wx1 = wx0 + 7.0f;
+    const float wy0 = (float)(y0 + (warp >> 1) * 4) + 0.5f, wy1 = wy0 + 3.0f;
 
     float T = 1.0f, ar = 0.0f, ag = 0.0f, ab = 0.0f;
     int last = 0;
     bool done = !inside;
     int issued = 0;
+    int cursor = 0;  // next list position to examine; every thread holds the same value
 
-    for (int c = 0; c < chunks; c++) {
+    for (int c = 0;; c++) {
         const int s = c & 1;
         // The stage's buffers are still read by the MMAs of chunk c - 2 until its commit arrives.
         if (tid == 0 && c >= 2 && !tc::mbar_wait_bounded(&s_bar[s], ((c - 2) >> 1) & 1, WAIT_LIMIT)) s_fail = 1;
         // Barrier: previous chunk fully consumed by this block's threads; stop when every pixel is done.
-        if (__syncthreads_count(!done) == 0 || s_fail) break;
-        const int valid = min(Cfg::KC, count - c * Cfg::KC);
-        if (tid < Cfg::KC && tid < valid) {
-            int g = values[range.x + c * Cfg::KC + tid];
-            s_id[s][tid] = g;
-            s_mean[s][tid] = means2D[g];
-            s_conic[s][tid] = conic4[g];
-            s_col[s][tid] = color_opacity[g];
+        if (__syncthreads_count(!done) == 0 || s_fail || cursor >= count) break;
+
+        // Warp 0 fills the chunk with the next list entries whose opacity-aware box touches this
+        // half tile (the others can never blend here), remembering each one's list position.
+        if (warp == 0) {
+            int filled = 0, cur = cursor;
+            while (filled < Cfg::KC && cur < count) {
+                const int pos = cur + lane;
+                bool hit = false;
+                int g = 0;
+                float2 m = make_float2(0.0f, 0.0f), e = make_float2(0.0f, 0.0f);
+                float4 q = make_float4(0.0f, 0.0f, 0.0f, 0.0f), col = q;
+                if (pos < count) {
+                    g = values[range.x + pos];
+                    m = means2D[g];
+                    q = conic4[g];
+                    col = color_opacity[g];
+                    e = cull_extent(q.x, q.y, q.z, col.w);
+                    hit = box_hits(m, e, hx0, hx1, hy0, hy1);
+                }
+                const unsigned mask = __ballot_sync(FULL_MASK, hit);
+                const int hits = __popc(mask);
+                const int take = min(hits, Cfg::KC - filled);
+                const int rank = __popc(mask & ((1u << lane) - 1u));
+                if (hit && rank < take) {
+                    const int slot = filled + rank;
+                    s_id[s][slot] = g;
+                    s_mean[s][slot] = m;
+                    s_conic[s][slot] = q;
+                    s_col[s][slot] = col;
+                    s_ext[s][slot] = e;
+                    s_pos[s][slot] = pos;
+                }
+                // When the chunk fills mid-batch, resume right after the last entry taken.
+                cur = take < hits ? cur + nth_set_bit(mask, take - 1) + 1 : cur + 32;
+                filled += take;
+            }
+            if (lane == 0) {
+                s_filled = filled;
+                s_cursor = min(cur, count);
+            }
         }
         __syncthreads();
+        const int valid = s_filled;
+        cursor = s_cursor;
+        if (valid == 0) break;  // nothing further in the list touches this half tile
 
         // B operand (K-major, no swizzle): element (k, n) at (k/4)*B_LBO + (n/8)*128 + (n%8)*16 + (k%4)*4,
         // so one 16-byte slot holds four consecutive gaussians of one channel.  Item i = (quad kq,
         // channel n = i % C): a warp fills 512 contiguous bytes, and each of its four 4-byte gathers
-        // reads 128 contiguous bytes of one gaussian's feature row.
+        // reads 128 contiguous bytes of one gaussian's feature row.  Unused rows are zeroed.
         const uint32_t b_stage = b_base + s * Cfg::B_BYTES;
         for (int i = tid; i < 8 * C; i += Cfg::THREADS) {
             const int n = i % C, kq = i / C;
@@ -146,6 +198,7 @@ __global__ void __launch_bounds__(128, 1) feature_forward_kernel(
         cp_async_commit();
 
         // A operand (K-major, no swizzle): row m = tid, K-quad qd at qd*A_LBO + (m/8)*128 + (m%8)*16.
+        // A warp whose 8 x 4 pixel block the gaussian's box misses skips it (weight 0 for all lanes).
         float* a_row = reinterpret_cast<float*>(smem + s * Cfg::A_BYTES + (tid >> 3) * 128 + (tid & 7) * 16);
 #pragma unroll 1
         for (int qd = 0; qd < Cfg::KC / 4; qd++) {
@@ -154,7 +207,7 @@ __global__ void __launch_bounds__(128, 1) feature_forward_kernel(
             for (int e = 0; e < 4; e++) {
                 const int k = qd * 4 + e;
                 float w = 0.0f;
-                if (k < valid && !done) {
+                if (k < valid && !done && box_hits(s_mean[s][k], s_ext[s][k], wx0, wx1, wy0, wy1)) {
                     const float2 m = s_mean[s][k];
                     const float4 q = s_conic[s][k];
                     const float4 col = s_col[s][k];
@@ -172,7 +225,7 @@ __global__ void __launch_bounds__(128, 1) feature_forward_kernel(
                                 ab = fmaf(w, col.z, ab);
                             }
                             T = test;
-                            last = c * Cfg::KC + k + 1;
+                            last = s_pos[s][k] + 1;
                         }
                     }
                 }

@@ -23,19 +23,6 @@ __device__ __forceinline__ int2 warp_pixel(int warp, int lane) {
     return make_int2((warp & 1) * 8 + (lane & 7), (warp >> 1) * 4 + (lane >> 3));
 }
 
-// Conservative half-widths of the box where alpha can reach MIN_ALPHA: the binning extent widened
-// by 0.1% + 0.01 px so rounding never culls a pair the walk would blend (features.cu:8-17).
-__device__ __forceinline__ float2 cull_extent(float a, float b, float c, float opacity) {
-    if (!(opacity > MIN_ALPHA)) return make_float2(-1e30f, -1e30f);  // never blends anywhere
-    float k = sqrtf(2.0f * logf_det(opacity / MIN_ALPHA));
-    float det = a * c - b * b;
-    float ex = k * sqrtf(c / det) * 1.001f + 0.01f;
-    float ey = k * sqrtf(a / det) * 1.001f + 0.01f;
-    if (!(ex >= 0.0f)) ex = 1e30f;
-    if (!(ey >= 0.0f)) ey = 1e30f;
-    return make_float2(ex, ey);
-}
-
 // Sums V values over the warp, scattered: afterwards lane l holds the total of value l * V / 32
 // (for V = 32 that is value l).  V is a power of two <= 32.
 template <int V>
@@ -138,7 +125,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) feature_backward_kernel(
             if (cand < n) {
                 float2 m = s_mean[cand];
                 float2 e = s_ext[cand];
-                hit = m.x + e.x >= rx0 && m.x - e.x <= rx1 && m.y + e.y >= ry0 && m.y - e.y <= ry1;
+                hit = box_hits(m, e, rx0, rx1, ry0, ry1);
             }
             unsigned mask = __ballot_sync(FULL_MASK, hit);
             while (mask) {

@@ -2,7 +2,8 @@
 //
 // Restates forward.cu:141-237 (render_gaussians) and backward.cu:7-164 (render_gaussians_backward)
 // of the reference.  One block per 16x16 tile; the tile's list is staged through shared memory in
-// batches of 256 entries.  The per-pair arithmetic is pair_alpha() and the blend update below, in
+// batches of 256 entries.  Each warp owns an 8x4 pixel block and skips the gaussians whose
+// opacity-aware box misses it.  The per-pair arithmetic is pair_alpha() and the blend update below, in
 // the same order as the CPU oracle, so image, final_T and n_contrib are bit-identical to it.
 #include "hds_common.cuh"
 
@@ -10,6 +11,13 @@ namespace hds {
 namespace {
 
 constexpr int BATCH = TILE_PIXELS;
+
+// Pixel of thread tid inside its 16x16 tile: warp w owns the 8x4 block at ((w & 1) * 8, (w >> 1) * 4), so
+// a warp's pixels are compact and one box test decides whether a gaussian can touch any of them.
+__device__ __forceinline__ int2 tile_pixel(int tid) {
+    const int warp = tid >> 5, lane = tid & 31;
+    return make_int2((warp & 1) * 8 + (lane & 7), (warp >> 1) * 4 + (lane >> 3));
+}
 
 __global__ void __launch_bounds__(TILE_PIXELS) rgb_forward_kernel(int width, int height, int tiles_x,
                                                                   const int2* __restrict__ ranges,
@@ -23,12 +31,16 @@ __global__ void __launch_bounds__(TILE_PIXELS) rgb_forward_kernel(int width, int
     __shared__ float2 s_mean[BATCH];
     __shared__ float4 s_conic[BATCH];
     __shared__ float4 s_color[BATCH];
-    const int tid = threadIdx.x;
+    __shared__ float2 s_ext[BATCH];
+    const int tid = threadIdx.x, warp = tid >> 5;
     const int tile = blockIdx.x;
-    const int px = (tile % tiles_x) * TILE + (tid % TILE);
-    const int py = (tile / tiles_x) * TILE + (tid / TILE);
+    const int x0 = (tile % tiles_x) * TILE, y0 = (tile / tiles_x) * TILE;
+    const int2 lp = tile_pixel(tid);
+    const int px = x0 + lp.x, py = y0 + lp.y;
     const bool inside = px < width && py < height;
     const float cx = (float)px + 0.5f, cy = (float)py + 0.5f;
+    const float wx0 = (float)(x0 + (warp & 1) * 8) + 0.5f, wx1 = wx0 + 7.0f;
+    const float wy0 = (float)(y0 + (warp >> 1) * 4) + 0.5f, wy1 = wy0 + 3.0f;
     const int2 range = ranges[tile];
     const int count = range.y - range.x;
 
@@ -42,14 +54,18 @@ __global__ void __launch_bounds__(TILE_PIXELS) rgb_forward_kernel(int width, int
         int j = base + tid;
         if (j < count) {
             int g = values[range.x + j];
+            float4 q = conic4[g], col = color_opacity[g];
             s_mean[tid] = means2D[g];
-            s_conic[tid] = conic4[g];
-            s_color[tid] = color_opacity[g];
+            s_conic[tid] = q;
+            s_color[tid] = col;
+            s_ext[tid] = cull_extent(q.x, q.y, q.z, col.w);
         }
         __syncthreads();
         const int n = min(BATCH, count - base);
         for (int k = 0; k < n && !done; k++) {
             float2 m = s_mean[k];
+            // Warp-uniform: a gaussian whose box misses this warp's pixels has alpha < MIN_ALPHA on all of them.
+            if (!box_hits(m, s_ext[k], wx0, wx1, wy0, wy1)) continue;
             float4 q = s_conic[k];
             float4 col = s_color[k];
             PairAlpha pa = pair_alpha(cx, cy, m.x, m.y, q.x, q.y, q.z, col.w);
@@ -126,11 +142,15 @@ __global__ void __launch_bounds__(TILE_PIXELS) rgb_backward_kernel(
     __shared__ float2 s_mean[BATCH];
     __shared__ float4 s_conic[BATCH];
     __shared__ float4 s_color[BATCH];
+    __shared__ float2 s_ext[BATCH];
     __shared__ int s_max_last;
-    const int tid = threadIdx.x, lane = tid & 31;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int tile = blockIdx.x;
-    const int px = (tile % tiles_x) * TILE + (tid % TILE);
-    const int py = (tile / tiles_x) * TILE + (tid / TILE);
+    const int x0 = (tile % tiles_x) * TILE, y0 = (tile / tiles_x) * TILE;
+    const int2 lp = tile_pixel(tid);
+    const int px = x0 + lp.x, py = y0 + lp.y;
+    const float wx0 = (float)(x0 + (warp & 1) * 8) + 0.5f, wx1 = wx0 + 7.0f;
+    const float wy0 = (float)(y0 + (warp >> 1) * 4) + 0.5f, wy1 = wy0 + 3.0f;
     const bool inside = px < width && py < height;
     const float cx = (float)px + 0.5f, cy = (float)py + 0.5f;
     const int2 range = ranges[tile];
@@ -161,13 +181,17 @@ __global__ void __launch_bounds__(TILE_PIXELS) rgb_backward_kernel(
         __syncthreads();
         if (tid < n) {
             int g = values[range.x + start + tid];
+            float4 q = conic4[g], col = color_opacity[g];
             s_id[tid] = g;
             s_mean[tid] = means2D[g];
-            s_conic[tid] = conic4[g];
-            s_color[tid] = color_opacity[g];
+            s_conic[tid] = q;
+            s_color[tid] = col;
+            s_ext[tid] = cull_extent(q.x, q.y, q.z, col.w);
         }
         __syncthreads();
         for (int k = n - 1; k >= 0; k--) {
+            // Warp-uniform skip of gaussians whose box misses this warp's pixels (they never blended there).
+            if (!box_hits(s_mean[k], s_ext[k], wx0, wx1, wy0, wy1)) continue;
             float v[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
             float v8 = 0.0f;
             bool contributes = inside && start + k < last;

@@ -41,11 +41,13 @@ SIGNATURES = {
                                   ctypes.POINTER(c_int64), S],
     "hds_last_error": [],
     "hds_abi_version": [],
+    "hds_launch_count": [],
 }
 RESTYPES = {
     "hds_rasterize_prepare_scratch_bytes": c_size_t,
     "hds_rasterize_sort_scratch_bytes": c_size_t,
     "hds_last_error": ctypes.c_char_p,
+    "hds_launch_count": ctypes.c_ulonglong,
 }
 
 

@@ -47,6 +47,9 @@ const char* hds_last_error(void);
 
 /* ABI version of this header (bumped on any signature change). */
 int hds_abi_version(void);
+
+/* Number of kernels this library has launched in the process so far (all threads and devices). */
+unsigned long long hds_launch_count(void);
 #define HDS_ABI_VERSION 1
 
 /* ---------------------------------------------------------------------------------------------

@@ -1,0 +1,130 @@
+"""Host logic of the multi-GPU paths, on CPU: view sharding, tile-row bands (checked by rendering
+bands with the oracle and comparing with the full render), and the flat gradient bucket summed
+over two gloo ranks."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+import oracle
+from helpers import assert_close_abs, assert_grads_close
+from hds_b200 import parallel
+from scenes_np import reference_scene
+
+
+def test_shard_views_cover_every_view_once():
+    for world in (1, 2, 3, 8):
+        got = sorted(v for r in range(world) for v in parallel.shard_views(64, r, world))
+        assert got == list(range(64))
+
+
+@pytest.mark.parametrize("height, world", [(546, 2), (546, 4), (1080, 8), (17, 2), (48, 3)])
+def test_row_bands_partition_whole_tile_rows(height, world):
+    rows = (height + 15) // 16
+    rng = np.random.default_rng(height)
+    for weights in (None, list(rng.random(rows) * 10 + 1)):
+        bands = parallel.row_bands(height, world, weights)
+        assert len(bands) == world and bands[0][0] == 0 and bands[-1][1] == height
+        for (a0, a1), (b0, b1) in zip(bands, bands[1:]):
+            assert a1 == b0
+        for y0, y1 in bands:
+            assert y0 % 16 == 0 and y1 > y0
+
+
+def band_render_np(inputs, width, y0, y1, background):
+    m2, dep, rad, con, col, opac = inputs
+    shifted = m2 - np.array([0.0, y0], np.float32)
+    return oracle.rasterize(shifted, dep, rad, con, col, opac, width, y1 - y0, background=background)
+
+
+def test_bands_stitch_into_the_full_render():
+    width, height = 96, 80
+    inputs = reference_scene(5, 3000, width, height)
+    bg = np.array([0.3, 0.5, 0.7], np.float32)
+    full = oracle.rasterize(*inputs, width, height, background=bg)
+    parts = [band_render_np(inputs, width, y0, y1, bg) for y0, y1 in parallel.row_bands(height, 3)]
+    stitched = np.concatenate([p["image"] for p in parts], axis=0)
+    # Shifting the means re-rounds them (about 1 ulp of a few hundred pixels); a pixel whose pair sits
+    # exactly on a cutoff may flip, so a tiny fraction may differ by more.
+    assert_close_abs(stitched, full["image"], 1e-5, "stitched bands", max_bad_fraction=1e-3)
+    assert np.array_equal(np.concatenate([p["n_contrib"] for p in parts]) > 0, full["n_contrib"] > 0)
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _gloo_worker(rank, world, port, out):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        # 1. The flat bucket sums every parameter's gradient over ranks with one collective.
+        params = [torch.zeros(5, 3, requires_grad=True), torch.zeros(7, requires_grad=True)]
+        bucket = parallel.GradBucket(params)
+        bucket.zero()
+        ((params[0] * (rank + 1)).sum() + (params[1] * 10 * (rank + 1)).sum()).backward()
+        bucket.all_reduce()
+        total = sum(r + 1 for r in range(world))
+        ok_bucket = torch.equal(params[0].grad, torch.full((5, 3), float(total))) and \
+            torch.equal(params[1].grad, torch.full((7,), 10.0 * total))
+
+        # 2. Tile-row split: each rank renders and back-propagates its band with the oracle; the
+        #    all-gathered images and the all-reduced gradients must match the full render.
+        width, height = 64, 48
+        inputs = reference_scene(9, 1500, width, height)
+        m2, dep, rad, con, col, opac = inputs
+        y0, y1 = parallel.row_bands(height, world)[rank]
+        band = band_render_np(inputs, width, y0, y1, None)
+        grad_image = np.random.default_rng(3).random((height, width, 3), dtype=np.float32)
+        shifted = m2 - np.array([0.0, y0], np.float32)
+        g = oracle.render_backward(band["ranges"], band["values"], shifted, con, col, opac, width, y1 - y0,
+                                   band["final_T"], band["n_contrib"], grad_image=grad_image[y0:y1])
+        grads = [torch.from_numpy(np.ascontiguousarray(x)) for x in g[:4]]
+        for t in grads:
+            dist.all_reduce(t)
+        images = [None] * world
+        dist.all_gather_object(images, band["image"])
+        out[rank] = {"bucket": ok_bucket, "image": np.concatenate(images, axis=0),
+                     "grads": [t.numpy() for t in grads]}
+    finally:
+        dist.destroy_process_group()
+
+
+def _gloo_entry(rank, world, port, queue):
+    out = {}
+    _gloo_worker(rank, world, port, out)
+    queue.put((rank, out[rank]))
+
+
+def test_two_gloo_ranks_bucket_and_band_split():
+    world = 2
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_gloo_entry, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(queue.get(timeout=240) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    width, height = 64, 48
+    inputs = reference_scene(9, 1500, width, height)
+    m2, dep, rad, con, col, opac = inputs
+    full = oracle.rasterize(*inputs, width, height)
+    grad_image = np.random.default_rng(3).random((height, width, 3), dtype=np.float32)
+    want = oracle.render_backward(full["ranges"], full["values"], m2, con, col, opac, width, height, full["final_T"],
+                                  full["n_contrib"], grad_image=grad_image)
+    for rank in range(world):
+        r = results[rank]
+        assert r["bucket"]
+        assert_close_abs(r["image"], full["image"], 1e-5, "stitched bands", max_bad_fraction=1e-3)
+        for name, got, w in zip(("means2D", "conics", "colors", "opacities"), r["grads"], want[:4]):
+            assert_grads_close(got, w, name)
