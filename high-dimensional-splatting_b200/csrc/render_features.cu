@@ -4,26 +4,25 @@
 // blends its tile's sorted list front to back with the same alpha / transmittance walk as the RGB
 // pass, and the feature image is out[p, c] = sum_j w[p, j] f[j, c] with w = alpha * T.
 //
-// Blackwell design.  A block owns half a 16x16 tile: 128 pixels, one per thread and one per TMEM
-// lane.  The tile's list is consumed in chunks of 32 gaussians; a chunk holds only entries whose
-// opacity-aware box touches the half tile (warp 0 compacts them, keeping each list position for
-// the contributor count), and each warp skips the entries whose box misses its 8 x 4 pixels.
-// Per chunk:
-//   * every thread starts cp.async gathers of its share of the chunk's feature rows into the B
-//     operand buffer, transposed to the K-major core-matrix layout (no registers held while they fly),
-//   * walks the 32 gaussians for its pixel (FP32, the oracle's exact arithmetic), and writes the
-//     TF32-rounded weights as four float4s of the A operand (K-major, conflict-free),
-//   * rounds the landed feature rows to TF32 in place (cvt.rna; the tensor core would otherwise
-//     truncate them),
-//   * after a barrier, one thread issues 4 x (C / 256) tcgen05.mma (M = 128, N <= 256, K = 8) that
-//     accumulate into TMEM, and commits them to the stage's mbarrier.
-// Two stages alternate, so the tensor cores run chunk c while the threads prepare chunk c + 1.  The
-// accumulators never leave TMEM until the epilogue reads them back with tcgen05.ld and stores the
-// pixel's C channels.  The same walk optionally writes the RGB image, which the reference computes
-// in a separate pass.
+// Blackwell design.  A block owns half a 16x16 tile: 128 pixels, one per TMEM lane.  It runs two
+// warp groups that hand chunks of 32 gaussians to each other through a two-stage ring:
+//   * producer warps 4-7: warp 4 fills a stage with the next list entries whose opacity-aware box
+//     touches the half tile (keeping each one's list position for the contributor count); all four
+//     then gather the entries' feature rows with 4-byte cp.async into the K-major core-matrix
+//     layout of the B operand (8 channel rows x 16 bytes = 4 gaussians), and round them to TF32
+//     (cvt.rna; the tensor core would otherwise truncate);
+//   * pixel warps 0-3: one thread per pixel walks the stage's entries with the oracle's exact FP32
+//     arithmetic (a warp skips entries whose box misses its 8 x 4 pixels) and writes the
+//     TF32-rounded weights as the K-major A operand; then thread 0 issues 4 x C/256
+//     tcgen05.mma (M = 128, N <= 256, K = 8) into the TMEM accumulators and commits them to the
+//     stage's mbarrier.
+// The producers run a stage ahead, so gathering, walking and the tensor cores overlap.  The
+// accumulators stay in TMEM until the epilogue (tcgen05.ld).  The same walk writes the RGB image,
+// final transmittance and contributor count, bit-identical to the RGB kernel.
 //
-// Every mbarrier wait is bounded; a wait that runs out records HDS_ERR_DEVICE in g_status (read by
-// hds_device_status), frees the block's TMEM and returns.
+// Every mbarrier wait is bounded; a group that sees a wait run out stops uniformly (the decision is
+// taken at a group barrier), records HDS_ERR_DEVICE in g_status (read by hds_device_status), frees
+// the block's TMEM and returns.
 #include "hds_common.cuh"
 #include "tcgen05.cuh"
 
@@ -34,11 +33,13 @@ __device__ int g_status = 0;
 namespace {
 
 constexpr uint32_t WAIT_LIMIT = 1u << 22;
+constexpr int STAGES = 2;
+constexpr int PIXEL_BAR = 1, PRODUCER_BAR = 2;  // named barriers of the two warp groups
 
 template <int C>
 struct FwdCfg {
     static constexpr int PIX = 128;
-    static constexpr int THREADS = 128;
+    static constexpr int THREADS = 256;
     static constexpr int KC = 32;
     static constexpr int N_MMA = C < 256 ? C : 256;
     static constexpr int N_BLOCKS = C / N_MMA;
@@ -47,7 +48,7 @@ struct FwdCfg {
     static constexpr int B_BYTES = KC * C * 4;
     static constexpr int A_LBO = (PIX / 8) * 128;  // between K-quads: all 16 row groups of 8 rows x 16 B
     static constexpr int B_LBO = (C / 8) * 128;    // between K-quads: all C/8 groups of 8 channel rows x 16 B
-    static constexpr int SMEM = 2 * (A_BYTES + B_BYTES) + 1024;
+    static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + 1024;
     // Both operands K-major: tf32 in MN-major layout is only readable with the 128B/32B-atom swizzle.
     static constexpr uint32_t IDESC = tc::idesc_tf32(128, N_MMA, false, false);
     static_assert(C == 32 || C == 64 || C == 128 || C == 256 || C == 512, "unsupported channel count");
@@ -59,30 +60,52 @@ __device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
+__device__ __forceinline__ void group_sync(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
+
+// Group barrier that also returns how many of its 128 threads passed pred = true.
+__device__ __forceinline__ int group_sync_count(int id, bool pred) {
+    int r;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.s32 p, %1, 0;\n\tbarrier.cta.red.popc.u32 %0, %2, 128, p;\n\t}"
+        : "=r"(r)
+        : "r"((int)pred), "r"(id)
+        : "memory");
+    return r;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_addr(bar)) : "memory");
+}
+
 // Lane of the (n+1)-th set bit of mask (n >= 0, fewer than popc(mask)).
 __device__ __forceinline__ int nth_set_bit(unsigned mask, int n) {
     for (int i = 0; i < n; i++) mask &= mask - 1;
     return __ffs(mask) - 1;
 }
 
+// One stage's list entries (written by producer warp 4, read by everyone).
+struct Chunk {
+    int id[32];
+    int pos[32];  // position in the tile's list, for the contributor count
+    float2 mean[32];
+    float2 ext[32];
+    float4 conic[32];  // a, b, c, 0
+    float4 col[32];    // r, g, b, opacity
+    int count;
+};
+
 template <int C>
-__global__ void __launch_bounds__(128, 1) feature_forward_kernel(
+__global__ void __launch_bounds__(256, 1) feature_forward_kernel(
     int width, int height, int tiles_x, const int2* __restrict__ ranges, const int32_t* __restrict__ values,
     const float2* __restrict__ means2D, const float4* __restrict__ conic4, const float4* __restrict__ color_opacity,
     const float* __restrict__ features, const float* __restrict__ background, float* __restrict__ feature_image,
     float* __restrict__ final_T, int32_t* __restrict__ n_contrib, float4* __restrict__ image4) {
     using Cfg = FwdCfg<C>;
     extern __shared__ uint8_t smem_raw[];
-    __shared__ int s_id[2][32];
-    __shared__ float2 s_mean[2][32];
-    __shared__ float4 s_conic[2][32];
-    __shared__ float4 s_col[2][32];
-    __shared__ float2 s_ext[2][32];
-    __shared__ int s_pos[2][32];
-    __shared__ int s_filled, s_cursor;
-    __shared__ uint64_t s_bar[2];
+    __shared__ Chunk s_chunk[STAGES];
+    __shared__ uint64_t s_geo_full[STAGES], s_b_full[STAGES], s_mma_done[STAGES];
     __shared__ uint32_t s_tmem;
-    __shared__ int s_fail;
+    __shared__ int s_fail, s_stop;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int tile = blockIdx.x >> 1;
@@ -90,212 +113,261 @@ __global__ void __launch_bounds__(128, 1) feature_forward_kernel(
     const int y0 = (tile / tiles_x) * TILE + (blockIdx.x & 1) * 8;
     if (y0 >= height) return;  // the lower half of a bottom-row tile can lie wholly outside the image
 
-    // Pixel of this thread (= A row = TMEM lane): warp w covers an 8 x 4 block of the 16 x 8 half tile.
-    const int px = x0 + (warp & 1) * 8 + (lane & 7);
-    const int py = y0 + (warp >> 1) * 4 + (lane >> 3);
-    const bool inside = px < width && py < height;
-    const float cx = (float)px + 0.5f, cy = (float)py + 0.5f;
-
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t a_base = tc::smem_addr(smem);
-    const uint32_t b_base = a_base + 2 * Cfg::A_BYTES;
+    const uint32_t b_base = a_base + STAGES * Cfg::A_BYTES;
 
     if (warp == 0) tc::tmem_alloc(&s_tmem, Cfg::TMEM_COLS);
     if (tid == 0) {
-        tc::mbar_init(&s_bar[0], 1);
-        tc::mbar_init(&s_bar[1], 1);
+        for (int s = 0; s < STAGES; s++) {
+            tc::mbar_init(&s_geo_full[s], 32);
+            tc::mbar_init(&s_b_full[s], 128);
+            tc::mbar_init(&s_mma_done[s], 1);
+        }
         tc::fence_mbar_init();
         s_fail = 0;
+        s_stop = 0;
     }
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = s_tmem;
-
     const int2 range = ranges[tile];
     const int count = range.y - range.x;
-    const bool rgb = image4 != nullptr;
-    // Pixel-centre rectangles of this block's half tile and of this warp's 8 x 4 pixel block.
-    const float hx0 = (float)x0 + 0.5f, hx1 = hx0 + 15.0f, hy0 = (float)y0 + 0.5f, hy1 = hy0 + 7.0f;
-    const float wx0 = (float)(x0 + (warp & 1) * 8) + 0.5f, wx1 = wx0 + 7.0f;
-    const float wy0 = (float)(y0 + (warp >> 1) * 4) + 0.5f, wy1 = wy0 + 3.0f;
 
-    float T = 1.0f, ar = 0.0f, ag = 0.0f, ab = 0.0f;
-    int last = 0;
-    bool done = !inside;
-    int issued = 0;
-    int cursor = 0;  // next list position to examine; every thread holds the same value
-
-    for (int c = 0;; c++) {
-        const int s = c & 1;
-        // The stage's buffers are still read by the MMAs of chunk c - 2 until its commit arrives.
-        if (tid == 0 && c >= 2 && !tc::mbar_wait_bounded(&s_bar[s], ((c - 2) >> 1) & 1, WAIT_LIMIT)) s_fail = 1;
-        // Barrier: previous chunk fully consumed by this block's threads; stop when every pixel is done.
-        if (__syncthreads_count(!done) == 0 || s_fail || cursor >= count) break;
-
-        // Warp 0 fills the chunk with the next list entries whose opacity-aware box touches this
-        // half tile (the others can never blend here), remembering each one's list position.
-        if (warp == 0) {
-            int filled = 0, cur = cursor;
-            while (filled < Cfg::KC && cur < count) {
-                const int pos = cur + lane;
-                bool hit = false;
-                int g = 0;
-                float2 m = make_float2(0.0f, 0.0f), e = make_float2(0.0f, 0.0f);
-                float4 q = make_float4(0.0f, 0.0f, 0.0f, 0.0f), col = q;
-                if (pos < count) {
-                    g = values[range.x + pos];
-                    m = means2D[g];
-                    q = conic4[g];
-                    col = color_opacity[g];
-                    e = cull_extent(q.x, q.y, q.z, col.w);
-                    hit = box_hits(m, e, hx0, hx1, hy0, hy1);
-                }
-                const unsigned mask = __ballot_sync(FULL_MASK, hit);
-                const int hits = __popc(mask);
-                const int take = min(hits, Cfg::KC - filled);
-                const int rank = __popc(mask & ((1u << lane) - 1u));
-                if (hit && rank < take) {
-                    const int slot = filled + rank;
-                    s_id[s][slot] = g;
-                    s_mean[s][slot] = m;
-                    s_conic[s][slot] = q;
-                    s_col[s][slot] = col;
-                    s_ext[s][slot] = e;
-                    s_pos[s][slot] = pos;
-                }
-                // When the chunk fills mid-batch, resume right after the last entry taken.
-                cur = take < hits ? cur + nth_set_bit(mask, take - 1) + 1 : cur + 32;
-                filled += take;
+    if (warp >= 4) {
+        // ------------------------------------------------------------------ producer warps 4-7
+        const int ptid = tid - 128;
+        // Pixel-centre rectangle of the half tile.
+        const float hx0 = (float)x0 + 0.5f, hx1 = hx0 + 15.0f, hy0 = (float)y0 + 0.5f, hy1 = hy0 + 7.0f;
+        int cursor = 0;
+        for (int c = 0;; c++) {
+            const int s = c % STAGES;
+            Chunk& ch = s_chunk[s];
+            // The stage is free once the MMAs of chunk c - STAGES have read it.  Whether to stop is
+            // thread 0's view, broadcast by the barrier, so warp 4's lanes never diverge on it.
+            bool halt = false;
+            if (ptid == 0) {
+                if (c >= STAGES && !tc::mbar_wait_bounded(&s_mma_done[s], ((c - STAGES) / STAGES) & 1, WAIT_LIMIT))
+                    s_fail = 1;
+                halt = *(volatile int*)&s_stop || *(volatile int*)&s_fail;
             }
-            if (lane == 0) {
-                s_filled = filled;
-                s_cursor = min(cur, count);
-            }
-        }
-        __syncthreads();
-        const int valid = s_filled;
-        cursor = s_cursor;
-        if (valid == 0) break;  // nothing further in the list touches this half tile
-
-        // B operand (K-major, no swizzle): element (k, n) at (k/4)*B_LBO + (n/8)*128 + (n%8)*16 + (k%4)*4,
-        // so one 16-byte slot holds four consecutive gaussians of one channel.  Item i = (quad kq,
-        // channel n = i % C): a warp fills 512 contiguous bytes, and each of its four 4-byte gathers
-        // reads 128 contiguous bytes of one gaussian's feature row.  Unused rows are zeroed.
-        const uint32_t b_stage = b_base + s * Cfg::B_BYTES;
-        for (int i = tid; i < 8 * C; i += Cfg::THREADS) {
-            const int n = i % C, kq = i / C;
-            const uint32_t dst = b_stage + kq * Cfg::B_LBO + (n >> 3) * 128 + (n & 7) * 16;
+            const bool stop = group_sync_count(PRODUCER_BAR, halt) != 0 || cursor >= count;
+            if (warp == 4) {
+                int filled = 0, cur = cursor;
+                if (!stop) {
+                    while (filled < Cfg::KC && cur < count) {
+                        // Two batches of 32 candidates per round trip to memory.
+                        int g[2];
+                        float2 m[2], e[2];
+                        float4 q[2], col[2];
+                        bool hit[2];
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const int k = kq * 4 + e;
-                if (k < valid)
-                    cp_async4(dst + 4 * e, features + (size_t)s_id[s][k] * C + n);
-                else
-                    asm volatile("st.shared.f32 [%0], %1;" ::"r"(dst + 4 * e), "f"(0.0f) : "memory");
-            }
-        }
-        cp_async_commit();
-
-        // A operand (K-major, no swizzle): row m = tid, K-quad qd at qd*A_LBO + (m/8)*128 + (m%8)*16.
-        // A warp whose 8 x 4 pixel block the gaussian's box misses skips it (weight 0 for all lanes).
-        float* a_row = reinterpret_cast<float*>(smem + s * Cfg::A_BYTES + (tid >> 3) * 128 + (tid & 7) * 16);
-#pragma unroll 1
-        for (int qd = 0; qd < Cfg::KC / 4; qd++) {
-            float w4[4];
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const int k = qd * 4 + e;
-                float w = 0.0f;
-                if (k < valid && !done && box_hits(s_mean[s][k], s_ext[s][k], wx0, wx1, wy0, wy1)) {
-                    const float2 m = s_mean[s][k];
-                    const float4 q = s_conic[s][k];
-                    const float4 col = s_col[s][k];
-                    PairAlpha pa = pair_alpha(cx, cy, m.x, m.y, q.x, q.y, q.z, col.w);
-                    float alpha = fminf(MAX_ALPHA, pa.raw);
-                    if (!(alpha < MIN_ALPHA)) {
-                        float test = T * (1.0f - alpha);
-                        if (test < MIN_T) {
-                            done = true;
-                        } else {
-                            w = alpha * T;
-                            if (rgb) {
-                                ar = fmaf(w, col.x, ar);
-                                ag = fmaf(w, col.y, ag);
-                                ab = fmaf(w, col.z, ab);
+                        for (int b = 0; b < 2; b++) {
+                            const int pos = cur + 32 * b + lane;
+                            hit[b] = false;
+                            g[b] = 0;
+                            m[b] = e[b] = make_float2(0.0f, 0.0f);
+                            q[b] = col[b] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                            if (pos < count) {
+                                g[b] = values[range.x + pos];
+                                m[b] = means2D[g[b]];
+                                q[b] = conic4[g[b]];
+                                col[b] = color_opacity[g[b]];
+                                e[b] = cull_extent(q[b].x, q[b].y, q[b].z, col[b].w);
+                                hit[b] = box_hits(m[b], e[b], hx0, hx1, hy0, hy1);
                             }
-                            T = test;
-                            last = s_pos[s][k] + 1;
+                        }
+#pragma unroll
+                        for (int b = 0; b < 2; b++) {
+                            if (filled == Cfg::KC || cur >= count) break;
+                            const unsigned mask = __ballot_sync(FULL_MASK, hit[b]);
+                            const int hits = __popc(mask);
+                            const int take = min(hits, Cfg::KC - filled);
+                            const int rank = __popc(mask & ((1u << lane) - 1u));
+                            if (hit[b] && rank < take) {
+                                const int slot = filled + rank;
+                                ch.id[slot] = g[b];
+                                ch.pos[slot] = cur + lane;
+                                ch.mean[slot] = m[b];
+                                ch.ext[slot] = e[b];
+                                ch.conic[slot] = q[b];
+                                ch.col[slot] = col[b];
+                            }
+                            // When the chunk fills mid-batch, resume right after the last entry taken.
+                            cur = take < hits ? cur + nth_set_bit(mask, take - 1) + 1 : cur + 32;
+                            filled += take;
                         }
                     }
                 }
-                w4[e] = tc::to_tf32(w);
+                if (lane == 0) ch.count = filled;
+                mbar_arrive(&s_geo_full[s]);  // every lane, after its own writes
+                cursor = min(cur, count);
             }
-            *reinterpret_cast<float4*>(a_row + qd * (Cfg::A_LBO / 4)) = make_float4(w4[0], w4[1], w4[2], w4[3]);
-        }
+            group_sync(PRODUCER_BAR);  // the chunk's entries (and count) are visible to warps 5-7
+            const int valid = ch.count;
+            if (valid == 0) break;
 
-        // Round this thread's landed feature slots to TF32 in place.
-        cp_async_wait_all();
-        for (int i = tid; i < 8 * C; i += Cfg::THREADS) {
-            const int n = i % C, kq = i / C;
-            float4* p = reinterpret_cast<float4*>(smem + 2 * Cfg::A_BYTES + s * Cfg::B_BYTES + kq * Cfg::B_LBO +
-                                                  (n >> 3) * 128 + (n & 7) * 16);
-            float4 v = *p;
-            *p = make_float4(tc::to_tf32(v.x), tc::to_tf32(v.y), tc::to_tf32(v.z), tc::to_tf32(v.w));
-        }
-        tc::fence_proxy_async();
-        __syncthreads();
-
-        if (tid == 0) {
-            tc::fence_after_sync();
-            const uint32_t a_stage = a_base + s * Cfg::A_BYTES;
+            // B operand (K-major, no swizzle): element (k, n) at (k/4)*B_LBO + (n/8)*128 + (n%8)*16 + (k%4)*4,
+            // one 16-byte slot = four consecutive gaussians of one channel.  Item i = (quad kq, channel
+            // n = i % C): a warp fills 512 contiguous bytes, and each 4-byte gather of a warp reads 128
+            // contiguous bytes of one feature row.  Unused rows are zeroed.
+            const uint32_t b_stage = b_base + s * Cfg::B_BYTES;
+            for (int i = ptid; i < 8 * C; i += 128) {
+                const int n = i % C, kq = i / C;
+                const uint32_t dst = b_stage + kq * Cfg::B_LBO + (n >> 3) * 128 + (n & 7) * 16;
 #pragma unroll
-            for (int ks = 0; ks < Cfg::KC / 8; ks++) {
-#pragma unroll
-                for (int nb = 0; nb < Cfg::N_BLOCKS; nb++) {
-                    uint64_t ad = tc::smem_desc(a_stage + ks * 2 * Cfg::A_LBO, Cfg::A_LBO, 128);
-                    uint64_t bd =
-                        tc::smem_desc(b_stage + ks * 2 * Cfg::B_LBO + nb * (Cfg::N_MMA / 8) * 128, Cfg::B_LBO, 128);
-                    tc::mma_tf32(tmem + nb * Cfg::N_MMA, ad, bd, Cfg::IDESC, (c > 0 || ks > 0) ? 1u : 0u);
+                for (int e = 0; e < 4; e++) {
+                    const int k = kq * 4 + e;
+                    if (k < valid)
+                        cp_async4(dst + 4 * e, features + (size_t)ch.id[k] * C + n);
+                    else
+                        asm volatile("st.shared.f32 [%0], %1;" ::"r"(dst + 4 * e), "f"(0.0f) : "memory");
                 }
             }
-            tc::commit(&s_bar[s]);
+            cp_async_commit();
+            cp_async_wait_all();
+            for (int i = ptid; i < 8 * C; i += 128) {
+                const int n = i % C, kq = i / C;
+                float4* p = reinterpret_cast<float4*>(smem + STAGES * Cfg::A_BYTES + s * Cfg::B_BYTES +
+                                                      kq * Cfg::B_LBO + (n >> 3) * 128 + (n & 7) * 16);
+                const float4 v = *p;
+                *p = make_float4(tc::to_tf32(v.x), tc::to_tf32(v.y), tc::to_tf32(v.z), tc::to_tf32(v.w));
+            }
+            tc::fence_proxy_async();
+            mbar_arrive(&s_b_full[s]);
         }
-        issued = c + 1;
-    }
+    } else {
+        // ------------------------------------------------------------------ pixel warps 0-3
+        // Pixel of this thread (= A row = TMEM lane): warp w covers an 8 x 4 block of the half tile.
+        const int px = x0 + (warp & 1) * 8 + (lane & 7);
+        const int py = y0 + (warp >> 1) * 4 + (lane >> 3);
+        const bool inside = px < width && py < height;
+        const float cx = (float)px + 0.5f, cy = (float)py + 0.5f;
+        const float wx0 = (float)(x0 + (warp & 1) * 8) + 0.5f, wx1 = wx0 + 7.0f;
+        const float wy0 = (float)(y0 + (warp >> 1) * 4) + 0.5f, wy1 = wy0 + 3.0f;
+        const bool rgb = image4 != nullptr;
 
-    // Every issued MMA has completed once the last chunk's commit arrives.
-    if (issued > 0 && tid == 0 && !s_fail &&
-        !tc::mbar_wait_bounded(&s_bar[(issued - 1) & 1], ((issued - 1) >> 1) & 1, WAIT_LIMIT))
-        s_fail = 1;
-    __syncthreads();
-    tc::fence_after_sync();
-    const bool have = issued > 0 && !s_fail;
+        float T = 1.0f, ar = 0.0f, ag = 0.0f, ab = 0.0f;
+        int last = 0;
+        bool done = !inside;
+        int committed = 0;  // chunks whose MMAs thread 0 issued and committed
+        for (int c = 0;; c++) {
+            const int s = c % STAGES;
+            const Chunk& ch = s_chunk[s];
+            bool bad = false;
+            if (tid == 0) {
+                bad = *(volatile int*)&s_fail;
+                if (!bad && !tc::mbar_wait_bounded(&s_geo_full[s], (c / STAGES) & 1, WAIT_LIMIT)) {
+                    s_fail = 1;
+                    bad = true;
+                }
+            }
+            if (group_sync_count(PIXEL_BAR, bad) != 0) break;
+            const int valid = ch.count;
+            if (valid == 0) break;
 
-    const size_t p = (size_t)py * width + px;
-    float* dst = feature_image + p * C;
-    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+            // A operand (K-major, no swizzle): row m = tid, K-quad qd at qd*A_LBO + (m/8)*128 + (m%8)*16.
+            float* a_row = reinterpret_cast<float*>(smem + s * Cfg::A_BYTES + (tid >> 3) * 128 + (tid & 7) * 16);
+            const bool warp_done = __all_sync(FULL_MASK, done);
 #pragma unroll 1
-    for (int col = 0; col < C; col += 16) {
-        float v[16];
-        if (have) {
-            tc::tmem_ld16(lane_addr + col, v);  // warp-collective: every lane executes it
-        } else {
+            for (int qd = 0; qd < Cfg::KC / 4; qd++) {
+                float w4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                if (!warp_done) {
 #pragma unroll
-            for (int i = 0; i < 16; i++) v[i] = 0.0f;
+                    for (int e = 0; e < 4; e++) {
+                        const int k = qd * 4 + e;
+                        float w = 0.0f;
+                        if (k < valid && !done && box_hits(ch.mean[k], ch.ext[k], wx0, wx1, wy0, wy1)) {
+                            const float2 m = ch.mean[k];
+                            const float4 q = ch.conic[k];
+                            const float4 col = ch.col[k];
+                            PairAlpha pa = pair_alpha(cx, cy, m.x, m.y, q.x, q.y, q.z, col.w);
+                            float alpha = fminf(MAX_ALPHA, pa.raw);
+                            if (!(alpha < MIN_ALPHA)) {
+                                float test = T * (1.0f - alpha);
+                                if (test < MIN_T) {
+                                    done = true;
+                                } else {
+                                    w = alpha * T;
+                                    if (rgb) {
+                                        ar = fmaf(w, col.x, ar);
+                                        ag = fmaf(w, col.y, ag);
+                                        ab = fmaf(w, col.z, ab);
+                                    }
+                                    T = test;
+                                    last = ch.pos[k] + 1;
+                                }
+                            }
+                        }
+                        w4[e] = tc::to_tf32(w);
+                    }
+                }
+                *reinterpret_cast<float4*>(a_row + qd * (Cfg::A_LBO / 4)) = make_float4(w4[0], w4[1], w4[2], w4[3]);
+            }
+            tc::fence_proxy_async();
+            // Every pixel thread has written its A row; tell the producers when all pixels are done.
+            if (group_sync_count(PIXEL_BAR, done) == 128 && tid == 0) *(volatile int*)&s_stop = 1;
+            if (tid == 0) {
+                if (!tc::mbar_wait_bounded(&s_b_full[s], (c / STAGES) & 1, WAIT_LIMIT)) {
+                    s_fail = 1;
+                } else {
+                    tc::fence_after_sync();
+                    const uint32_t a_stage = a_base + s * Cfg::A_BYTES;
+                    const uint32_t b_stage = b_base + s * Cfg::B_BYTES;
+#pragma unroll
+                    for (int ks = 0; ks < Cfg::KC / 8; ks++) {
+#pragma unroll
+                        for (int nb = 0; nb < Cfg::N_BLOCKS; nb++) {
+                            uint64_t ad = tc::smem_desc(a_stage + ks * 2 * Cfg::A_LBO, Cfg::A_LBO, 128);
+                            uint64_t bd = tc::smem_desc(b_stage + ks * 2 * Cfg::B_LBO + nb * (Cfg::N_MMA / 8) * 128,
+                                                        Cfg::B_LBO, 128);
+                            tc::mma_tf32(tmem + nb * Cfg::N_MMA, ad, bd, Cfg::IDESC, (c > 0 || ks > 0) ? 1u : 0u);
+                        }
+                    }
+                    tc::commit(&s_mma_done[s]);
+                    committed = c + 1;
+                }
+            }
+        }
+
+        // tcgen05 operations complete in issue order: once the last commit arrives, every MMA has
+        // finished.  This wait runs on the failure path too, so TMEM is never freed under an MMA.
+        bool ok = false;
+        if (tid == 0) {
+            ok = committed > 0 && tc::mbar_wait_bounded(&s_mma_done[(committed - 1) % STAGES],
+                                                        ((committed - 1) / STAGES) & 1, WAIT_LIMIT);
+            if (committed > 0 && !ok) s_fail = 1;
+            ok = ok && !*(volatile int*)&s_fail;
+        }
+        // Uniform across the group: it decides whether the warp-collective tcgen05.ld runs.
+        const bool have = group_sync_count(PIXEL_BAR, ok) != 0;
+        tc::fence_after_sync();
+        const size_t p = (size_t)py * width + px;
+        float* dst = feature_image + p * C;
+        const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+#pragma unroll 1
+        for (int col = 0; col < C; col += 16) {
+            float v[16];
+            if (have) {
+                tc::tmem_ld16(lane_addr + col, v);  // warp-collective: every lane executes it
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; i++) v[i] = 0.0f;
+            }
+            if (inside) {
+#pragma unroll
+                for (int i = 0; i < 16; i += 4)
+                    *reinterpret_cast<float4*>(dst + col + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+            }
         }
         if (inside) {
-#pragma unroll
-            for (int i = 0; i < 16; i += 4)
-                *reinterpret_cast<float4*>(dst + col + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+            final_T[p] = T;
+            n_contrib[p] = last;
+            if (rgb)
+                image4[p] = make_float4(fmaf(T, background[0], ar), fmaf(T, background[1], ag),
+                                        fmaf(T, background[2], ab), 0.0f);
         }
-    }
-    if (inside) {
-        final_T[p] = T;
-        n_contrib[p] = last;
-        if (rgb)
-            image4[p] = make_float4(fmaf(T, background[0], ar), fmaf(T, background[1], ag), fmaf(T, background[2], ab),
-                                    0.0f);
     }
     tc::fence_before_sync();
     __syncthreads();
