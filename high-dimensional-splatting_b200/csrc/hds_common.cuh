@@ -87,6 +87,16 @@ __device__ __forceinline__ bool tile_rect(float u, float v, float a, float b, fl
 
 // The per-pair opacity term of every blend: mahalanobis distance of the pixel centre under the
 // conic, G = exp(-m/2), raw alpha = opacity * G (forward.cu:197-208).  Same order as the oracle.
+// Reads and clears the feature backward kernel's device status (render_features_bwd.cu); the
+// copies are queued on `stream`.
+int read_and_clear_backward_status(int* status, cudaStream_t stream);
+
+// Lane of the (n+1)-th set bit of mask (n >= 0, fewer than popc(mask)).
+__device__ __forceinline__ int nth_set_bit(unsigned mask, int n) {
+    for (int i = 0; i < n; i++) mask &= mask - 1;
+    return __ffs(mask) - 1;
+}
+
 struct PairAlpha {
     float dx, dy, G, raw;
 };

@@ -60,28 +60,6 @@ __device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-__device__ __forceinline__ void group_sync(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
-
-// Group barrier that also returns how many of its 128 threads passed pred = true.
-__device__ __forceinline__ int group_sync_count(int id, bool pred) {
-    int r;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.s32 p, %1, 0;\n\tbarrier.cta.red.popc.u32 %0, %2, 128, p;\n\t}"
-        : "=r"(r)
-        : "r"((int)pred), "r"(id)
-        : "memory");
-    return r;
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_addr(bar)) : "memory");
-}
-
-// Lane of the (n+1)-th set bit of mask (n >= 0, fewer than popc(mask)).
-__device__ __forceinline__ int nth_set_bit(unsigned mask, int n) {
-    for (int i = 0; i < n; i++) mask &= mask - 1;
-    return __ffs(mask) - 1;
-}
 
 // One stage's list entries (written by producer warp 4, read by everyone).
 struct Chunk {
@@ -152,7 +130,7 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
                     s_fail = 1;
                 halt = *(volatile int*)&s_stop || *(volatile int*)&s_fail;
             }
-            const bool stop = group_sync_count(PRODUCER_BAR, halt) != 0 || cursor >= count;
+            const bool stop = tc::group_sync_count(PRODUCER_BAR, halt) != 0 || cursor >= count;
             if (warp == 4) {
                 int filled = 0, cur = cursor;
                 if (!stop) {
@@ -201,10 +179,10 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
                     }
                 }
                 if (lane == 0) ch.count = filled;
-                mbar_arrive(&s_geo_full[s]);  // every lane, after its own writes
+                tc::mbar_arrive(&s_geo_full[s]);  // every lane, after its own writes
                 cursor = min(cur, count);
             }
-            group_sync(PRODUCER_BAR);  // the chunk's entries (and count) are visible to warps 5-7
+            tc::group_sync(PRODUCER_BAR);  // the chunk's entries (and count) are visible to warps 5-7
             const int valid = ch.count;
             if (valid == 0) break;
 
@@ -235,7 +213,7 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
                 *p = make_float4(tc::to_tf32(v.x), tc::to_tf32(v.y), tc::to_tf32(v.z), tc::to_tf32(v.w));
             }
             tc::fence_proxy_async();
-            mbar_arrive(&s_b_full[s]);
+            tc::mbar_arrive(&s_b_full[s]);
         }
     } else {
         // ------------------------------------------------------------------ pixel warps 0-3
@@ -263,7 +241,7 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
                     bad = true;
                 }
             }
-            if (group_sync_count(PIXEL_BAR, bad) != 0) break;
+            if (tc::group_sync_count(PIXEL_BAR, bad) != 0) break;
             const int valid = ch.count;
             if (valid == 0) break;
 
@@ -307,7 +285,7 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
             }
             tc::fence_proxy_async();
             // Every pixel thread has written its A row; tell the producers when all pixels are done.
-            if (group_sync_count(PIXEL_BAR, done) == 128 && tid == 0) *(volatile int*)&s_stop = 1;
+            if (tc::group_sync_count(PIXEL_BAR, done) == 128 && tid == 0) *(volatile int*)&s_stop = 1;
             if (tid == 0) {
                 if (!tc::mbar_wait_bounded(&s_b_full[s], (c / STAGES) & 1, WAIT_LIMIT)) {
                     s_fail = 1;
@@ -341,7 +319,7 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
             ok = ok && !*(volatile int*)&s_fail;
         }
         // Uniform across the group: it decides whether the warp-collective tcgen05.ld runs.
-        const bool have = group_sync_count(PIXEL_BAR, ok) != 0;
+        const bool have = tc::group_sync_count(PIXEL_BAR, ok) != 0;
         tc::fence_after_sync();
         const size_t p = (size_t)py * width + px;
         float* dst = feature_image + p * C;
@@ -424,9 +402,11 @@ extern "C" int hds_render_features_forward(int n, int channels, int width, int h
 extern "C" int hds_device_status(int* status, hds_stream_t stream) {
     clear_error();
     HDS_REQUIRE(status != nullptr, HDS_ERR_INVALID, "device_status: null output");
-    int zero = 0;
-    HDS_CHECK_CUDA(cudaMemcpyFromSymbolAsync(status, g_status, sizeof(int), 0, cudaMemcpyDeviceToHost, stream));
+    int zero = 0, forward = 0, backward = 0;
+    HDS_CHECK_CUDA(cudaMemcpyFromSymbolAsync(&forward, g_status, sizeof(int), 0, cudaMemcpyDeviceToHost, stream));
     HDS_CHECK_CUDA(cudaMemcpyToSymbolAsync(g_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, stream));
+    if (int rc = read_and_clear_backward_status(&backward, stream)) return rc;
     HDS_CHECK_CUDA(cudaStreamSynchronize(stream));
+    *status = forward ? forward : backward;
     return HDS_OK;
 }

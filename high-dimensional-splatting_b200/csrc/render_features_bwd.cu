@@ -1,228 +1,573 @@
-// render_features_bwd.cu -- backward of the feature blend.
+// render_features_bwd.cu -- backward of the feature blend on tcgen05 tensor cores.
 //
 // Restates features.cu:350-616 of the reference (render_features_backward + host wrapper): each
 // pixel walks its tile's list back to front from its last contributor, recovering T by division,
-// and produces dL/dfeatures (w * dL/dout summed over pixels), and dL/dalpha = T (dot - behind_dot)
-// with dot = f . dL/dout, which drives the opacity, mean and conic gradients.
+// and produces dL/dfeatures[g, c] = sum_p w[p, g] dL/dout[p, c] (w = alpha * T), and
+// dL/dalpha = T (dot - behind) with dot[p, g] = f[g] . dL/dout[p], which drives the opacity, mean
+// and conic gradients.  As in the reference, channels are processed in slices and every slice adds
+// its share of the geometric gradients (they are linear in the dots).
 //
-// Layout (the reference's "lane owns a channel slice"): a block owns one 16x16 tile and a slice of
-// W channels; warp w owns an 8x4 pixel block and lane l owns channels l, l+32, ... of the slice for
-// all 32 pixels of its warp, so dL/dout for (pixel, channel) sits in that lane's registers.  The
-// feature gradient of a gaussian then accumulates inside one lane with no shuffles; shuffles are
-// used only to finish the per-pixel dot (a 32-value reduce-scatter) and the six geometric
-// gradients.  Gaussians whose opacity-aware box misses a warp's pixel block are skipped by ballot.
+// Blackwell design.  The two contractions run on the tensor cores; only the per-pixel recurrence
+// (T, behind) and the geometric partials stay on the FP32 pipes.  A block owns half a 16x16 tile
+// (128 pixels = 128 TMEM lanes) and a slice of CK <= 128 channels:
+//   * dL/dout of the block, G[p][c], is staged once in shared memory as bf16 hi + lo
+//     (x = hi + lo + O(2^-17 x)), in a layout that is at once the K-major A operand of
+//     dot = G F^T and the MN-major A operand of dF^T = G^T W;
+//   * producer warps 4-7 walk the tile's list back to front in chunks of 32 entries whose
+//     opacity-aware box touches the half tile, gather the chunk's feature slices as bf16 hi + lo,
+//     and issue dot[p, k] (M = 128 pixels, N = 32, K = CK) as three MMAs
+//     (hi.hi + hi.lo + lo.hi: relative error ~2^-16 against the FP32 sum);
+//   * pixel warps 0-3 read their 32 dots from TMEM and run only what is serial per pixel: alpha,
+//     the recurrence, w = T * alpha (written as the MN-major B operand, bf16 hi + lo) and
+//     u = dL/dalpha * G (fp32); then they issue dF^T[c, k] (M = 128 channels, N = 32,
+//     K = 128 pixels), again as three MMAs;
+//   * the producers turn u into the geometric gradients -- they are linear in the moments
+//     sum_p u {1, dx, dy, dx^2, dx dy, dy^2}, one entry per lane, FP32 -- and drain dF^T from TMEM
+//     (lane = channel) into coalesced atomics.
+// Stages rotate through a three-deep ring, so gathering, walking and both contractions overlap.
+// Every mbarrier wait is bounded; a group that sees one run out stops (decided group-uniformly at a
+// barrier), records HDS_ERR_DEVICE for hds_device_status, waits for its own MMAs, frees TMEM and
+// returns.
+#include <cuda_bf16.h>
+
 #include "hds_common.cuh"
+#include "tcgen05.cuh"
 
 namespace hds {
+
+__device__ int g_backward_status = 0;
+
 namespace {
 
-constexpr int BWD_THREADS = 256;
-constexpr int BWD_BATCH = 128;
+constexpr uint32_t WAIT_LIMIT = 1u << 22;
+constexpr int STAGES = 3;
+constexpr int KC = 32;      // list entries per chunk (the N of both MMAs)
+constexpr int PIX = 128;    // pixels per block
+constexpr int MAX_CK = 128; // channels per block (the M of the dF MMA)
+constexpr int LIST_SLOTS = 6;  // list ring: the list warp runs up to three chunks past the operand stages
+constexpr int THREADS = 416;   // pixel warps 0-7, list warp 8, operand warps 9-12
+constexpr int PIXEL_THREADS = 256, LIST_WARP = 8, OPERAND_WARP0 = 9;
+constexpr int PIXEL_BAR = 1, OPERAND_BAR = 2;
+constexpr int G_BYTES = PIX * MAX_CK * 2;  // one bf16 copy of G: [c/8][p][c%8]
+constexpr int W_BYTES = PIX * KC * 2;      // one bf16 copy of W: [k/8][p][k%8]
+// u = dL/dalpha * G per (pixel, entry), fp32 as [k/4][p][k%4]; the quad rows are padded by 16 bytes
+// so that 32 lanes reading one pixel's 32 entries hit 32 different banks.
+constexpr int U_QUAD_STRIDE = PIX * 16 + 16;
+constexpr int U_BYTES = (KC / 4) * U_QUAD_STRIDE;
+constexpr uint32_t TMEM_COLS = 256;        // dots at s*32, dF^T at 128 + s*32
 
-__device__ __forceinline__ int2 warp_pixel(int warp, int lane) {
-    return make_int2((warp & 1) * 8 + (lane & 7), (warp >> 1) * 4 + (lane >> 3));
+template <int CK>
+struct BwdCfg {
+    static constexpr int F_BYTES = KC * CK * 2;  // one bf16 copy of a chunk's features: [c/8][k][c%8]
+    static constexpr int STAGE_BYTES = 2 * F_BYTES + 2 * W_BYTES + U_BYTES;
+    static constexpr int SMEM = 2 * G_BYTES + STAGES * STAGE_BYTES + 1024;
+    static constexpr int F_LBO = (KC / 8) * 128;  // 512: between 8-channel blocks of F
+    // dot = G F^T: A = G K-major (SBO 128 between pixel groups, LBO 2048 between channel blocks),
+    //              B = F K-major (SBO 128 between entry groups, LBO 512 between channel blocks).
+    static constexpr uint32_t IDESC_DOT = tc::idesc_bf16(128, KC, false, false);
+    // dF^T = G^T W: A = G MN-major (SBO 2048 between channel blocks, LBO 128 between pixel groups),
+    //               B = W MN-major (SBO 2048 between entry blocks, LBO 128 between pixel groups).
+    static constexpr uint32_t IDESC_DF = tc::idesc_bf16(128, KC, true, true);
+    static_assert(CK == 32 || CK == 64 || CK == 128, "unsupported slice");
+};
+
+// (a, b) -> bf16x2 hi and lo with a in the low half: a = hi.x + lo.x + O(2^-17 a).
+__device__ __forceinline__ void split_bf16(float a, float b, uint32_t& hi, uint32_t& lo) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    float2 hf = __bfloat1622float2(h);
+    __nv_bfloat162 l = __floats2bfloat162_rn(__fsub_rn(a, hf.x), __fsub_rn(b, hf.y));
+    hi = *reinterpret_cast<uint32_t*>(&h);
+    lo = *reinterpret_cast<uint32_t*>(&l);
 }
 
-// Sums V values over the warp, scattered: afterwards lane l holds the total of value l * V / 32
-// (for V = 32 that is value l).  V is a power of two <= 32.
-template <int V>
-__device__ __forceinline__ float reduce_scatter(float* v, int lane) {
-    int n = V;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        if (n > 1) {
-            const bool hi = lane & o;
-#pragma unroll
-            for (int i = 0; i < V / 2; i++) {
-                if (i < n / 2) {
-                    float send = hi ? v[i] : v[i + n / 2];
-                    float keep = hi ? v[i + n / 2] : v[i];
-                    v[i] = keep + __shfl_xor_sync(FULL_MASK, send, o);
-                }
-            }
-            n >>= 1;
-        } else {
-            v[0] += __shfl_xor_sync(FULL_MASK, v[0], o);
-        }
-    }
-    return v[0];
+__device__ __forceinline__ void st_shared_v2(uint32_t addr, uint32_t a, uint32_t b) {
+    asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
+}
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 
-template <int W>
-__global__ void __launch_bounds__(BWD_THREADS, 1) feature_backward_kernel(
-    int D, int width, int height, int tiles_x, const int2* __restrict__ ranges, const int32_t* __restrict__ values,
-    const float2* __restrict__ means2D, const float4* __restrict__ conic4, const float4* __restrict__ color_opacity,
-    const float* __restrict__ features, const float* __restrict__ final_T_in, const int32_t* __restrict__ n_contrib,
-    const float* __restrict__ grad_out, float* __restrict__ grad_means2D, float* __restrict__ grad_conics,
-    float* __restrict__ grad_features, float* __restrict__ grad_opacities) {
-    constexpr int CPL = W / 32;
-    const int slices = D / W;
-    extern __shared__ float4 s_feat4[];
-    __shared__ int s_id[BWD_BATCH];
-    __shared__ float2 s_mean[BWD_BATCH];
-    __shared__ float4 s_conic[BWD_BATCH];  // a, b, c, opacity
-    __shared__ float2 s_ext[BWD_BATCH];
-    __shared__ float s_w[BWD_THREADS];
-    __shared__ int s_max_last;
-    const float* s_feat = reinterpret_cast<const float*>(s_feat4);
+// Pixel of block thread p (p < 128): warp p/32 covers an 8 x 4 block of the 16 x 8 half tile.
+__device__ __forceinline__ int2 half_tile_pixel(int p) {
+    return make_int2(((p >> 5) & 1) * 8 + (p & 7), (p >> 6) * 4 + ((p & 31) >> 3));
+}
+
+// One stage's list entries, in walk order (descending list position).
+struct BwdChunk {
+    int id[KC];
+    int pos[KC];
+    float2 mean[KC];
+    float2 ext[KC];
+    float4 conic[KC];  // a, b, c, opacity
+    int count;
+};
+
+template <int CK>
+__global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
+    int C, int width, int height, int tiles_x, int slices, const int2* __restrict__ ranges,
+    const int32_t* __restrict__ values, const float2* __restrict__ means2D, const float4* __restrict__ conic4,
+    const float4* __restrict__ color_opacity, const float* __restrict__ features, const float* __restrict__ final_T_in,
+    const int32_t* __restrict__ n_contrib, const float* __restrict__ grad_out, float* __restrict__ grad_means2D,
+    float* __restrict__ grad_conics, float* __restrict__ grad_features, float* __restrict__ grad_opacities) {
+    using Cfg = BwdCfg<CK>;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ BwdChunk s_list[LIST_SLOTS];
+    __shared__ uint64_t s_ready[STAGES], s_dot_full[STAGES], s_walk_done[STAGES], s_df_full[STAGES];
+    __shared__ uint64_t s_list_full[LIST_SLOTS], s_list_free[LIST_SLOTS];
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_fail;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int tile = blockIdx.x / slices;
-    const int c0 = (blockIdx.x % slices) * W;
-    const int x0 = (tile % tiles_x) * TILE, y0 = (tile / tiles_x) * TILE;
-    const int2 lp = warp_pixel(warp, lane);
-    const int px = x0 + lp.x, py = y0 + lp.y;
-    const bool inside = px < width && py < height;
-    const float cx = (float)px + 0.5f, cy = (float)py + 0.5f;
-    const int p = py * width + px;
-    // The warp's pixel-centre rectangle: lane 0 is its top-left pixel, lane 31 its bottom-right.
-    const float rx0 = (float)(x0 + (warp & 1) * 8) + 0.5f, rx1 = rx0 + 7.0f;
-    const float ry0 = (float)(y0 + (warp >> 1) * 4) + 0.5f, ry1 = ry0 + 3.0f;
+    const int slice = blockIdx.x % slices;
+    const int half_id = blockIdx.x / slices;
+    const int tile = half_id >> 1;
+    const int c0 = slice * CK;
+    const int x0 = (tile % tiles_x) * TILE;
+    const int y0 = (tile / tiles_x) * TILE + (half_id & 1) * 8;
+    if (y0 >= height) return;  // the lower half of a bottom-row tile can lie wholly outside the image
 
-    float grad[CPL][32];
-#pragma unroll
-    for (int q = 0; q < 32; q++) {
-        int2 qp = warp_pixel(warp, q);
-        int x = x0 + qp.x, y = y0 + qp.y;
-        bool in = x < width && y < height;
-#pragma unroll
-        for (int i = 0; i < CPL; i++)
-            grad[i][q] = in ? grad_out[(size_t)D * (y * width + x) + c0 + lane + 32 * i] : 0.0f;
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t g_hi = tc::smem_addr(smem), g_lo = g_hi + G_BYTES;
+    const uint32_t stage0 = g_hi + 2 * G_BYTES;
+    // Stage s: F hi, F lo, W hi, W lo.
+    auto f_hi = [&](int s) { return stage0 + s * Cfg::STAGE_BYTES; };
+    auto w_hi = [&](int s) { return stage0 + s * Cfg::STAGE_BYTES + 2 * Cfg::F_BYTES; };
+    auto u_base = [&](int s) { return stage0 + s * Cfg::STAGE_BYTES + 2 * Cfg::F_BYTES + 2 * W_BYTES; };
+
+    if (warp == 0) tc::tmem_alloc(&s_tmem, TMEM_COLS);
+    if (tid == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            tc::mbar_init(&s_ready[s], 1);
+            tc::mbar_init(&s_dot_full[s], 1);
+            tc::mbar_init(&s_walk_done[s], 1);
+            tc::mbar_init(&s_df_full[s], 1);
+        }
+        for (int l = 0; l < LIST_SLOTS; l++) {
+            tc::mbar_init(&s_list_full[l], 1);
+            tc::mbar_init(&s_list_free[l], 1);
+        }
+        tc::fence_mbar_init();
+        s_fail = 0;
     }
-    float T = inside ? final_T_in[p] : 0.0f;
-    const int last = inside ? n_contrib[p] : 0;
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = s_tmem;
     const int2 range = ranges[tile];
-    if (tid == 0) s_max_last = 0;
-    __syncthreads();
-    atomicMax(&s_max_last, last);
-    __syncthreads();
-    const int todo = min(range.y - range.x, s_max_last);
 
-    float behind = 0.0f;
-    for (int end = todo; end > 0; end -= BWD_BATCH) {
-        const int n = min(BWD_BATCH, end);
-        const int start = end - n;
-        __syncthreads();
-        if (tid < n) {
-            int g = values[range.x + start + tid];
-            s_id[tid] = g;
-            s_mean[tid] = means2D[g];
-            float4 q = conic4[g];
-            float o = color_opacity[g].w;
-            s_conic[tid] = make_float4(q.x, q.y, q.z, o);
-            s_ext[tid] = cull_extent(q.x, q.y, q.z, o);
+    if (warp == LIST_WARP) {
+        // ------------------------------------------------------------------ list warp 8
+        // Entries past every pixel's last contributor cannot contribute: start there.
+        int m = 0;
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int2 lp = half_tile_pixel(q * 32 + lane);
+            const int px = x0 + lp.x, py = y0 + lp.y;
+            if (px < width && py < height) m = max(m, n_contrib[(size_t)py * width + px]);
         }
-        __syncthreads();
-        for (int i = tid; i < n * (W / 4); i += BWD_THREADS) {
-            int slot = i / (W / 4);
-            s_feat4[i] = reinterpret_cast<const float4*>(features + (size_t)s_id[slot] * D + c0)[i % (W / 4)];
-        }
-        __syncthreads();
-
-        for (int group = ((n - 1) >> 5) << 5; group >= 0; group -= 32) {
-            const int cand = group + lane;
-            bool hit = false;
-            if (cand < n) {
-                float2 m = s_mean[cand];
-                float2 e = s_ext[cand];
-                hit = box_hits(m, e, rx0, rx1, ry0, ry1);
+        int end = min(range.y - range.x, __reduce_max_sync(FULL_MASK, m));
+        const float hx0 = (float)x0 + 0.5f, hx1 = hx0 + 15.0f, hy0 = (float)y0 + 0.5f, hy1 = hy0 + 7.0f;
+        for (int c = 0;; c++) {
+            const int slot = c % LIST_SLOTS;
+            BwdChunk& ch = s_list[slot];
+            if (c >= LIST_SLOTS) {  // the slot's previous chunk must be drained
+                bool ok = true;
+                if (lane == 0) {
+                    ok = !*(volatile int*)&s_fail &&
+                         tc::mbar_wait_bounded(&s_list_free[slot], ((c - LIST_SLOTS) / LIST_SLOTS) & 1, WAIT_LIMIT);
+                    if (!ok) s_fail = 1;
+                }
+                if (!__shfl_sync(FULL_MASK, ok, 0)) break;
             }
-            unsigned mask = __ballot_sync(FULL_MASK, hit);
-            while (mask) {
-                const int bit = 31 - __clz(mask);
-                mask &= ~(1u << bit);
-                const int slot = group + bit;
-                const float4 q = s_conic[slot];
-                bool contributes = inside && start + slot < last;
-                PairAlpha pa{0.0f, 0.0f, 0.0f, 0.0f};
-                float alpha = 0.0f;
-                if (contributes) {
-                    float2 m = s_mean[slot];
-                    pa = pair_alpha(cx, cy, m.x, m.y, q.x, q.y, q.z, q.w);
-                    alpha = fminf(MAX_ALPHA, pa.raw);
-                    contributes = alpha >= MIN_ALPHA;
-                }
-                if (!__any_sync(FULL_MASK, contributes)) continue;
-
-                float f[CPL];
+            // Select the next entries (back to front) whose box meets the half tile; two batches of
+            // 32 candidates per round trip to memory.
+            int filled = 0;
+            while (filled < KC && end > 0) {
+                int g[2];
+                float2 mm[2], e2[2];
+                float4 q[2];
+                bool hit[2];
 #pragma unroll
-                for (int i = 0; i < CPL; i++) f[i] = s_feat[slot * W + lane + 32 * i];
-                float part[32];
-#pragma unroll
-                for (int qq = 0; qq < 32; qq++) {
-                    float acc = 0.0f;
-#pragma unroll
-                    for (int i = 0; i < CPL; i++) acc = fmaf(f[i], grad[i][qq], acc);
-                    part[qq] = acc;
-                }
-                const float dot = reduce_scatter<32>(part, lane);
-
-                float weight = 0.0f, dL_dalpha = 0.0f;
-                if (contributes) {
-                    T = T / (1.0f - alpha);
-                    weight = T * alpha;
-                    dL_dalpha = T * (dot - behind);
-                    behind = alpha * dot + (1.0f - alpha) * behind;
-                }
-                float v[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
-                if (contributes && pa.raw <= MAX_ALPHA) {
-                    const float dG = q.w * dL_dalpha * pa.G;
-                    v[0] = pa.G * dL_dalpha;
-                    v[1] = dG * (q.x * pa.dx + q.y * pa.dy);
-                    v[2] = dG * (q.y * pa.dx + q.z * pa.dy);
-                    v[3] = dG * (-0.5f * pa.dx * pa.dx);
-                    v[4] = dG * (-pa.dx * pa.dy);
-                    v[5] = dG * (-0.5f * pa.dy * pa.dy);
-                }
-                const float total = reduce_scatter<8>(v, lane);
-                const int g = s_id[slot];
-                if ((lane & 3) == 0) {
-                    const int k = lane >> 2;
-                    if (k < 6 && total != 0.0f) {
-                        float* dst = k == 0 ? grad_opacities + g : k < 3 ? grad_means2D + 2 * g + (k - 1)
-                                                                         : grad_conics + 3 * g + (k - 3);
-                        atomicAdd(dst, total);
+                for (int b = 0; b < 2; b++) {
+                    const int pos = end - 1 - 32 * b - lane;
+                    hit[b] = false;
+                    g[b] = 0;
+                    mm[b] = e2[b] = make_float2(0.0f, 0.0f);
+                    q[b] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    if (pos >= 0) {
+                        g[b] = values[range.x + pos];
+                        mm[b] = means2D[g[b]];
+                        const float4 cq = conic4[g[b]];
+                        q[b] = make_float4(cq.x, cq.y, cq.z, color_opacity[g[b]].w);
+                        e2[b] = cull_extent(q[b].x, q[b].y, q[b].z, q[b].w);
+                        hit[b] = box_hits(mm[b], e2[b], hx0, hx1, hy0, hy1);
                     }
                 }
-                s_w[tid] = weight;
-                __syncwarp();
-                float df[CPL];
 #pragma unroll
-                for (int i = 0; i < CPL; i++) df[i] = 0.0f;
-#pragma unroll
-                for (int qq = 0; qq < 32; qq++) {
-                    const float wq = s_w[warp * 32 + qq];
-#pragma unroll
-                    for (int i = 0; i < CPL; i++) df[i] = fmaf(wq, grad[i][qq], df[i]);
+                for (int b = 0; b < 2; b++) {
+                    if (filled == KC || end <= 0) break;
+                    const unsigned mask = __ballot_sync(FULL_MASK, hit[b]);
+                    const int hits = __popc(mask);
+                    const int take = min(hits, KC - filled);
+                    const int rank = __popc(mask & ((1u << lane) - 1u));
+                    if (hit[b] && rank < take) {
+                        const int k = filled + rank;
+                        ch.id[k] = g[b];
+                        ch.pos[k] = end - 1 - lane;
+                        ch.mean[k] = mm[b];
+                        ch.ext[k] = e2[b];
+                        ch.conic[k] = q[b];
+                    }
+                    // When the chunk fills mid-batch, resume just below the last entry taken.
+                    end = take < hits ? end - 1 - nth_set_bit(mask, take - 1) : end - 32;
+                    filled += take;
                 }
-                __syncwarp();
+                end = max(end, 0);
+            }
+            if (lane == 0) ch.count = filled;
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&s_list_full[slot]);
+            if (filled == 0) break;  // the empty chunk ends the list
+        }
+    } else if (warp >= OPERAND_WARP0) {
+        // ------------------------------------------------------------------ operand warps 9-12
+        const int otid = tid - OPERAND_WARP0 * 32, ow = otid >> 5;
+        const int q4 = warp & 3;                                   // TMEM subpartition of this warp
+        const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;      // its lanes (channels of dF^T)
+
+        // Stage G (dL/dout of the half tile and slice) as bf16 hi + lo.  Each warp instruction
+        // reads 8 pixels x 64 contiguous bytes and writes two 128-byte runs of shared memory.
+#pragma unroll 1
+        for (int pp = 0; pp < 4; pp++) {
 #pragma unroll
-                for (int i = 0; i < CPL; i++)
-                    if (df[i] != 0.0f) atomicAdd(grad_features + (size_t)g * D + c0 + lane + 32 * i, df[i]);
+            for (int j = 0; j < CK / 16; j++) {
+                const int p = pp * 32 + ow * 8 + (lane >> 2);
+                const int c4 = j * 4 + (lane & 3);
+                const int2 lp = half_tile_pixel(p);
+                const int px = x0 + lp.x, py = y0 + lp.y;
+                float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (px < width && py < height)
+                    v = __ldg(reinterpret_cast<const float4*>(grad_out + ((size_t)py * width + px) * C + c0) + c4);
+                uint32_t h0, l0, h1, l1;
+                split_bf16(v.x, v.y, h0, l0);
+                split_bf16(v.z, v.w, h1, l1);
+                const uint32_t off = (c4 >> 1) * 2048 + p * 16 + (c4 & 1) * 8;
+                st_shared_v2(g_hi + off, h0, h1);
+                st_shared_v2(g_lo + off, l0, l1);
             }
         }
+        // The dF MMA reads 128 channel rows of G: zero the rows past the slice.
+        for (int i = CK * 16 + otid; i < G_BYTES / 16; i += 128) {  // channel blocks CK/8.. are 2048 B each
+            st_shared_v4(g_hi + i * 16, 0u, 0u, 0u, 0u);
+            st_shared_v4(g_lo + i * 16, 0u, 0u, 0u, 0u);
+        }
+
+        int n_real = -1;  // number of non-empty chunks, known once the empty chunk arrives
+        int dot_committed = 0;
+        for (int c = 0;; c++) {
+            if (n_real >= 0 && c - STAGES >= n_real) break;  // every chunk is drained
+            const int s = c % STAGES, slot = c % LIST_SLOTS;
+            const bool fresh = n_real < 0;
+            int cnt = 0;
+            float4 fv[CK / 16];
+            if (fresh) {
+                bool bad = false;
+                if (otid == 0) {
+                    bad = *(volatile int*)&s_fail ||
+                          !tc::mbar_wait_bounded(&s_list_full[slot], (c / LIST_SLOTS) & 1, WAIT_LIMIT);
+                    if (bad) s_fail = 1;
+                }
+                if (tc::group_sync_count(OPERAND_BAR, bad) != 0) break;
+                cnt = s_list[slot].count;
+                // Issue chunk c's feature loads now; they land while chunk c - STAGES is drained.
+                const int k = ow * 8 + (lane >> 2);
+                const float4* row =
+                    reinterpret_cast<const float4*>(features + (size_t)(k < cnt ? s_list[slot].id[k] : 0) * C + c0);
+#pragma unroll
+                for (int j = 0; j < CK / 16; j++)
+                    fv[j] = k < cnt ? __ldg(row + j * 4 + (lane & 3)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+            if (c >= STAGES) {
+                // Drain chunk e = c - STAGES (stage s, list slot e % LIST_SLOTS).
+                const int e = c - STAGES;
+                const BwdChunk& ce = s_list[e % LIST_SLOTS];
+                const uint32_t par = (e / STAGES) & 1;
+                bool bad = false;
+                if (otid == 0) {
+                    bad = *(volatile int*)&s_fail || !tc::mbar_wait_bounded(&s_walk_done[s], par, WAIT_LIMIT);
+                    if (bad) s_fail = 1;
+                }
+                if (tc::group_sync_count(OPERAND_BAR, bad) != 0) break;
+                const int ecnt = ce.count;
+                // Geometric gradients of entry k = lane over the pixels of pixel warp q4 (an 8 x 4
+                // block): with u = dL/dalpha * G they are linear in sum u {1, dx, dy, dx^2, dx dy, dy^2}.
+                if (lane < ecnt) {
+                    const float2 m = ce.mean[lane];
+                    const float4 q = ce.conic[lane];
+                    const float bx = (float)(x0 + (q4 & 1) * 8) + 0.5f, by = (float)(y0 + (q4 >> 1) * 4) + 0.5f;
+                    const uint8_t* ub = smem + (u_base(s) - g_hi) + (lane >> 2) * U_QUAD_STRIDE + (lane & 3) * 4 +
+                                        q4 * 32 * 16;
+                    float m0 = 0.0f, mx = 0.0f, my = 0.0f, mxx = 0.0f, mxy = 0.0f, myy = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < 32; i++) {
+                        const float u = *reinterpret_cast<const float*>(ub + i * 16);
+                        const float dx = __fsub_rn(bx + (float)(i & 7), m.x), dy = __fsub_rn(by + (float)(i >> 3), m.y);
+                        const float ux = u * dx, uy = u * dy;
+                        m0 += u;
+                        mx += ux;
+                        my += uy;
+                        mxx = fmaf(ux, dx, mxx);
+                        mxy = fmaf(ux, dy, mxy);
+                        myy = fmaf(uy, dy, myy);
+                    }
+                    const int g = ce.id[lane];
+                    const float o = q.w;
+                    const float v[6] = {m0, o * fmaf(q.y, my, q.x * mx), o * fmaf(q.z, my, q.y * mx), -0.5f * o * mxx,
+                                        -o * mxy, -0.5f * o * myy};
+                    if (v[0] != 0.0f) atomicAdd(grad_opacities + g, v[0]);
+                    if (v[1] != 0.0f) atomicAdd(grad_means2D + 2 * g, v[1]);
+                    if (v[2] != 0.0f) atomicAdd(grad_means2D + 2 * g + 1, v[2]);
+                    if (v[3] != 0.0f) atomicAdd(grad_conics + 3 * g, v[3]);
+                    if (v[4] != 0.0f) atomicAdd(grad_conics + 3 * g + 1, v[4]);
+                    if (v[5] != 0.0f) atomicAdd(grad_conics + 3 * g + 2, v[5]);
+                }
+                // dF of the chunk: wait for its MMA, then drain TMEM (lane = channel).
+                if (otid == 0) {
+                    bad = *(volatile int*)&s_fail || !tc::mbar_wait_bounded(&s_df_full[s], par, WAIT_LIMIT);
+                    if (bad) s_fail = 1;
+                }
+                if (tc::group_sync_count(OPERAND_BAR, bad) != 0) break;
+                tc::fence_after_sync();
+                float v[32];
+                tc::tmem_ld32(tmem + lane_base + 128 + s * 32, v);
+                tc::fence_before_sync();
+                // Transpose dF^T (lane = channel) through stage s's feature buffer -- free, its dot MMA
+                // has completed -- into rows of the entry, then add them with float4 atomics.
+                uint8_t* tr = smem + (f_hi(s) - g_hi);
+                const int cl = q4 * 32 + lane;
+                if (cl < CK) {
+#pragma unroll
+                    for (int k = 0; k < KC; k++)
+                        if (k < ecnt) *reinterpret_cast<float*>(tr + (k * CK + cl) * 4) = v[k];
+                }
+                tc::group_sync(OPERAND_BAR);
+                for (int i = otid; i < ecnt * (CK / 4); i += 128) {
+                    const int k = i / (CK / 4), c4 = i % (CK / 4);
+                    const float4 d = *reinterpret_cast<const float4*>(tr + (k * CK + 4 * c4) * 4);
+                    if (d.x != 0.0f || d.y != 0.0f || d.z != 0.0f || d.w != 0.0f)
+                        atomicAdd(reinterpret_cast<float4*>(grad_features + (size_t)ce.id[k] * C + c0) + c4, d);
+                }
+                tc::group_sync(OPERAND_BAR);
+                if (otid == 0) tc::mbar_arrive(&s_list_free[e % LIST_SLOTS]);
+            }
+            if (!fresh) continue;
+            if (cnt > 0) {
+                // Chunk c's features as bf16 hi + lo (zeros past cnt).  Stage s is free: the pixels
+                // finished chunk c - STAGES, so its dot MMA has completed.
+                const int k = ow * 8 + (lane >> 2);
+                const uint32_t fh = f_hi(s), fl = fh + Cfg::F_BYTES;
+#pragma unroll
+                for (int j = 0; j < CK / 16; j++) {
+                    const int c4 = j * 4 + (lane & 3);
+                    uint32_t h0, l0, h1, l1;
+                    split_bf16(fv[j].x, fv[j].y, h0, l0);
+                    split_bf16(fv[j].z, fv[j].w, h1, l1);
+                    const uint32_t off = (c4 >> 1) * Cfg::F_LBO + k * 16 + (c4 & 1) * 8;
+                    st_shared_v2(fh + off, h0, h1);
+                    st_shared_v2(fl + off, l0, l1);
+                }
+            }
+            tc::fence_proxy_async();
+            tc::group_sync(OPERAND_BAR);
+            if (otid == 0) {
+                if (cnt > 0) {
+                    tc::fence_after_sync();
+                    const uint32_t fh = f_hi(s), fl = fh + Cfg::F_BYTES;
+#pragma unroll
+                    for (int ks = 0; ks < CK / 16; ks++) {
+                        const uint64_t ah = tc::smem_desc(g_hi + ks * 4096, 2048, 128);
+                        const uint64_t al = tc::smem_desc(g_lo + ks * 4096, 2048, 128);
+                        const uint64_t bh = tc::smem_desc(fh + ks * 2 * Cfg::F_LBO, Cfg::F_LBO, 128);
+                        const uint64_t bl = tc::smem_desc(fl + ks * 2 * Cfg::F_LBO, Cfg::F_LBO, 128);
+                        const uint32_t d = tmem + s * 32;
+                        tc::mma_bf16(d, ah, bh, Cfg::IDESC_DOT, ks > 0 ? 1u : 0u);
+                        tc::mma_bf16(d, ah, bl, Cfg::IDESC_DOT, 1u);
+                        tc::mma_bf16(d, al, bh, Cfg::IDESC_DOT, 1u);
+                    }
+                    tc::commit(&s_dot_full[s]);
+                    dot_committed = c + 1;
+                }
+                tc::mbar_arrive(&s_ready[s]);
+            }
+            if (cnt == 0) n_real = c;
+        }
+        // Every dot MMA this thread issued has finished before TMEM is freed.
+        if (otid == 0 && dot_committed > 0 &&
+            !tc::mbar_wait_bounded(&s_dot_full[(dot_committed - 1) % STAGES], ((dot_committed - 1) / STAGES) & 1,
+                                   WAIT_LIMIT))
+            s_fail = 1;
+    } else {
+        // ------------------------------------------------------------------ pixel warps 0-7
+        // Two threads per pixel: warp w covers 16 pixels of TMEM lane quadrant w & 3 (an 8 x 2
+        // block); thread t < 16 and its partner t + 16 share pixel t, and each computes the alphas
+        // of half of every group of eight entries (role 0: entries 0-3, role 1: entries 4-7).
+        const int quad = warp & 3, half16 = warp >> 2, role = lane >> 4;
+        const int p = quad * 32 + half16 * 16 + (lane & 15);
+        const int2 lp = half_tile_pixel(p);
+        const int px = x0 + lp.x, py = y0 + lp.y;
+        const bool inside = px < width && py < height;
+        const float cx = (float)px + 0.5f, cy = (float)py + 0.5f;
+        const float wx0 = (float)(x0 + (quad & 1) * 8) + 0.5f, wx1 = wx0 + 7.0f;
+        const float wy0 = (float)(y0 + (quad >> 1) * 4 + half16 * 2) + 0.5f, wy1 = wy0 + 1.0f;
+        const size_t pix = (size_t)py * width + px;
+        float T = inside ? final_T_in[pix] : 0.0f;
+        const int last = inside ? n_contrib[pix] : 0;
+        float behind = 0.0f;
+        const uint32_t lane_base = (uint32_t)(quad * 32 + half16 * 16) << 16;
+        int df_committed = 0;
+
+        for (int c = 0;; c++) {
+            const int s = c % STAGES;
+            const BwdChunk& ch = s_list[c % LIST_SLOTS];
+            const uint32_t par = (c / STAGES) & 1;
+            bool bad = false;
+            if (tid == 0) {
+                bad = *(volatile int*)&s_fail;
+                if (!bad && !tc::mbar_wait_bounded(&s_ready[s], par, WAIT_LIMIT)) bad = true;
+                if (!bad && ch.count > 0 && !tc::mbar_wait_bounded(&s_dot_full[s], par, WAIT_LIMIT)) bad = true;
+                if (bad) s_fail = 1;
+            }
+            if (tc::group_sync_count(PIXEL_BAR, bad, PIXEL_THREADS) != 0) break;
+            const int cnt = ch.count;
+            if (cnt == 0) break;
+            tc::fence_after_sync();
+
+            // Groups of eight entries, in a rolled loop so one group body is all the code the walk
+            // needs.  The walk is branch-free: an entry that does not contribute gets alpha 0, for
+            // which the recurrence is the identity (T / 1, w = 0, behind kept).  Each thread computes
+            // alpha, 1 / (1 - alpha) and G for its four entries; the pair swaps them with the dots,
+            // and both run the short serial T / behind chain over all eight.  Each thread writes its
+            // half of the group's W block (bf16 hi + lo) and its u quad; the geometric partials
+            // leave as u = dL/dalpha * G, summed by the operand warps.
+            const uint32_t wh = w_hi(s), wl = wh + W_BYTES, ub = u_base(s) + p * 16;
+#pragma unroll 1
+            for (int k0 = 0; k0 < cnt; k0 += 8) {
+                const int kb = k0 + 4 * role;  // this thread's four entries
+                float d_own[4];
+                tc::tmem_ld16x2_4(tmem + lane_base + s * 32 + k0, d_own);
+                bool hit[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    hit[i] = kb + i < cnt && box_hits(ch.mean[kb + i], ch.ext[kb + i], wx0, wx1, wy0, wy1);
+                float w_own[4] = {0.0f, 0.0f, 0.0f, 0.0f}, u_own[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                if (__any_sync(FULL_MASK, hit[0] || hit[1] || hit[2] || hit[3])) {  // uniform per warp
+                    float a_own[4], r_own[4], g_own[4];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float4 q = ch.conic[kb + i];
+                        const float2 m = ch.mean[kb + i];
+                        const PairAlpha pa = pair_alpha(cx, cy, m.x, m.y, q.x, q.y, q.z, q.w);
+                        const float alpha = fminf(MAX_ALPHA, pa.raw);
+                        const bool ok = hit[i] && inside && ch.pos[kb + i] < last && alpha >= MIN_ALPHA;
+                        a_own[i] = ok ? alpha : 0.0f;
+                        r_own[i] = ok ? __fdividef(1.0f, 1.0f - alpha) : 1.0f;
+                        // A clamped alpha no longer depends on the gaussian: nothing flows past it.
+                        g_own[i] = ok && pa.raw <= MAX_ALPHA ? pa.G : 0.0f;
+                    }
+                    // Entries 0-3 come from role 0, entries 4-7 from role 1.
+                    float a8[8], r8[8], d8[8];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float a_p = __shfl_xor_sync(FULL_MASK, a_own[i], 16);
+                        const float r_p = __shfl_xor_sync(FULL_MASK, r_own[i], 16);
+                        const float d_p = __shfl_xor_sync(FULL_MASK, d_own[i], 16);
+                        a8[i] = role ? a_p : a_own[i];
+                        a8[i + 4] = role ? a_own[i] : a_p;
+                        r8[i] = role ? r_p : r_own[i];
+                        r8[i + 4] = role ? r_own[i] : r_p;
+                        d8[i] = role ? d_p : d_own[i];
+                        d8[i + 4] = role ? d_own[i] : d_p;
+                    }
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        T = T * r8[i];
+                        const float dL_dalpha = T * (d8[i] - behind);
+                        if ((i >> 2) == role) {  // this thread's entry: a select, not a branch
+                            w_own[i & 3] = T * a8[i];
+                            u_own[i & 3] = dL_dalpha * g_own[i & 3];
+                        }
+                        behind = fmaf(a8[i], d8[i], (1.0f - a8[i]) * behind);
+                    }
+                }
+                // W block k0/8 as the MN-major B operand: this pixel's 8 weights are one 16-byte run,
+                // of which this thread writes its half.
+                uint32_t h0, l0, h1, l1;
+                split_bf16(w_own[0], w_own[1], h0, l0);
+                split_bf16(w_own[2], w_own[3], h1, l1);
+                st_shared_v2(wh + (k0 >> 3) * 2048 + p * 16 + role * 8, h0, h1);
+                st_shared_v2(wl + (k0 >> 3) * 2048 + p * 16 + role * 8, l0, l1);
+                st_shared_v4(ub + ((k0 >> 2) + role) * U_QUAD_STRIDE, __float_as_uint(u_own[0]),
+                             __float_as_uint(u_own[1]), __float_as_uint(u_own[2]), __float_as_uint(u_own[3]));
+            }
+            tc::fence_proxy_async();
+            tc::fence_before_sync();
+            tc::group_sync(PIXEL_BAR, PIXEL_THREADS);
+            if (tid == 0) {
+                tc::fence_after_sync();
+#pragma unroll
+                for (int ks = 0; ks < PIX / 16; ks++) {
+                    const uint64_t ah = tc::smem_desc(g_hi + ks * 256, 128, 2048);
+                    const uint64_t al = tc::smem_desc(g_lo + ks * 256, 128, 2048);
+                    const uint64_t bh = tc::smem_desc(wh + ks * 256, 128, 2048);
+                    const uint64_t bl = tc::smem_desc(wl + ks * 256, 128, 2048);
+                    const uint32_t d = tmem + 128 + s * 32;
+                    tc::mma_bf16(d, ah, bh, Cfg::IDESC_DF, ks > 0 ? 1u : 0u);
+                    tc::mma_bf16(d, ah, bl, Cfg::IDESC_DF, 1u);
+                    tc::mma_bf16(d, al, bh, Cfg::IDESC_DF, 1u);
+                }
+                tc::commit(&s_df_full[s]);
+                tc::mbar_arrive(&s_walk_done[s]);
+                df_committed = c + 1;
+            }
+        }
+        if (tid == 0 && df_committed > 0 &&
+            !tc::mbar_wait_bounded(&s_df_full[(df_committed - 1) % STAGES], ((df_committed - 1) / STAGES) & 1,
+                                   WAIT_LIMIT))
+            s_fail = 1;
     }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) tc::tmem_dealloc(tmem, TMEM_COLS);
+    if (tid == 0 && s_fail) atomicExch(&g_backward_status, HDS_ERR_DEVICE);
 }
 
-template <int W>
-int launch_backward(int n, int D, int width, int height, const int32_t* tile_ranges, const int32_t* values,
+template <int CK>
+int launch_backward(int D, int width, int height, const int32_t* tile_ranges, const int32_t* values,
                     const float* means2D, const float* conic4, const float* color_opacity, const float* features,
                     const float* final_T, const int32_t* n_contrib, const float* grad_output, float* grad_features,
                     float* grad_means2D, float* grad_conics, float* grad_opacities, cudaStream_t stream) {
-    (void)n;
-    const int smem = BWD_BATCH * W * (int)sizeof(float);
-    auto kernel = feature_backward_kernel<W>;
-    HDS_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    int tx = tiles_for(width), ty = tiles_for(height);
-    kernel<<<tx * ty * (D / W), BWD_THREADS, smem, stream>>>(
-        D, width, height, tx, reinterpret_cast<const int2*>(tile_ranges), values, reinterpret_cast<const float2*>(means2D),
-        reinterpret_cast<const float4*>(conic4), reinterpret_cast<const float4*>(color_opacity), features, final_T,
-        n_contrib, grad_output, grad_means2D, grad_conics, grad_features, grad_opacities);
+    using Cfg = BwdCfg<CK>;
+    auto kernel = feature_backward_kernel<CK>;
+    HDS_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    const int tx = tiles_for(width), ty = tiles_for(height), slices = D / CK;
+    kernel<<<2 * tx * ty * slices, THREADS, Cfg::SMEM, stream>>>(
+        D, width, height, tx, slices, reinterpret_cast<const int2*>(tile_ranges), values,
+        reinterpret_cast<const float2*>(means2D), reinterpret_cast<const float4*>(conic4),
+        reinterpret_cast<const float4*>(color_opacity), features, final_T, n_contrib, grad_output, grad_means2D,
+        grad_conics, grad_features, grad_opacities);
     HDS_CHECK_LAUNCH("feature_backward_kernel");
     return HDS_OK;
 }
 
 }  // namespace
+
+int read_and_clear_backward_status(int* status, cudaStream_t stream) {
+    int zero = 0;
+    HDS_CHECK_CUDA(cudaMemcpyFromSymbolAsync(status, g_backward_status, sizeof(int), 0, cudaMemcpyDeviceToHost, stream));
+    HDS_CHECK_CUDA(cudaMemcpyToSymbolAsync(g_backward_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, stream));
+    return HDS_OK;
+}
+
 }  // namespace hds
 
 using namespace hds;
@@ -244,15 +589,18 @@ extern "C" int hds_render_features_backward(int n, int channels, int slice_width
                            (D == 128 && (Wd == 128 || Wd == 64 || Wd == 32)) || (D == 256 && (Wd == 128 || Wd == 64)) ||
                            (D == 512 && (Wd == 128 || Wd == 64));
     HDS_REQUIRE(supported, HDS_ERR_UNSUPPORTED, "no feature backward for %d channels in slices of %d", D, Wd);
-    HDS_REQUIRE(((uintptr_t)features & 15) == 0, HDS_ERR_INVALID, "rasterize_features_backward: features must be 16-byte aligned");
+    HDS_REQUIRE(((uintptr_t)features & 15) == 0 && ((uintptr_t)grad_output & 15) == 0, HDS_ERR_INVALID,
+                "rasterize_features_backward: features and grad_output must be 16-byte aligned");
     if (n == 0) return HDS_OK;
     HDS_CHECK_CUDA(cudaMemsetAsync(grad_features, 0, sizeof(float) * (size_t)n * D, stream));
     HDS_CHECK_CUDA(cudaMemsetAsync(grad_means2D, 0, sizeof(float) * 2 * (size_t)n, stream));
     HDS_CHECK_CUDA(cudaMemsetAsync(grad_conics, 0, sizeof(float) * 3 * (size_t)n, stream));
     HDS_CHECK_CUDA(cudaMemsetAsync(grad_opacities, 0, sizeof(float) * (size_t)n, stream));
-    switch (Wd) {
-        case 32: return launch_backward<32>(n, D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, stream);
-        case 64: return launch_backward<64>(n, D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, stream);
-        default: return launch_backward<128>(n, D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, stream);
+    // The slice width only selects the reference's kernel instantiation; the sums are the same for
+    // any slicing, and these kernels always take slices of min(channels, 128).
+    switch (D) {
+        case 32: return launch_backward<32>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, stream);
+        case 64: return launch_backward<64>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, stream);
+        default: return launch_backward<128>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, stream);
     }
 }
