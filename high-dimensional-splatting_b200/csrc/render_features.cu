@@ -130,7 +130,7 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
                     s_fail = 1;
                 halt = *(volatile int*)&s_stop || *(volatile int*)&s_fail;
             }
-            const bool stop = tc::group_sync_count(PRODUCER_BAR, halt) != 0 || cursor >= count;
+            const bool stop = tc::group_sync_count<PRODUCER_BAR>(halt) != 0 || cursor >= count;
             if (warp == 4) {
                 int filled = 0, cur = cursor;
                 if (!stop) {
@@ -182,7 +182,7 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
                 tc::mbar_arrive(&s_geo_full[s]);  // every lane, after its own writes
                 cursor = min(cur, count);
             }
-            tc::group_sync(PRODUCER_BAR);  // the chunk's entries (and count) are visible to warps 5-7
+            tc::group_sync<PRODUCER_BAR>();  // the chunk's entries (and count) are visible to warps 5-7
             const int valid = ch.count;
             if (valid == 0) break;
 
@@ -241,7 +241,7 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
                     bad = true;
                 }
             }
-            if (tc::group_sync_count(PIXEL_BAR, bad) != 0) break;
+            if (tc::group_sync_count<PIXEL_BAR>(bad) != 0) break;
             const int valid = ch.count;
             if (valid == 0) break;
 
@@ -285,7 +285,7 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
             }
             tc::fence_proxy_async();
             // Every pixel thread has written its A row; tell the producers when all pixels are done.
-            if (tc::group_sync_count(PIXEL_BAR, done) == 128 && tid == 0) *(volatile int*)&s_stop = 1;
+            if (tc::group_sync_count<PIXEL_BAR>(done) == 128 && tid == 0) *(volatile int*)&s_stop = 1;
             if (tid == 0) {
                 if (!tc::mbar_wait_bounded(&s_b_full[s], (c / STAGES) & 1, WAIT_LIMIT)) {
                     s_fail = 1;
@@ -319,7 +319,7 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
             ok = ok && !*(volatile int*)&s_fail;
         }
         // Uniform across the group: it decides whether the warp-collective tcgen05.ld runs.
-        const bool have = tc::group_sync_count(PIXEL_BAR, ok) != 0;
+        const bool have = tc::group_sync_count<PIXEL_BAR>(ok) != 0;
         tc::fence_after_sync();
         const size_t p = (size_t)py * width + px;
         float* dst = feature_image + p * C;

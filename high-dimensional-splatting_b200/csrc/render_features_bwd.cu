@@ -40,13 +40,24 @@ __device__ int g_backward_status = 0;
 namespace {
 
 constexpr uint32_t WAIT_LIMIT = 1u << 22;
-constexpr int STAGES = 3;
+constexpr int STAGES = 4;
 constexpr int KC = 32;      // list entries per chunk (the N of both MMAs)
 constexpr int PIX = 128;    // pixels per block
 constexpr int MAX_CK = 128; // channels per block (the M of the dF MMA)
 constexpr int LIST_SLOTS = 6;  // list ring: the list warp runs up to three chunks past the operand stages
-constexpr int THREADS = 416;   // pixel warps 0-7, list warp 8, operand warps 9-12
-constexpr int PIXEL_THREADS = 256, LIST_WARP = 8, OPERAND_WARP0 = 9;
+// Warp roles: pixel warps 0-7, list warp 8, operand warps 9-12, MMA warp 13.
+constexpr int PIXEL_WARPS = 8, LIST_WARP = 8, OPERAND_WARP0 = 9, OPERAND_WARPS = 4, MMA_WARP = 13;
+constexpr int THREADS = (MMA_WARP + 1) * 32, PIXEL_THREADS = PIXEL_WARPS * 32;
+static_assert(LIST_WARP == PIXEL_WARPS && OPERAND_WARP0 == LIST_WARP + 1 &&
+                  MMA_WARP == OPERAND_WARP0 + OPERAND_WARPS,
+              "warp roles must partition the block");
+enum class Role { Pixel, List, Operand, Mma };
+__device__ __forceinline__ Role role_of(int warp) {
+    return warp < PIXEL_WARPS ? Role::Pixel
+           : warp == LIST_WARP ? Role::List
+           : warp < OPERAND_WARP0 + OPERAND_WARPS ? Role::Operand
+                                                   : Role::Mma;
+}
 constexpr int PIXEL_BAR = 1, OPERAND_BAR = 2;
 constexpr int G_BYTES = PIX * MAX_CK * 2;  // one bf16 copy of G: [c/8][p][c%8]
 constexpr int W_BYTES = PIX * KC * 2;      // one bf16 copy of W: [k/8][p][k%8]
@@ -59,7 +70,12 @@ constexpr uint32_t TMEM_COLS = 256;        // dots at s*32, dF^T at 128 + s*32
 template <int CK>
 struct BwdCfg {
     static constexpr int F_BYTES = KC * CK * 2;  // one bf16 copy of a chunk's features: [c/8][k][c%8]
-    static constexpr int STAGE_BYTES = 2 * F_BYTES + 2 * W_BYTES + U_BYTES;
+    // A chunk's features are dead once its dot MMA has run and its weights are written only after
+    // that, so F and W share one buffer per stage; once the dF MMA has read W, the buffer also
+    // holds the dF transpose ([k][c] fp32, KC * CK * 4 bytes).
+    static constexpr int FW_BYTES = F_BYTES > W_BYTES ? 2 * F_BYTES : 2 * W_BYTES;
+    static_assert(KC * CK * 4 <= FW_BYTES, "dF transpose must fit the stage buffer");
+    static constexpr int STAGE_BYTES = FW_BYTES + U_BYTES;
     static constexpr int SMEM = 2 * G_BYTES + STAGES * STAGE_BYTES + 1024;
     static constexpr int F_LBO = (KC / 8) * 128;  // 512: between 8-channel blocks of F
     // dot = G F^T: A = G K-major (SBO 128 between pixel groups, LBO 2048 between channel blocks),
@@ -131,8 +147,8 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
     const uint32_t stage0 = g_hi + 2 * G_BYTES;
     // Stage s: F hi, F lo, W hi, W lo.
     auto f_hi = [&](int s) { return stage0 + s * Cfg::STAGE_BYTES; };
-    auto w_hi = [&](int s) { return stage0 + s * Cfg::STAGE_BYTES + 2 * Cfg::F_BYTES; };
-    auto u_base = [&](int s) { return stage0 + s * Cfg::STAGE_BYTES + 2 * Cfg::F_BYTES + 2 * W_BYTES; };
+    auto w_hi = [&](int s) { return stage0 + s * Cfg::STAGE_BYTES; };
+    auto u_base = [&](int s) { return stage0 + s * Cfg::STAGE_BYTES + Cfg::FW_BYTES; };
 
     if (warp == 0) tc::tmem_alloc(&s_tmem, TMEM_COLS);
     if (tid == 0) {
@@ -155,7 +171,8 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
     const uint32_t tmem = s_tmem;
     const int2 range = ranges[tile];
 
-    if (warp == LIST_WARP) {
+    const Role role = role_of(warp);
+    if (role == Role::List) {
         // ------------------------------------------------------------------ list warp 8
         // Entries past every pixel's last contributor cannot contribute: start there.
         int m = 0;
@@ -229,7 +246,7 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
             if (lane == 0) tc::mbar_arrive(&s_list_full[slot]);
             if (filled == 0) break;  // the empty chunk ends the list
         }
-    } else if (warp >= OPERAND_WARP0) {
+    } else if (role == Role::Operand) {
         // ------------------------------------------------------------------ operand warps 9-12
         const int otid = tid - OPERAND_WARP0 * 32, ow = otid >> 5;
         const int q4 = warp & 3;                                   // TMEM subpartition of this warp
@@ -263,7 +280,6 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
         }
 
         int n_real = -1;  // number of non-empty chunks, known once the empty chunk arrives
-        int dot_committed = 0;
         for (int c = 0;; c++) {
             if (n_real >= 0 && c - STAGES >= n_real) break;  // every chunk is drained
             const int s = c % STAGES, slot = c % LIST_SLOTS;
@@ -277,7 +293,7 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
                           !tc::mbar_wait_bounded(&s_list_full[slot], (c / LIST_SLOTS) & 1, WAIT_LIMIT);
                     if (bad) s_fail = 1;
                 }
-                if (tc::group_sync_count(OPERAND_BAR, bad) != 0) break;
+                if (tc::group_sync_count<OPERAND_BAR>(bad) != 0) break;
                 cnt = s_list[slot].count;
                 // Issue chunk c's feature loads now; they land while chunk c - STAGES is drained.
                 const int k = ow * 8 + (lane >> 2);
@@ -297,7 +313,7 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
                     bad = *(volatile int*)&s_fail || !tc::mbar_wait_bounded(&s_walk_done[s], par, WAIT_LIMIT);
                     if (bad) s_fail = 1;
                 }
-                if (tc::group_sync_count(OPERAND_BAR, bad) != 0) break;
+                if (tc::group_sync_count<OPERAND_BAR>(bad) != 0) break;
                 const int ecnt = ce.count;
                 // Geometric gradients of entry k = lane over the pixels of pixel warp q4 (an 8 x 4
                 // block): with u = dL/dalpha * G they are linear in sum u {1, dx, dy, dx^2, dx dy, dy^2}.
@@ -336,7 +352,7 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
                     bad = *(volatile int*)&s_fail || !tc::mbar_wait_bounded(&s_df_full[s], par, WAIT_LIMIT);
                     if (bad) s_fail = 1;
                 }
-                if (tc::group_sync_count(OPERAND_BAR, bad) != 0) break;
+                if (tc::group_sync_count<OPERAND_BAR>(bad) != 0) break;
                 tc::fence_after_sync();
                 float v[32];
                 tc::tmem_ld32(tmem + lane_base + 128 + s * 32, v);
@@ -350,14 +366,14 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
                     for (int k = 0; k < KC; k++)
                         if (k < ecnt) *reinterpret_cast<float*>(tr + (k * CK + cl) * 4) = v[k];
                 }
-                tc::group_sync(OPERAND_BAR);
+                tc::group_sync<OPERAND_BAR>();
                 for (int i = otid; i < ecnt * (CK / 4); i += 128) {
                     const int k = i / (CK / 4), c4 = i % (CK / 4);
                     const float4 d = *reinterpret_cast<const float4*>(tr + (k * CK + 4 * c4) * 4);
                     if (d.x != 0.0f || d.y != 0.0f || d.z != 0.0f || d.w != 0.0f)
                         atomicAdd(reinterpret_cast<float4*>(grad_features + (size_t)ce.id[k] * C + c0) + c4, d);
                 }
-                tc::group_sync(OPERAND_BAR);
+                tc::group_sync<OPERAND_BAR>();
                 if (otid == 0) tc::mbar_arrive(&s_list_free[e % LIST_SLOTS]);
             }
             if (!fresh) continue;
@@ -378,40 +394,86 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
                 }
             }
             tc::fence_proxy_async();
-            tc::group_sync(OPERAND_BAR);
-            if (otid == 0) {
-                if (cnt > 0) {
-                    tc::fence_after_sync();
-                    const uint32_t fh = f_hi(s), fl = fh + Cfg::F_BYTES;
-#pragma unroll
-                    for (int ks = 0; ks < CK / 16; ks++) {
-                        const uint64_t ah = tc::smem_desc(g_hi + ks * 4096, 2048, 128);
-                        const uint64_t al = tc::smem_desc(g_lo + ks * 4096, 2048, 128);
-                        const uint64_t bh = tc::smem_desc(fh + ks * 2 * Cfg::F_LBO, Cfg::F_LBO, 128);
-                        const uint64_t bl = tc::smem_desc(fl + ks * 2 * Cfg::F_LBO, Cfg::F_LBO, 128);
-                        const uint32_t d = tmem + s * 32;
-                        tc::mma_bf16(d, ah, bh, Cfg::IDESC_DOT, ks > 0 ? 1u : 0u);
-                        tc::mma_bf16(d, ah, bl, Cfg::IDESC_DOT, 1u);
-                        tc::mma_bf16(d, al, bh, Cfg::IDESC_DOT, 1u);
-                    }
-                    tc::commit(&s_dot_full[s]);
-                    dot_committed = c + 1;
-                }
-                tc::mbar_arrive(&s_ready[s]);
-            }
+            tc::fence_before_sync();
+            tc::group_sync<OPERAND_BAR>();
+            // Chunk c is published: its list, its features, and a stage whose previous chunk is drained.
+            if (otid == 0) tc::mbar_arrive(&s_ready[s]);
             if (cnt == 0) n_real = c;
         }
-        // Every dot MMA this thread issued has finished before TMEM is freed.
-        if (otid == 0 && dot_committed > 0 &&
-            !tc::mbar_wait_bounded(&s_dot_full[(dot_committed - 1) % STAGES], ((dot_committed - 1) / STAGES) & 1,
-                                   WAIT_LIMIT))
-            s_fail = 1;
-    } else {
+    } else if (role == Role::Mma) {
+        // ------------------------------------------------------------------ MMA warp 13 (one lane)
+        // Issues every tensor-core instruction, polling two queues: the dot of the next published
+        // chunk, and the dF of the oldest chunk whose walk is done.
+        if (lane == 0) {
+            int cd = 0, cf = 0, n_end = -1;  // next chunk for dot / dF; the empty chunk's index
+            uint64_t* last_bar = nullptr;    // the most recent commit and its phase parity
+            uint32_t last_par = 0, idle = 0;
+            while (n_end < 0 || cf < n_end) {
+                if (*(volatile int*)&s_fail) break;
+                bool progress = false;
+                if (n_end < 0 && tc::mbar_try_wait(&s_ready[cd % STAGES], (cd / STAGES) & 1)) {
+                    const int s = cd % STAGES;
+                    if (s_list[cd % LIST_SLOTS].count == 0) {
+                        n_end = cd;
+                    } else {
+                        tc::fence_after_sync();
+                        const uint32_t fh = f_hi(s), fl = fh + Cfg::F_BYTES;
+#pragma unroll
+                        for (int ks = 0; ks < CK / 16; ks++) {
+                            const uint64_t ah = tc::smem_desc(g_hi + ks * 4096, 2048, 128);
+                            const uint64_t al = tc::smem_desc(g_lo + ks * 4096, 2048, 128);
+                            const uint64_t bh = tc::smem_desc(fh + ks * 2 * Cfg::F_LBO, Cfg::F_LBO, 128);
+                            const uint64_t bl = tc::smem_desc(fl + ks * 2 * Cfg::F_LBO, Cfg::F_LBO, 128);
+                            const uint32_t d = tmem + s * 32;
+                            tc::mma_bf16(d, ah, bh, Cfg::IDESC_DOT, ks > 0 ? 1u : 0u);
+                            tc::mma_bf16(d, ah, bl, Cfg::IDESC_DOT, 1u);
+                            tc::mma_bf16(d, al, bh, Cfg::IDESC_DOT, 1u);
+                        }
+                        tc::commit(&s_dot_full[s]);
+                        last_bar = &s_dot_full[s];
+                        last_par = (cd / STAGES) & 1;
+                        cd++;
+                    }
+                    progress = true;
+                }
+                if (cf < cd && tc::mbar_try_wait(&s_walk_done[cf % STAGES], (cf / STAGES) & 1)) {
+                    // dF^T of chunk cf = G^T W (its weights are in the stage's F/W buffer).
+                    const int s = cf % STAGES;
+                    tc::fence_after_sync();
+                    const uint32_t wh = w_hi(s), wl = wh + W_BYTES;
+#pragma unroll
+                    for (int ks = 0; ks < PIX / 16; ks++) {
+                        const uint64_t ah = tc::smem_desc(g_hi + ks * 256, 128, 2048);
+                        const uint64_t al = tc::smem_desc(g_lo + ks * 256, 128, 2048);
+                        const uint64_t bh = tc::smem_desc(wh + ks * 256, 128, 2048);
+                        const uint64_t bl = tc::smem_desc(wl + ks * 256, 128, 2048);
+                        const uint32_t d = tmem + 128 + s * 32;
+                        tc::mma_bf16(d, ah, bh, Cfg::IDESC_DF, ks > 0 ? 1u : 0u);
+                        tc::mma_bf16(d, ah, bl, Cfg::IDESC_DF, 1u);
+                        tc::mma_bf16(d, al, bh, Cfg::IDESC_DF, 1u);
+                    }
+                    tc::commit(&s_df_full[s]);
+                    last_bar = &s_df_full[s];
+                    last_par = (cf / STAGES) & 1;
+                    cf++;
+                    progress = true;
+                }
+                if (progress) {
+                    idle = 0;
+                } else if (++idle > WAIT_LIMIT) {
+                    s_fail = 1;
+                    break;
+                }
+            }
+            // tcgen05 operations complete in issue order: the last commit covers every MMA.
+            if (last_bar != nullptr && !tc::mbar_wait_bounded(last_bar, last_par, WAIT_LIMIT)) s_fail = 1;
+        }
+    } else {  // Role::Pixel
         // ------------------------------------------------------------------ pixel warps 0-7
         // Two threads per pixel: warp w covers 16 pixels of TMEM lane quadrant w & 3 (an 8 x 2
         // block); thread t < 16 and its partner t + 16 share pixel t, and each computes the alphas
-        // of half of every group of eight entries (role 0: entries 0-3, role 1: entries 4-7).
-        const int quad = warp & 3, half16 = warp >> 2, role = lane >> 4;
+        // of half of every group of eight entries (part 0: entries 0-3, part 1: entries 4-7).
+        const int quad = warp & 3, half16 = warp >> 2, part = lane >> 4;
         const int p = quad * 32 + half16 * 16 + (lane & 15);
         const int2 lp = half_tile_pixel(p);
         const int px = x0 + lp.x, py = y0 + lp.y;
@@ -424,7 +486,6 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
         const int last = inside ? n_contrib[pix] : 0;
         float behind = 0.0f;
         const uint32_t lane_base = (uint32_t)(quad * 32 + half16 * 16) << 16;
-        int df_committed = 0;
 
         for (int c = 0;; c++) {
             const int s = c % STAGES;
@@ -437,7 +498,7 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
                 if (!bad && ch.count > 0 && !tc::mbar_wait_bounded(&s_dot_full[s], par, WAIT_LIMIT)) bad = true;
                 if (bad) s_fail = 1;
             }
-            if (tc::group_sync_count(PIXEL_BAR, bad, PIXEL_THREADS) != 0) break;
+            if (tc::group_sync_count<PIXEL_BAR>(bad, PIXEL_THREADS) != 0) break;
             const int cnt = ch.count;
             if (cnt == 0) break;
             tc::fence_after_sync();
@@ -452,7 +513,7 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
             const uint32_t wh = w_hi(s), wl = wh + W_BYTES, ub = u_base(s) + p * 16;
 #pragma unroll 1
             for (int k0 = 0; k0 < cnt; k0 += 8) {
-                const int kb = k0 + 4 * role;  // this thread's four entries
+                const int kb = k0 + 4 * part;  // this thread's four entries
                 float d_own[4];
                 tc::tmem_ld16x2_4(tmem + lane_base + s * 32 + k0, d_own);
                 bool hit[4];
@@ -474,25 +535,25 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
                         // A clamped alpha no longer depends on the gaussian: nothing flows past it.
                         g_own[i] = ok && pa.raw <= MAX_ALPHA ? pa.G : 0.0f;
                     }
-                    // Entries 0-3 come from role 0, entries 4-7 from role 1.
+                    // Entries 0-3 come from part 0, entries 4-7 from part 1.
                     float a8[8], r8[8], d8[8];
 #pragma unroll
                     for (int i = 0; i < 4; i++) {
                         const float a_p = __shfl_xor_sync(FULL_MASK, a_own[i], 16);
                         const float r_p = __shfl_xor_sync(FULL_MASK, r_own[i], 16);
                         const float d_p = __shfl_xor_sync(FULL_MASK, d_own[i], 16);
-                        a8[i] = role ? a_p : a_own[i];
-                        a8[i + 4] = role ? a_own[i] : a_p;
-                        r8[i] = role ? r_p : r_own[i];
-                        r8[i + 4] = role ? r_own[i] : r_p;
-                        d8[i] = role ? d_p : d_own[i];
-                        d8[i + 4] = role ? d_own[i] : d_p;
+                        a8[i] = part ? a_p : a_own[i];
+                        a8[i + 4] = part ? a_own[i] : a_p;
+                        r8[i] = part ? r_p : r_own[i];
+                        r8[i + 4] = part ? r_own[i] : r_p;
+                        d8[i] = part ? d_p : d_own[i];
+                        d8[i + 4] = part ? d_own[i] : d_p;
                     }
 #pragma unroll
                     for (int i = 0; i < 8; i++) {
                         T = T * r8[i];
                         const float dL_dalpha = T * (d8[i] - behind);
-                        if ((i >> 2) == role) {  // this thread's entry: a select, not a branch
+                        if ((i >> 2) == part) {  // this thread's entry: a select, not a branch
                             w_own[i & 3] = T * a8[i];
                             u_own[i & 3] = dL_dalpha * g_own[i & 3];
                         }
@@ -504,36 +565,16 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
                 uint32_t h0, l0, h1, l1;
                 split_bf16(w_own[0], w_own[1], h0, l0);
                 split_bf16(w_own[2], w_own[3], h1, l1);
-                st_shared_v2(wh + (k0 >> 3) * 2048 + p * 16 + role * 8, h0, h1);
-                st_shared_v2(wl + (k0 >> 3) * 2048 + p * 16 + role * 8, l0, l1);
-                st_shared_v4(ub + ((k0 >> 2) + role) * U_QUAD_STRIDE, __float_as_uint(u_own[0]),
+                st_shared_v2(wh + (k0 >> 3) * 2048 + p * 16 + part * 8, h0, h1);
+                st_shared_v2(wl + (k0 >> 3) * 2048 + p * 16 + part * 8, l0, l1);
+                st_shared_v4(ub + ((k0 >> 2) + part) * U_QUAD_STRIDE, __float_as_uint(u_own[0]),
                              __float_as_uint(u_own[1]), __float_as_uint(u_own[2]), __float_as_uint(u_own[3]));
             }
             tc::fence_proxy_async();
             tc::fence_before_sync();
-            tc::group_sync(PIXEL_BAR, PIXEL_THREADS);
-            if (tid == 0) {
-                tc::fence_after_sync();
-#pragma unroll
-                for (int ks = 0; ks < PIX / 16; ks++) {
-                    const uint64_t ah = tc::smem_desc(g_hi + ks * 256, 128, 2048);
-                    const uint64_t al = tc::smem_desc(g_lo + ks * 256, 128, 2048);
-                    const uint64_t bh = tc::smem_desc(wh + ks * 256, 128, 2048);
-                    const uint64_t bl = tc::smem_desc(wl + ks * 256, 128, 2048);
-                    const uint32_t d = tmem + 128 + s * 32;
-                    tc::mma_bf16(d, ah, bh, Cfg::IDESC_DF, ks > 0 ? 1u : 0u);
-                    tc::mma_bf16(d, ah, bl, Cfg::IDESC_DF, 1u);
-                    tc::mma_bf16(d, al, bh, Cfg::IDESC_DF, 1u);
-                }
-                tc::commit(&s_df_full[s]);
-                tc::mbar_arrive(&s_walk_done[s]);
-                df_committed = c + 1;
-            }
+            tc::group_sync<PIXEL_BAR>(PIXEL_THREADS);
+            if (tid == 0) tc::mbar_arrive(&s_walk_done[s]);
         }
-        if (tid == 0 && df_committed > 0 &&
-            !tc::mbar_wait_bounded(&s_df_full[(df_committed - 1) % STAGES], ((df_committed - 1) / STAGES) & 1,
-                                   WAIT_LIMIT))
-            s_fail = 1;
     }
     tc::fence_before_sync();
     __syncthreads();

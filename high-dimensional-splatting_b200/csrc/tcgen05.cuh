@@ -159,19 +159,23 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
-// Named barrier over the n threads (a multiple of 32) of one warp group; ids 1..15 (0 is
-// __syncthreads).
-__device__ __forceinline__ void group_sync(int id, int n = 128) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+// Named barrier ID over the n threads (a multiple of 32) of one warp group; IDs 1..15 (0 is
+// __syncthreads).  The ID is an immediate so that ptxas reserves every barrier the kernel uses.
+template <int ID>
+__device__ __forceinline__ void group_sync(int n = 128) {
+    static_assert(ID > 0 && ID < 16, "named barrier id");
+    asm volatile("bar.sync %0, %1;" ::"n"(ID), "r"(n) : "memory");
 }
 
 // Group barrier that also returns how many of its n threads passed pred = true.
-__device__ __forceinline__ int group_sync_count(int id, bool pred, int n = 128) {
+template <int ID>
+__device__ __forceinline__ int group_sync_count(bool pred, int n = 128) {
+    static_assert(ID > 0 && ID < 16, "named barrier id");
     int r;
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.s32 p, %1, 0;\n\tbarrier.cta.red.popc.u32 %0, %2, %3, p;\n\t}"
         : "=r"(r)
-        : "r"((int)pred), "r"(id), "r"(n)
+        : "r"((int)pred), "n"(ID), "r"(n)
         : "memory");
     return r;
 }
@@ -186,6 +190,21 @@ __device__ __forceinline__ void tmem_ld16x2_4(uint32_t taddr, float* v) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 4; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// As mbar_wait_bounded, for waits off the critical path: after a few polls the thread sleeps
+// between polls (up to 256 ns), leaving issue slots to the warps that do the work.  Gives up after
+// `limit` polls.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, uint32_t limit) {
+    uint32_t ns = 0;
+    for (uint32_t i = 0; i < limit; i++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (i >= 4) {
+            ns = ns < 256 ? ns + 32 : 256;
+            __nanosleep(ns);
+        }
+    }
+    return false;
 }
 
 __device__ __forceinline__ float to_tf32(float x) {
