@@ -174,6 +174,10 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
     const Role role = role_of(warp);
     if (role == Role::List) {
         // ------------------------------------------------------------------ list warp 8
+        // Walks the tile's list back to front in batches of 32 positions (lane l: position
+        // top - 1 - l), software-pipelined over three batches: the sorted ids of batch A, the
+        // gathered means / conics / opacities of batch B, and the hit mask of batch C that chunks
+        // are cut from.  Hits left over when a chunk fills stay in C's mask for the next chunk.
         // Entries past every pixel's last contributor cannot contribute: start there.
         int m = 0;
 #pragma unroll
@@ -182,8 +186,37 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
             const int px = x0 + lp.x, py = y0 + lp.y;
             if (px < width && py < height) m = max(m, n_contrib[(size_t)py * width + px]);
         }
-        int end = min(range.y - range.x, __reduce_max_sync(FULL_MASK, m));
+        int top = min(range.y - range.x, __reduce_max_sync(FULL_MASK, m));
         const float hx0 = (float)x0 + 0.5f, hx1 = hx0 + 15.0f, hy0 = (float)y0 + 0.5f, hy1 = hy0 + 7.0f;
+        auto fetch_id = [&](int t) { return t - 1 - lane >= 0 ? values[range.x + t - 1 - lane] : -1; };
+        // Batch A: ids only.  Batch B: ids and gathered geometry.  Batch C: geometry and hits.
+        int top_a = top, id_a = fetch_id(top);
+        top -= 32;
+        int top_b = top, id_b = fetch_id(top);
+        top -= 32;
+        float2 m_b = make_float2(0.0f, 0.0f);
+        float4 q_b = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        auto gather = [&](int g, float2& mm, float4& qq) {
+            if (g >= 0) {
+                mm = means2D[g];
+                const float4 cq = conic4[g];
+                qq = make_float4(cq.x, cq.y, cq.z, color_opacity[g].w);
+            }
+        };
+        // Prime: B <- first batch (gathered), A <- second batch.
+        {
+            const int t = top_a, i = id_a;
+            top_a = top_b;
+            id_a = id_b;
+            top_b = t;
+            id_b = i;
+            gather(id_b, m_b, q_b);
+        }
+        int top_c = 0, id_c = -1;
+        float2 m_c = make_float2(0.0f, 0.0f), e_c = make_float2(0.0f, 0.0f);
+        float4 q_c = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        unsigned mask_c = 0;
+        bool more = top_b > 0;  // does batch B hold any position?
         for (int c = 0;; c++) {
             const int slot = c % LIST_SLOTS;
             BwdChunk& ch = s_list[slot];
@@ -196,50 +229,47 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
                 }
                 if (!__shfl_sync(FULL_MASK, ok, 0)) break;
             }
-            // Select the next entries (back to front) whose box meets the half tile; two batches of
-            // 32 candidates per round trip to memory.
             int filled = 0;
-            while (filled < KC && end > 0) {
-                int g[2];
-                float2 mm[2], e2[2];
-                float4 q[2];
-                bool hit[2];
-#pragma unroll
-                for (int b = 0; b < 2; b++) {
-                    const int pos = end - 1 - 32 * b - lane;
-                    hit[b] = false;
-                    g[b] = 0;
-                    mm[b] = e2[b] = make_float2(0.0f, 0.0f);
-                    q[b] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                    if (pos >= 0) {
-                        g[b] = values[range.x + pos];
-                        mm[b] = means2D[g[b]];
-                        const float4 cq = conic4[g[b]];
-                        q[b] = make_float4(cq.x, cq.y, cq.z, color_opacity[g[b]].w);
-                        e2[b] = cull_extent(q[b].x, q[b].y, q[b].z, q[b].w);
-                        hit[b] = box_hits(mm[b], e2[b], hx0, hx1, hy0, hy1);
-                    }
+            while (filled < KC) {
+                if (mask_c == 0) {
+                    if (!more) break;  // list exhausted
+                    // Promote B to C (its gathers were issued a batch ago), A to B, and fetch a new A.
+                    top_c = top_b;
+                    id_c = id_b;
+                    m_c = m_b;
+                    q_c = q_b;
+                    e_c = id_c >= 0 ? cull_extent_fast(q_c.x, q_c.y, q_c.z, q_c.w) : make_float2(-1e30f, -1e30f);
+                    mask_c = __ballot_sync(FULL_MASK, id_c >= 0 && box_hits(m_c, e_c, hx0, hx1, hy0, hy1));
+                    more = top_a > 0;
+                    top_b = top_a;
+                    id_b = id_a;
+                    m_b = make_float2(0.0f, 0.0f);
+                    q_b = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    gather(id_b, m_b, q_b);
+                    top_a = top;
+                    id_a = fetch_id(top);
+                    top -= 32;
+                    continue;
                 }
-#pragma unroll
-                for (int b = 0; b < 2; b++) {
-                    if (filled == KC || end <= 0) break;
-                    const unsigned mask = __ballot_sync(FULL_MASK, hit[b]);
-                    const int hits = __popc(mask);
-                    const int take = min(hits, KC - filled);
-                    const int rank = __popc(mask & ((1u << lane) - 1u));
-                    if (hit[b] && rank < take) {
-                        const int k = filled + rank;
-                        ch.id[k] = g[b];
-                        ch.pos[k] = end - 1 - lane;
-                        ch.mean[k] = mm[b];
-                        ch.ext[k] = e2[b];
-                        ch.conic[k] = q[b];
-                    }
-                    // When the chunk fills mid-batch, resume just below the last entry taken.
-                    end = take < hits ? end - 1 - nth_set_bit(mask, take - 1) : end - 32;
-                    filled += take;
+                const int hits = __popc(mask_c);
+                const int take = min(hits, KC - filled);
+                const int rank = __popc(mask_c & ((1u << lane) - 1u));
+                if (((mask_c >> lane) & 1u) && rank < take) {
+                    const int k = filled + rank;
+                    ch.id[k] = id_c;
+                    ch.pos[k] = top_c - 1 - lane;
+                    ch.mean[k] = m_c;
+                    ch.ext[k] = e_c;
+                    ch.conic[k] = q_c;
                 }
-                end = max(end, 0);
+                // Clear the taken bits (the lowest `take` set bits: descending positions).
+                if (take == hits) {
+                    mask_c = 0;
+                } else {
+                    const int last_lane = nth_set_bit(mask_c, take - 1);
+                    mask_c &= ~((2u << last_lane) - 1u);
+                }
+                filled += take;
             }
             if (lane == 0) ch.count = filled;
             __syncwarp();
