@@ -176,7 +176,7 @@ def render_view(wl, i, pose, gt_u8):
 
     from hds_b200.loss import l1_loss, ssim
     from hds_b200.projection import project_gaussians
-    from hds_b200.rasterizer import rasterize
+    from hds_b200.rasterizer import accumulate_leaf_grads, rasterize
     from hds_b200.sh import eval_sh_grad
 
     cam = wl["cams"][wl["views"][i]]
@@ -186,8 +186,10 @@ def render_view(wl, i, pose, gt_u8):
     center = -(pose[:3, :3].T @ pose[:3, 3])
     dirs = torch.nn.functional.normalize(L["means"] - center, dim=-1)
     colors = eval_sh_grad(L["sh_dc"], L["sh_rest"], dirs, 3, radii)
-    image, feat = rasterize(means2D, depths, radii, conics, colors, L["opacities"], cam.width, cam.height, wl["bg"],
-                            L["features"])
+    # The views of a step accumulate into the gradient bucket: the feature backward adds straight into it.
+    with accumulate_leaf_grads():
+        image, feat = rasterize(means2D, depths, radii, conics, colors, L["opacities"], cam.width, cam.height,
+                                wl["bg"], L["features"])
     gt = gt_u8.float() / 255.0
     loss = 0.8 * l1_loss(image, gt) + 0.2 * (1.0 - ssim(image, gt))
     torch.autograd.backward([loss, feat], [None, wl["feat_grad"]])
@@ -257,7 +259,7 @@ def roofline(name, ms_per_launch, stats, args, peaks, n):
         return {"bound": "tensor", "achieved": ach, "peak": tf32_peak, "unit": "TFLOP/s", "frac": ach / tf32_peak,
                 "traffic": None, "kernel": name,
                 "peak_note": f"TF32 dense = half the {peaks['source']} cuBLAS bf16 rate"}
-    if name == "hds_render_features_backward":
+    if name in ("hds_render_features_backward", "hds_render_features_backward_accumulate"):
         nbytes = P * (4 * C + 12) + V * (4 * C + 32) + n * (4 * C + 36) * 2
     elif name == "hds_render_backward":
         nbytes = P * (12 + 8) + V * 44 + n * 36 * 2

@@ -643,13 +643,13 @@ int read_and_clear_backward_status(int* status, cudaStream_t stream) {
 
 using namespace hds;
 
-extern "C" int hds_render_features_backward(int n, int channels, int slice_width, int width, int height,
-                                            const float* grad_output, const float* features, const float* means2D,
-                                            const float* conic4, const float* color_opacity,
-                                            const int32_t* values_sorted, const int32_t* tile_ranges,
-                                            const float* final_T, const int32_t* n_contrib, float* grad_features,
-                                            float* grad_means2D, float* grad_conics, float* grad_opacities,
-                                            hds_stream_t stream) {
+namespace {
+
+int features_backward(int n, int channels, int slice_width, int width, int height, const float* grad_output,
+                      const float* features, const float* means2D, const float* conic4, const float* color_opacity,
+                      const int32_t* values_sorted, const int32_t* tile_ranges, const float* final_T,
+                      const int32_t* n_contrib, float* grad_features, float* grad_means2D, float* grad_conics,
+                      float* grad_opacities, bool accumulate_features, cudaStream_t stream) {
     clear_error();
     HDS_REQUIRE(n >= 0 && width > 0 && height > 0, HDS_ERR_INVALID, "rasterize_features_backward: bad sizes");
     HDS_REQUIRE((int64_t)channels * width * height <= INT32_MAX, HDS_ERR_TOO_LARGE,
@@ -660,10 +660,11 @@ extern "C" int hds_render_features_backward(int n, int channels, int slice_width
                            (D == 128 && (Wd == 128 || Wd == 64 || Wd == 32)) || (D == 256 && (Wd == 128 || Wd == 64)) ||
                            (D == 512 && (Wd == 128 || Wd == 64));
     HDS_REQUIRE(supported, HDS_ERR_UNSUPPORTED, "no feature backward for %d channels in slices of %d", D, Wd);
-    HDS_REQUIRE(((uintptr_t)features & 15) == 0 && ((uintptr_t)grad_output & 15) == 0, HDS_ERR_INVALID,
-                "rasterize_features_backward: features and grad_output must be 16-byte aligned");
+    HDS_REQUIRE(((uintptr_t)features & 15) == 0 && ((uintptr_t)grad_output & 15) == 0 &&
+                    ((uintptr_t)grad_features & 15) == 0,
+                HDS_ERR_INVALID, "rasterize_features_backward: features, grad_output and grad_features must be 16-byte aligned");
     if (n == 0) return HDS_OK;
-    HDS_CHECK_CUDA(cudaMemsetAsync(grad_features, 0, sizeof(float) * (size_t)n * D, stream));
+    if (!accumulate_features) HDS_CHECK_CUDA(cudaMemsetAsync(grad_features, 0, sizeof(float) * (size_t)n * D, stream));
     HDS_CHECK_CUDA(cudaMemsetAsync(grad_means2D, 0, sizeof(float) * 2 * (size_t)n, stream));
     HDS_CHECK_CUDA(cudaMemsetAsync(grad_conics, 0, sizeof(float) * 3 * (size_t)n, stream));
     HDS_CHECK_CUDA(cudaMemsetAsync(grad_opacities, 0, sizeof(float) * (size_t)n, stream));
@@ -674,4 +675,31 @@ extern "C" int hds_render_features_backward(int n, int channels, int slice_width
         case 64: return launch_backward<64>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, stream);
         default: return launch_backward<128>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, stream);
     }
+}
+
+}  // namespace
+
+extern "C" int hds_render_features_backward(int n, int channels, int slice_width, int width, int height,
+                                            const float* grad_output, const float* features, const float* means2D,
+                                            const float* conic4, const float* color_opacity,
+                                            const int32_t* values_sorted, const int32_t* tile_ranges,
+                                            const float* final_T, const int32_t* n_contrib, float* grad_features,
+                                            float* grad_means2D, float* grad_conics, float* grad_opacities,
+                                            hds_stream_t stream) {
+    return features_backward(n, channels, slice_width, width, height, grad_output, features, means2D, conic4,
+                             color_opacity, values_sorted, tile_ranges, final_T, n_contrib, grad_features,
+                             grad_means2D, grad_conics, grad_opacities, false, stream);
+}
+
+extern "C" int hds_render_features_backward_accumulate(int n, int channels, int slice_width, int width, int height,
+                                                       const float* grad_output, const float* features,
+                                                       const float* means2D, const float* conic4,
+                                                       const float* color_opacity, const int32_t* values_sorted,
+                                                       const int32_t* tile_ranges, const float* final_T,
+                                                       const int32_t* n_contrib, float* grad_features,
+                                                       float* grad_means2D, float* grad_conics, float* grad_opacities,
+                                                       hds_stream_t stream) {
+    return features_backward(n, channels, slice_width, width, height, grad_output, features, means2D, conic4,
+                             color_opacity, values_sorted, tile_ranges, final_T, n_contrib, grad_features,
+                             grad_means2D, grad_conics, grad_opacities, true, stream);
 }

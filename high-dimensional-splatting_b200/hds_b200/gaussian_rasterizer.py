@@ -159,6 +159,29 @@ def rasterize_features_backward(grad_output, features, means2D, conic, color_opa
     return gf, gm, gc, go
 
 
+def rasterize_features_backward_into(grad_features, grad_output, features, means2D, conic, color_opacity,
+                                     values_sorted, tile_ranges, final_transmittance, n_contrib, image_width: int,
+                                     image_height: int, slice_width: int):
+    """rasterize_features_backward that ADDS dL/dfeatures into grad_features ([N,D] fp32, contiguous)
+    instead of returning a fresh tensor; no counterpart in the reference.  Returns (dL/dmeans2D,
+    dL/dconics, dL/dopacities)."""
+    if not (grad_output.is_cuda and grad_output.is_contiguous()):
+        raise RuntimeError("grad_output must be a contiguous CUDA tensor")
+    n, d = features.shape
+    if not (grad_features.is_contiguous() and grad_features.dtype == _F32 and tuple(grad_features.shape) == (n, d)
+            and grad_features.device == features.device):
+        raise RuntimeError("grad_features must be a contiguous float32 tensor shaped like features")
+    dev = features.device
+    gm = torch.empty(n, 2, dtype=_F32, device=dev)
+    gc = torch.empty(n, 3, dtype=_F32, device=dev)
+    go = torch.empty(n, 1, dtype=_F32, device=dev)
+    check(lib.hds_render_features_backward_accumulate(
+        n, d, int(slice_width), int(image_width), int(image_height), ptr(grad_output), ptr(features), ptr(means2D),
+        ptr(conic), ptr(color_opacity), ptr(values_sorted), ptr(tile_ranges), ptr(final_transmittance),
+        ptr(n_contrib), ptr(grad_features), ptr(gm), ptr(gc), ptr(go), stream_of(dev)))
+    return gm, gc, go
+
+
 def eval_sh(sh_dc, sh_rest, dirs, degree: int, radii):
     """sh.cu:157-168.  Returns rgb [N,3]."""
     n = sh_dc.shape[0]

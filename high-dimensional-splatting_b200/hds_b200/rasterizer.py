@@ -15,6 +15,27 @@ from . import gaussian_rasterizer as _ext
 # (the reference's __init__.py:11-12, 158).
 FEATURE_SLICE_WIDTH: int | None = None
 
+# When true, the backward of a rasterize call whose features are a leaf that already holds a
+# contiguous float32 .grad of its shape adds dL/dfeatures straight into that .grad (and hands
+# autograd no gradient for it), instead of returning a fresh [N, D] tensor that autograd then adds.
+# For loops that accumulate several views into one gradient buffer.  Hooks registered on the
+# features tensor are not run for that gradient.  Off by default (the reference's behaviour).
+ACCUMULATE_INTO_LEAF_GRAD: bool = False
+
+
+class accumulate_leaf_grads:
+    """Context manager that turns ACCUMULATE_INTO_LEAF_GRAD on for its body."""
+
+    def __enter__(self):
+        global ACCUMULATE_INTO_LEAF_GRAD
+        self._old, ACCUMULATE_INTO_LEAF_GRAD = ACCUMULATE_INTO_LEAF_GRAD, True
+        return self
+
+    def __exit__(self, *exc):
+        global ACCUMULATE_INTO_LEAF_GRAD
+        ACCUMULATE_INTO_LEAF_GRAD = self._old
+        return False
+
 
 def _get_rasterizer() -> ModuleType:
     """The extension module with the reference's ten entry points (see gaussian_rasterizer.py)."""
@@ -40,6 +61,7 @@ class RasterizeGaussians(torch.autograd.Function):
             ctx.save_for_backward(means2D, conic, color_opacity, values, ranges, final_T, n_contrib, background, None,
                                   None, None)
             return image
+        ctx.features_leaf = features if (ACCUMULATE_INTO_LEAF_GRAD and features.is_leaf) else None
         features = features.contiguous()
         image, feature_image, final_T, n_contrib, values, ranges, conic, color_opacity = ext.rasterize_with_features(
             *args, features, width, height)
@@ -63,15 +85,26 @@ class RasterizeGaussians(torch.autograd.Function):
         grad_feats = None
         # Frozen features still shape the geometry gradients (the reference's __init__.py:150-153).
         if features is not None and grad_features is not None and any(ctx.needs_input_grad[i] for i in (0, 3, 5, 7)):
-            with torch.cuda.nvtx.range("rasterize_features_backward"):
-                grad_feats, f_means2D, f_conics, f_opacities = ext.rasterize_features_backward(
-                    grad_features.contiguous(), features, means2D, conic, color_opacity, values, ranges, feature_T,
-                    feature_contrib, width, height, FEATURE_SLICE_WIDTH or min(features.shape[1], 128))
+            slice_width = FEATURE_SLICE_WIDTH or min(features.shape[1], 128)
+            leaf = getattr(ctx, "features_leaf", None)
+            target = leaf.grad if (leaf is not None and ctx.needs_input_grad[7]) else None
+            if (target is not None and target.is_contiguous() and target.dtype == torch.float32
+                    and target.shape == features.shape and target.device == features.device
+                    and target.data_ptr() % 16 == 0):
+                with torch.cuda.nvtx.range("rasterize_features_backward"):
+                    f_means2D, f_conics, f_opacities = ext.rasterize_features_backward_into(
+                        target, grad_features.contiguous(), features, means2D, conic, color_opacity, values, ranges,
+                        feature_T, feature_contrib, width, height, slice_width)
+            else:
+                with torch.cuda.nvtx.range("rasterize_features_backward"):
+                    grad_feats, f_means2D, f_conics, f_opacities = ext.rasterize_features_backward(
+                        grad_features.contiguous(), features, means2D, conic, color_opacity, values, ranges,
+                        feature_T, feature_contrib, width, height, slice_width)
+                if not ctx.needs_input_grad[7]:
+                    grad_feats = None
             grad_means2D += f_means2D
             grad_conics += f_conics
             grad_opacities += f_opacities
-            if not ctx.needs_input_grad[7]:
-                grad_feats = None
         return grad_means2D, None, None, grad_conics, grad_colors, grad_opacities, None, grad_feats, None, None
 
 

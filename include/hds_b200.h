@@ -158,6 +158,18 @@ int hds_render_features_backward(int n, int channels, int slice_width, int width
                                  float* grad_features, float* grad_means2D, float* grad_conics,
                                  float* grad_opacities, hds_stream_t stream);
 
+/* As hds_render_features_backward, but dL/dfeatures is ADDED to grad_features (which is not
+ * cleared); the other three outputs are written as above.  No counterpart in the reference: it lets
+ * a training loop that accumulates several views into one gradient buffer skip clearing a fresh
+ * [n,C] buffer and adding it afterwards.  grad_features must be 16-byte aligned. */
+int hds_render_features_backward_accumulate(int n, int channels, int slice_width, int width, int height,
+                                            const float* grad_output, const float* features, const float* means2D,
+                                            const float* conic4, const float* color_opacity,
+                                            const int32_t* values_sorted, const int32_t* tile_ranges,
+                                            const float* final_T, const int32_t* n_contrib, float* grad_features,
+                                            float* grad_means2D, float* grad_conics, float* grad_opacities,
+                                            hds_stream_t stream);
+
 /* ---------------------------------------------------------------------------------------------
  * SSIM (11x11 gaussian window, sigma 1.5).  Replace ssim_forward (ssim.cu:306-338) and
  * ssim_backward (ssim.cu:340-367); glue utils/loss.py:57-90.  Images [H,W,3]; grad_mean is a
