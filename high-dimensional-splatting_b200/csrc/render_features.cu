@@ -353,6 +353,462 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
     if (tid == 0 && s_fail) atomicExch(&g_status, HDS_ERR_DEVICE);
 }
 
+// ----------------------------------------------------------------------------------------------
+// Warp-specialised variant for C >= 256, where the C-column accumulator (TMEM) admits one block per
+// SM anyway.  Roles (448 threads):
+//   * pixel warps 0-7, two threads per pixel: warp w covers 16 pixels of TMEM lane quadrant w & 3 (an
+//     8 x 2 block); thread t < 16 and t + 16 share a pixel and each computes the alphas of half of
+//     every group of eight entries, swaps them (shfl.xor 16), and both run the walk over all eight
+//     with the oracle's exact FP32 operations in list order -- RGB, final T and the contributor count
+//     stay bit-identical -- each writing its four TF32 weights of the K-major A operand;
+//   * list warp 8 cuts the tile's list (front to back) into chunks of 32 entries whose box meets the
+//     half tile, software-pipelined over three 32-position batches, into a ring of list slots;
+//   * gather warps 9-12 copy each chunk's feature rows with 16-byte loads, round them to TF32, and
+//     store them as the MN-major B operand in the 128-byte swizzle on 32-byte atoms (in row k of an
+//     atom the four 32-byte chunks are permuted by XOR with k mod 4) -- no transposition;
+//   * MMA warp 13 (one lane) issues 4 x C/256 tcgen05.mma per chunk (M = 128, N = 256, K = 8) into
+//     the TMEM accumulators, releases the list slot, and after the last chunk tells the pixel warps.
+// ----------------------------------------------------------------------------------------------
+namespace ws {
+
+constexpr int KC = 32;
+constexpr int LIST_SLOTS = 6;
+constexpr int PIXEL_WARPS = 8, LIST_WARP = 8, GATHER_WARP0 = 9, GATHER_WARPS = 4, MMA_WARP = 13;
+constexpr int THREADS = (MMA_WARP + 1) * 32, PIXEL_THREADS = PIXEL_WARPS * 32, GATHER_THREADS = GATHER_WARPS * 32;
+static_assert(LIST_WARP == PIXEL_WARPS && GATHER_WARP0 == LIST_WARP + 1 && MMA_WARP == GATHER_WARP0 + GATHER_WARPS,
+              "warp roles must partition the block");
+constexpr int PIX_BAR = 1, GATHER_BAR = 2;
+
+enum class Role { Pixel, List, Gather, Mma };
+__device__ __forceinline__ Role role_of(int warp) {
+    return warp < PIXEL_WARPS ? Role::Pixel
+           : warp == LIST_WARP ? Role::List
+           : warp < GATHER_WARP0 + GATHER_WARPS ? Role::Gather
+                                                 : Role::Mma;
+}
+
+template <int C>
+struct Cfg {
+    static constexpr int STAGES = C >= 512 ? 2 : 3;
+    static constexpr int N_MMA = 256;
+    static constexpr int N_BLOCKS = C / N_MMA;
+    static constexpr int A_BYTES = 128 * KC * 4;  // K-major: (k/4)*A_LBO + (p/8)*128 + (p%8)*16 + (k%4)*4
+    static constexpr int A_LBO = 2048;
+    static constexpr int B_SBO = (C / 32) * 512;  // between atoms of 4 entries; atoms of 32 channels are 512 B apart
+    static constexpr int B_BYTES = (KC / 4) * B_SBO;
+    static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + 1024;
+    static constexpr uint32_t IDESC = tc::idesc_tf32(128, N_MMA, false, true);
+    static_assert(C == 256 || C == 512, "the warp-specialised forward is for 256 or 512 channels");
+};
+
+// One list slot: chunk entries in list order.
+struct List {
+    int id[KC];
+    int pos[KC];
+    float2 mean[KC];
+    float2 ext[KC];
+    float4 conic[KC];  // a, b, c, opacity
+    float4 col[KC];    // r, g, b, opacity
+    int count;
+};
+
+__device__ __forceinline__ void st_shared_v4f(uint32_t addr, float4 v) {
+    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ int2 half_tile_pixel(int p) {
+    return make_int2(((p >> 5) & 1) * 8 + (p & 7), (p >> 6) * 4 + ((p & 31) >> 3));
+}
+
+template <int C>
+__global__ void __launch_bounds__(THREADS, 1) feature_forward_ws_kernel(
+    int width, int height, int tiles_x, const int2* __restrict__ ranges, const int32_t* __restrict__ values,
+    const float2* __restrict__ means2D, const float4* __restrict__ conic4, const float4* __restrict__ color_opacity,
+    const float* __restrict__ features, const float* __restrict__ background, float* __restrict__ feature_image,
+    float* __restrict__ final_T, int32_t* __restrict__ n_contrib, float4* __restrict__ image4) {
+    using K = Cfg<C>;
+    constexpr int S = K::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ List s_list[LIST_SLOTS];
+    __shared__ uint64_t s_list_full[LIST_SLOTS], s_list_free[LIST_SLOTS];
+    __shared__ uint64_t s_a_full[S], s_b_full[S], s_mma_done[S], s_acc_ready;
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_fail, s_have;
+    __shared__ int s_zero_from;  // first chunk walked after every pixel was done (its weights are all zero)
+    __shared__ int s_skip[S];  // the stage's weights are all zero: every pixel was done before its chunk
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tile = blockIdx.x >> 1;
+    const int x0 = (tile % tiles_x) * TILE;
+    const int y0 = (tile / tiles_x) * TILE + (blockIdx.x & 1) * 8;
+    if (y0 >= height) return;  // the lower half of a bottom-row tile can lie wholly outside the image
+
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t a_base = tc::smem_addr(smem);
+    const uint32_t b_base = a_base + S * K::A_BYTES;
+
+    if (warp == 0) tc::tmem_alloc(&s_tmem, C);
+    if (tid == 0) {
+        for (int i = 0; i < LIST_SLOTS; i++) {
+            tc::mbar_init(&s_list_full[i], 1);
+            tc::mbar_init(&s_list_free[i], 1);
+        }
+        for (int i = 0; i < S; i++) {
+            tc::mbar_init(&s_a_full[i], 1);
+            tc::mbar_init(&s_b_full[i], 1);
+            tc::mbar_init(&s_mma_done[i], 1);
+        }
+        tc::mbar_init(&s_acc_ready, 1);
+        tc::fence_mbar_init();
+        s_fail = 0;
+        s_zero_from = 0x7fffffff;
+        s_have = 0;
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = s_tmem;
+    const int2 range = ranges[tile];
+    const int count = range.y - range.x;
+    const Role role = role_of(warp);
+
+    if (role == Role::List) {
+        // ---------------------------------------------------------------- list warp
+        const float hx0 = (float)x0 + 0.5f, hx1 = hx0 + 15.0f, hy0 = (float)y0 + 0.5f, hy1 = hy0 + 7.0f;
+        auto fetch_id = [&](int b) { return b + lane < count ? values[range.x + b + lane] : -1; };
+        auto gather = [&](int g, float2& m, float4& q, float4& col) {
+            if (g >= 0) {
+                m = means2D[g];
+                col = color_opacity[g];
+                const float4 cq = conic4[g];
+                q = make_float4(cq.x, cq.y, cq.z, col.w);
+            }
+        };
+        // Batches of 32 positions (lane l: position base + l), front to back: A = ids, B = ids and
+        // geometry, C = geometry and the hit mask that chunks are cut from.
+        int base = 0;
+        int base_b = base, id_b = fetch_id(base);
+        base += 32;
+        int base_a = base, id_a = fetch_id(base);
+        base += 32;
+        float2 m_b = make_float2(0.0f, 0.0f);
+        float4 q_b = make_float4(0.0f, 0.0f, 0.0f, 0.0f), col_b = q_b;
+        gather(id_b, m_b, q_b, col_b);
+        int base_c = 0, id_c = -1;
+        float2 m_c = make_float2(0.0f, 0.0f), e_c = m_c;
+        float4 q_c = make_float4(0.0f, 0.0f, 0.0f, 0.0f), col_c = q_c;
+        unsigned mask_c = 0;
+        bool more = base_b < count;
+        for (int c = 0;; c++) {
+            const int slot = c % LIST_SLOTS;
+            List& ch = s_list[slot];
+            bool ok = true;
+            if (lane == 0 && c >= LIST_SLOTS) {
+                ok = !*(volatile int*)&s_fail &&
+                     tc::mbar_wait_bounded(&s_list_free[slot], ((c - LIST_SLOTS) / LIST_SLOTS) & 1, WAIT_LIMIT);
+                if (!ok) s_fail = 1;
+            }
+            if (!__shfl_sync(FULL_MASK, ok, 0)) break;
+            // Once every pixel is done, the empty chunk ends the list.
+            const bool stop = __shfl_sync(FULL_MASK, *(volatile int*)&s_zero_from, 0) != 0x7fffffff;
+            int filled = 0;
+            while (!stop && filled < KC) {
+                if (mask_c == 0) {
+                    if (!more) break;  // list exhausted
+                    base_c = base_b;
+                    id_c = id_b;
+                    m_c = m_b;
+                    q_c = q_b;
+                    col_c = col_b;
+                    e_c = id_c >= 0 ? cull_extent_fast(q_c.x, q_c.y, q_c.z, q_c.w) : make_float2(-1e30f, -1e30f);
+                    mask_c = __ballot_sync(FULL_MASK, id_c >= 0 && box_hits(m_c, e_c, hx0, hx1, hy0, hy1));
+                    more = base_a < count;
+                    base_b = base_a;
+                    id_b = id_a;
+                    m_b = make_float2(0.0f, 0.0f);
+                    q_b = col_b = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    gather(id_b, m_b, q_b, col_b);
+                    base_a = base;
+                    id_a = fetch_id(base);
+                    base += 32;
+                    continue;
+                }
+                const int hits = __popc(mask_c);
+                const int take = min(hits, KC - filled);
+                const int rank = __popc(mask_c & ((1u << lane) - 1u));
+                if (((mask_c >> lane) & 1u) && rank < take) {
+                    const int k = filled + rank;
+                    ch.id[k] = id_c;
+                    ch.pos[k] = base_c + lane;
+                    ch.mean[k] = m_c;
+                    ch.ext[k] = e_c;
+                    ch.conic[k] = q_c;
+                    ch.col[k] = col_c;
+                }
+                if (take == hits) {
+                    mask_c = 0;
+                } else {
+                    const int last_lane = nth_set_bit(mask_c, take - 1);
+                    mask_c &= ~((2u << last_lane) - 1u);
+                }
+                filled += take;
+            }
+            if (lane == 0) ch.count = filled;
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&s_list_full[slot]);
+            if (filled == 0) break;
+        }
+    } else if (role == Role::Gather) {
+        // ---------------------------------------------------------------- gather warps
+        const int gtid = tid - GATHER_WARP0 * 32;
+        for (int c = 0;; c++) {
+            const int s = c % S, slot = c % LIST_SLOTS;
+            const List& ch = s_list[slot];
+            bool bad = false;
+            if (gtid == 0) {
+                bad = *(volatile int*)&s_fail ||
+                      !tc::mbar_wait_bounded(&s_list_full[slot], (c / LIST_SLOTS) & 1, WAIT_LIMIT);
+                // Stage s is free once chunk c - S's MMAs have read it.
+                if (!bad && ch.count > 0 && c >= S)
+                    bad = !tc::mbar_wait_bounded(&s_mma_done[s], ((c - S) / S) & 1, WAIT_LIMIT);
+                if (bad) s_fail = 1;
+            }
+            if (tc::group_sync_count<GATHER_BAR>(bad, GATHER_THREADS) != 0) break;
+            const int cnt = ch.count;
+            if (cnt == 0) break;
+            // Chunks walked after every pixel was done carry zero weights and their MMAs are skipped.
+            // (Only those: the chunk that finished the last pixel is still blended.)
+            const bool stopped = tc::group_sync_count<GATHER_BAR>(gtid == 0 && c >= *(volatile int*)&s_zero_from,
+                                                                  GATHER_THREADS) != 0;
+            // Item (k, j): entry k's channels 4j .. 4j + 3; a warp reads 512 contiguous bytes of a row.
+            const uint32_t b_stage = b_base + s * K::B_BYTES;
+#pragma unroll 1
+            for (int i0 = 0; i0 < (stopped ? 0 : KC * (C / 4)); i0 += 8 * GATHER_THREADS) {
+                float4 v[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    const int i = i0 + u * GATHER_THREADS + gtid, k = i / (C / 4), j = i % (C / 4);
+                    v[u] = k < cnt ? __ldg(reinterpret_cast<const float4*>(features + (size_t)ch.id[k] * C) + j)
+                                   : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                }
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    const int i = i0 + u * GATHER_THREADS + gtid, k = i / (C / 4), j = i % (C / 4);
+                    const uint32_t off = (k >> 2) * K::B_SBO + (j >> 3) * 512 + (k & 3) * 128 +
+                                         ((((j & 7) >> 1) ^ (k & 3)) << 5) + (j & 1) * 16;
+                    st_shared_v4f(b_stage + off, make_float4(tc::to_tf32(v[u].x), tc::to_tf32(v[u].y),
+                                                             tc::to_tf32(v[u].z), tc::to_tf32(v[u].w)));
+                }
+            }
+            tc::fence_proxy_async();
+            tc::group_sync<GATHER_BAR>(GATHER_THREADS);
+            if (gtid == 0) tc::mbar_arrive(&s_b_full[s]);
+        }
+    } else if (role == Role::Mma) {
+        // ---------------------------------------------------------------- MMA warp (one lane)
+        if (lane == 0) {
+            int committed = 0;
+            bool issued = false;  // has any MMA written the accumulators?
+            for (int c = 0;; c++) {
+                const int s = c % S, slot = c % LIST_SLOTS;
+                bool ok = !*(volatile int*)&s_fail &&
+                          tc::mbar_wait_bounded(&s_list_full[slot], (c / LIST_SLOTS) & 1, WAIT_LIMIT);
+                if (ok && s_list[slot].count == 0) break;
+                ok = ok && tc::mbar_wait_bounded(&s_a_full[s], (c / S) & 1, WAIT_LIMIT) &&
+                     tc::mbar_wait_bounded(&s_b_full[s], (c / S) & 1, WAIT_LIMIT);
+                if (!ok) {
+                    s_fail = 1;
+                    break;
+                }
+                tc::fence_after_sync();
+                const uint32_t a_stage = a_base + s * K::A_BYTES, b_stage = b_base + s * K::B_BYTES;
+                const bool skip = *(volatile int*)&s_skip[s];
+#pragma unroll
+                for (int ks = 0; ks < (skip ? 0 : KC / 8); ks++) {
+#pragma unroll
+                    for (int nb = 0; nb < K::N_BLOCKS; nb++) {
+                        const uint64_t ad = tc::smem_desc(a_stage + ks * 2 * K::A_LBO, K::A_LBO, 128);
+                        // MN-major, 128-byte swizzle on 32-byte atoms (layout type 1): LBO between
+                        // 32-channel atoms, SBO between 4-entry atoms.
+                        const uint64_t bd = tc::smem_desc(b_stage + ks * 2 * K::B_SBO + nb * (K::N_MMA / 32) * 512, 512,
+                                                          K::B_SBO) |
+                                            (1ull << 61);
+                        tc::mma_tf32(tmem + nb * K::N_MMA, ad, bd, K::IDESC, (issued || ks > 0) ? 1u : 0u);
+                    }
+                }
+                issued = issued || !skip;
+                tc::commit(&s_mma_done[s]);  // also when skipped: the stage's phase must advance
+                committed = c + 1;
+                // Pixels and gathers are done with the chunk's list slot once its MMAs are issued.
+                tc::mbar_arrive(&s_list_free[slot]);
+            }
+            bool ok = committed == 0 ||
+                      tc::mbar_wait_bounded(&s_mma_done[(committed - 1) % S], ((committed - 1) / S) & 1, WAIT_LIMIT);
+            if (!ok) s_fail = 1;
+            s_have = issued && ok;
+            tc::fence_before_sync();
+            tc::mbar_arrive(&s_acc_ready);
+        }
+    } else {  // Role::Pixel
+        // ---------------------------------------------------------------- pixel warps
+        const int quad = warp & 3, half16 = warp >> 2, part = lane >> 4;
+        const int p = quad * 32 + half16 * 16 + (lane & 15);
+        const int2 lp = half_tile_pixel(p);
+        const int px = x0 + lp.x, py = y0 + lp.y;
+        const bool inside = px < width && py < height;
+        const float cx = (float)px + 0.5f, cy = (float)py + 0.5f;
+        const float wx0 = (float)(x0 + (quad & 1) * 8) + 0.5f, wx1 = wx0 + 7.0f;
+        const float wy0 = (float)(y0 + (quad >> 1) * 4 + half16 * 2) + 0.5f, wy1 = wy0 + 1.0f;
+        const bool rgb = image4 != nullptr;
+        float T = 1.0f, ar = 0.0f, ag = 0.0f, ab = 0.0f;
+        int last = 0;
+        bool done = !inside;
+        bool all_done = false;  // every pixel finished before the current chunk (uniform)
+        for (int c = 0;; c++) {
+            const int s = c % S, slot = c % LIST_SLOTS;
+            const List& ch = s_list[slot];
+            bool bad = false;
+            if (tid == 0) {
+                bad = *(volatile int*)&s_fail ||
+                      !tc::mbar_wait_bounded(&s_list_full[slot], (c / LIST_SLOTS) & 1, WAIT_LIMIT);
+                // The A stage is free once chunk c - S's MMAs have read it.
+                if (!bad && ch.count > 0 && c >= S)
+                    bad = !tc::mbar_wait_bounded(&s_mma_done[s], ((c - S) / S) & 1, WAIT_LIMIT);
+                if (bad) s_fail = 1;
+            }
+            if (tc::group_sync_count<PIX_BAR>(bad, PIXEL_THREADS) != 0) break;
+            const int cnt = ch.count;
+            if (cnt == 0) break;
+            // A row of pixel p: K-quad q at q*A_LBO + (p/8)*128 + (p%8)*16; this thread owns quad 2g + part
+            // of group g.
+            const uint32_t a_row = a_base + s * K::A_BYTES + (p >> 3) * 128 + (p & 7) * 16;
+#pragma unroll 1
+            for (int k0 = 0; k0 < (all_done ? 0 : KC); k0 += 8) {
+                const int kb = k0 + 4 * part;
+                float w_own[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                bool hit[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    hit[i] = kb + i < cnt && box_hits(ch.mean[kb + i], ch.ext[kb + i], wx0, wx1, wy0, wy1);
+                const bool any = __any_sync(FULL_MASK, hit[0] || hit[1] || hit[2] || hit[3]);
+                if (any && !__all_sync(FULL_MASK, done)) {  // uniform per warp
+                    float a_own[4];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float4 q = ch.conic[kb + i];
+                        const float2 m = ch.mean[kb + i];
+                        const PairAlpha pa = pair_alpha(cx, cy, m.x, m.y, q.x, q.y, q.z, q.w);
+                        const float alpha = fminf(MAX_ALPHA, pa.raw);
+                        a_own[i] = hit[i] && alpha >= MIN_ALPHA ? alpha : 0.0f;
+                    }
+                    float a8[8];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float a_p = __shfl_xor_sync(FULL_MASK, a_own[i], 16);
+                        a8[i] = part ? a_p : a_own[i];
+                        a8[i + 4] = part ? a_own[i] : a_p;
+                    }
+                    // The walk of the oracle, in list order (both threads of the pixel run it).
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        if (a8[i] > 0.0f && !done) {
+                            const float test = T * (1.0f - a8[i]);
+                            if (test < MIN_T) {
+                                done = true;
+                            } else {
+                                const float w = a8[i] * T;
+                                if (rgb) {
+                                    const float4 col = ch.col[k0 + i];
+                                    ar = fmaf(w, col.x, ar);
+                                    ag = fmaf(w, col.y, ag);
+                                    ab = fmaf(w, col.z, ab);
+                                }
+                                T = test;
+                                last = ch.pos[k0 + i] + 1;
+                                if ((i >> 2) == part) w_own[i & 3] = w;
+                            }
+                        }
+                    }
+                }
+                st_shared_v4f(a_row + ((k0 >> 2) + part) * K::A_LBO,
+                              make_float4(tc::to_tf32(w_own[0]), tc::to_tf32(w_own[1]), tc::to_tf32(w_own[2]),
+                                          tc::to_tf32(w_own[3])));
+            }
+            tc::fence_proxy_async();
+            // Every pixel thread has written its A quads (none when all were done before the chunk:
+            // then its MMAs are skipped); tell the list and gather warps when all pixels are done.
+            const bool was_done = all_done;
+            all_done = tc::group_sync_count<PIX_BAR>(done, PIXEL_THREADS) == PIXEL_THREADS;
+            if (tid == 0) {
+                s_skip[s] = was_done;
+                if (all_done && !was_done) *(volatile int*)&s_zero_from = c + 1;
+                tc::mbar_arrive(&s_a_full[s]);
+            }
+        }
+
+        // Epilogue: once the last MMA has completed, warp w drains TMEM lanes of quadrant w & 3
+        // (lane = pixel), columns [half16 * C/2, (half16 + 1) * C/2).
+        bool ok = false;
+        if (tid == 0) ok = tc::mbar_wait_bounded(&s_acc_ready, 0, WAIT_LIMIT) && *(volatile int*)&s_have;
+        const bool have = tc::group_sync_count<PIX_BAR>(ok, PIXEL_THREADS) != 0;
+        tc::fence_after_sync();
+        {
+            const int pe = quad * 32 + lane;
+            const int2 le = half_tile_pixel(pe);
+            const int ex = x0 + le.x, ey = y0 + le.y;
+            const bool e_inside = ex < width && ey < height;
+            float* dst = feature_image + ((size_t)ey * width + ex) * C;
+            const uint32_t lane_addr = tmem + ((uint32_t)(quad * 32) << 16);
+#pragma unroll 1
+            for (int col = half16 * (C / 2); col < (half16 + 1) * (C / 2); col += 16) {
+                float v[16];
+                if (have) {
+                    tc::tmem_ld16(lane_addr + col, v);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; i++) v[i] = 0.0f;
+                }
+                if (e_inside) {
+#pragma unroll
+                    for (int i = 0; i < 16; i += 4)
+                        *reinterpret_cast<float4*>(dst + col + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                }
+            }
+        }
+        if (inside && part == 0) {
+            const size_t pix = (size_t)py * width + px;
+            final_T[pix] = T;
+            n_contrib[pix] = last;
+            if (rgb)
+                image4[pix] = make_float4(fmaf(T, background[0], ar), fmaf(T, background[1], ag),
+                                          fmaf(T, background[2], ab), 0.0f);
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) tc::tmem_dealloc(tmem, C);
+    if (tid == 0 && s_fail) atomicExch(&g_status, HDS_ERR_DEVICE);
+}
+
+template <int C>
+int launch_forward_ws(int width, int height, const int32_t* tile_ranges, const int32_t* values, const float* means2D,
+                      const float* conic4, const float* color_opacity, const float* features,
+                      const float* background, float* feature_image, float* final_T, int32_t* n_contrib,
+                      float* image4, cudaStream_t stream) {
+    auto kernel = feature_forward_ws_kernel<C>;
+    HDS_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<C>::SMEM));
+    int tx = tiles_for(width), ty = tiles_for(height);
+    kernel<<<2 * tx * ty, THREADS, Cfg<C>::SMEM, stream>>>(
+        width, height, tx, reinterpret_cast<const int2*>(tile_ranges), values, reinterpret_cast<const float2*>(means2D),
+        reinterpret_cast<const float4*>(conic4), reinterpret_cast<const float4*>(color_opacity), features, background,
+        feature_image, final_T, n_contrib, reinterpret_cast<float4*>(image4));
+    HDS_CHECK_LAUNCH("feature_forward_ws_kernel");
+    return HDS_OK;
+}
+
+}  // namespace ws
+
 template <int C>
 int launch_forward(int width, int height, const int32_t* tile_ranges, const int32_t* values, const float* means2D,
                    const float* conic4, const float* color_opacity, const float* features, const float* background,
@@ -391,8 +847,8 @@ extern "C" int hds_render_features_forward(int n, int channels, int width, int h
         case 32: return launch_forward<32>(width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, background, feature_image, final_T, n_contrib, image4, stream);
         case 64: return launch_forward<64>(width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, background, feature_image, final_T, n_contrib, image4, stream);
         case 128: return launch_forward<128>(width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, background, feature_image, final_T, n_contrib, image4, stream);
-        case 256: return launch_forward<256>(width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, background, feature_image, final_T, n_contrib, image4, stream);
-        case 512: return launch_forward<512>(width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, background, feature_image, final_T, n_contrib, image4, stream);
+        case 256: return ws::launch_forward_ws<256>(width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, background, feature_image, final_T, n_contrib, image4, stream);
+        case 512: return ws::launch_forward_ws<512>(width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, background, feature_image, final_T, n_contrib, image4, stream);
         default:
             set_error("features must have 32, 64, 128, 256 or 512 channels, got %d", channels);
             return HDS_ERR_UNSUPPORTED;
