@@ -41,7 +41,7 @@ struct FwdCfg {
     static constexpr int PIX = 128;
     static constexpr int THREADS = 256;
     static constexpr int KC = 32;
-    static constexpr int N_MMA = C < 256 ? C : 256;
+    static constexpr int N_MMA = 256;
     static constexpr int N_BLOCKS = C / N_MMA;
     static constexpr int TMEM_COLS = C;
     static constexpr int A_BYTES = PIX * KC * 4;
@@ -399,6 +399,9 @@ struct Cfg {
     static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + 1024;
     static constexpr uint32_t IDESC = tc::idesc_tf32(128, N_MMA, false, true);
     static_assert(C == 256 || C == 512, "the warp-specialised forward is for 256 or 512 channels");
+    // The gather's 8 x GATHER_THREADS item sweeps tile the chunk exactly (and the loop bound guards
+    // any other count as well).
+    static_assert((KC * (C / 4)) % (8 * GATHER_THREADS) == 0, "gather sweep must tile the chunk");
 };
 
 // One list slot: chunk entries in list order.
@@ -589,12 +592,14 @@ __global__ void __launch_bounds__(THREADS, 1) feature_forward_ws_kernel(
 #pragma unroll
                 for (int u = 0; u < 8; u++) {
                     const int i = i0 + u * GATHER_THREADS + gtid, k = i / (C / 4), j = i % (C / 4);
-                    v[u] = k < cnt ? __ldg(reinterpret_cast<const float4*>(features + (size_t)ch.id[k] * C) + j)
-                                   : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    v[u] = k < cnt && k < KC
+                               ? __ldg(reinterpret_cast<const float4*>(features + (size_t)ch.id[k] * C) + j)
+                               : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                 }
 #pragma unroll
                 for (int u = 0; u < 8; u++) {
                     const int i = i0 + u * GATHER_THREADS + gtid, k = i / (C / 4), j = i % (C / 4);
+                    if (k >= KC) continue;  // past the chunk: no slot of this stage
                     const uint32_t off = (k >> 2) * K::B_SBO + (j >> 3) * 512 + (k & 3) * 128 +
                                          ((((j & 7) >> 1) ^ (k & 3)) << 5) + (j & 1) * 16;
                     st_shared_v4f(b_stage + off, make_float4(tc::to_tf32(v[u].x), tc::to_tf32(v[u].y),
