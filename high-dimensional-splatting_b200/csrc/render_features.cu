@@ -41,8 +41,9 @@ struct FwdCfg {
     static constexpr int PIX = 128;
     static constexpr int THREADS = 256;
     static constexpr int KC = 32;
-    static constexpr int N_MMA = 256;
+    static constexpr int N_MMA = C < 256 ? C : 256;
     static constexpr int N_BLOCKS = C / N_MMA;
+    static_assert(N_BLOCKS >= 1 && N_BLOCKS * N_MMA == C, "the MMAs must cover every channel");
     static constexpr int TMEM_COLS = C;
     static constexpr int A_BYTES = PIX * KC * 4;
     static constexpr int B_BYTES = KC * C * 4;
@@ -392,6 +393,7 @@ struct Cfg {
     static constexpr int STAGES = C >= 512 ? 2 : 3;
     static constexpr int N_MMA = 256;
     static constexpr int N_BLOCKS = C / N_MMA;
+    static_assert(N_BLOCKS >= 1 && N_BLOCKS * N_MMA == C, "the MMAs must cover every channel");
     static constexpr int A_BYTES = 128 * KC * 4;  // K-major: (k/4)*A_LBO + (p/8)*128 + (p%8)*16 + (k%4)*4
     static constexpr int A_LBO = 2048;
     static constexpr int B_SBO = (C / 32) * 512;  // between atoms of 4 entries; atoms of 32 channels are 512 B apart

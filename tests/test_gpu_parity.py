@@ -99,6 +99,9 @@ def test_feature_forward(ext, golden, name, channels):
     t_in = cuda(*inputs, BACKGROUND)
     f = cuda(feats)[0]
     image, fimg, final_T, n_contrib, *_ = ext.rasterize_with_features(*t_in, f, w, h)
+    from hds_b200.native import device_status
+
+    assert device_status() == 0, "a bounded wait in the feature blend ran out"
     assert np.array_equal(host(image), want["image"]), "fused RGB differs"
     assert np.array_equal(host(final_T), want["final_T"]), "final_T differs"
     assert np.array_equal(host(n_contrib), want["n_contrib"]), "n_contrib differs"
