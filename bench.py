@@ -259,8 +259,11 @@ def roofline(name, ms_per_launch, stats, args, peaks, n):
         return {"bound": "tensor", "achieved": ach, "peak": tf32_peak, "unit": "TFLOP/s", "frac": ach / tf32_peak,
                 "traffic": None, "kernel": name,
                 "peak_note": f"TF32 dense = half the {peaks['source']} cuBLAS bf16 rate"}
-    if name in ("hds_render_features_backward", "hds_render_features_backward_accumulate"):
+    if name in ("hds_render_features_backward", "hds_render_features_backward_accumulate",
+                "hds_render_backward_fused"):
         nbytes = P * (4 * C + 12) + V * (4 * C + 32) + n * (4 * C + 36) * 2
+        if name == "hds_render_backward_fused":  # plus the RGB terms: dL/dimage, colours and their gradient
+            nbytes += P * 12 + n * 24
     elif name == "hds_render_backward":
         nbytes = P * (12 + 8) + V * 44 + n * 36 * 2
     else:

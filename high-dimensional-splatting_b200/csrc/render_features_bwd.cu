@@ -115,16 +115,18 @@ struct BwdChunk {
     float2 mean[KC];
     float2 ext[KC];
     float4 conic[KC];  // a, b, c, opacity
+    float4 col[KC];    // r, g, b, opacity (the RGB terms of slice 0)
     int count;
 };
 
-template <int CK>
+template <int CK, bool RGB>
 __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
     int C, int width, int height, int tiles_x, int slices, const int2* __restrict__ ranges,
     const int32_t* __restrict__ values, const float2* __restrict__ means2D, const float4* __restrict__ conic4,
     const float4* __restrict__ color_opacity, const float* __restrict__ features, const float* __restrict__ final_T_in,
     const int32_t* __restrict__ n_contrib, const float* __restrict__ grad_out, float* __restrict__ grad_means2D,
-    float* __restrict__ grad_conics, float* __restrict__ grad_features, float* __restrict__ grad_opacities) {
+    float* __restrict__ grad_conics, float* __restrict__ grad_features, float* __restrict__ grad_opacities,
+    const float* __restrict__ grad_image, const float* __restrict__ background, float* __restrict__ grad_colors) {
     using Cfg = BwdCfg<CK>;
     extern __shared__ uint8_t smem_raw[];
     __shared__ BwdChunk s_list[LIST_SLOTS];
@@ -132,9 +134,13 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
     __shared__ uint64_t s_list_full[LIST_SLOTS], s_list_free[LIST_SLOTS];
     __shared__ uint32_t s_tmem;
     __shared__ int s_fail;
+    __shared__ float s_gp[PIX][3];  // dL/dimage of the block's pixels (the RGB terms of slice 0)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int slice = blockIdx.x % slices;
+    // With grad_image, the first slice's blocks also carry the RGB backward: its dot is colour . dL/dpixel
+    // and its recurrence the same as the features' (backward.cu:7-164), plus the background term.
+    const bool rgb = RGB && slice == 0;
     const int half_id = blockIdx.x / slices;
     const int tile = half_id >> 1;
     const int c0 = slice * CK;
@@ -195,12 +201,13 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
         int top_b = top, id_b = fetch_id(top);
         top -= 32;
         float2 m_b = make_float2(0.0f, 0.0f);
-        float4 q_b = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        auto gather = [&](int g, float2& mm, float4& qq) {
+        float4 q_b = make_float4(0.0f, 0.0f, 0.0f, 0.0f), col_b = q_b;
+        auto gather = [&](int g, float2& mm, float4& qq, float4& cc) {
             if (g >= 0) {
                 mm = means2D[g];
                 const float4 cq = conic4[g];
-                qq = make_float4(cq.x, cq.y, cq.z, color_opacity[g].w);
+                cc = color_opacity[g];
+                qq = make_float4(cq.x, cq.y, cq.z, cc.w);
             }
         };
         // Prime: B <- first batch (gathered), A <- second batch.
@@ -210,11 +217,11 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
             id_a = id_b;
             top_b = t;
             id_b = i;
-            gather(id_b, m_b, q_b);
+            gather(id_b, m_b, q_b, col_b);
         }
         int top_c = 0, id_c = -1;
         float2 m_c = make_float2(0.0f, 0.0f), e_c = make_float2(0.0f, 0.0f);
-        float4 q_c = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        float4 q_c = make_float4(0.0f, 0.0f, 0.0f, 0.0f), col_c = q_c;
         unsigned mask_c = 0;
         bool more = top_b > 0;  // does batch B hold any position?
         for (int c = 0;; c++) {
@@ -238,14 +245,15 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
                     id_c = id_b;
                     m_c = m_b;
                     q_c = q_b;
+                    col_c = col_b;
                     e_c = id_c >= 0 ? cull_extent_fast(q_c.x, q_c.y, q_c.z, q_c.w) : make_float2(-1e30f, -1e30f);
                     mask_c = __ballot_sync(FULL_MASK, id_c >= 0 && box_hits(m_c, e_c, hx0, hx1, hy0, hy1));
                     more = top_a > 0;
                     top_b = top_a;
                     id_b = id_a;
                     m_b = make_float2(0.0f, 0.0f);
-                    q_b = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                    gather(id_b, m_b, q_b);
+                    q_b = col_b = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    gather(id_b, m_b, q_b, col_b);
                     top_a = top;
                     id_a = fetch_id(top);
                     top -= 32;
@@ -261,6 +269,7 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
                     ch.mean[k] = m_c;
                     ch.ext[k] = e_c;
                     ch.conic[k] = q_c;
+                    if (RGB) ch.col[k] = col_c;
                 }
                 // Clear the taken bits (the lowest `take` set bits: descending positions).
                 if (take == hits) {
@@ -376,6 +385,25 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
                     if (v[3] != 0.0f) atomicAdd(grad_conics + 3 * g, v[3]);
                     if (v[4] != 0.0f) atomicAdd(grad_conics + 3 * g + 1, v[4]);
                     if (v[5] != 0.0f) atomicAdd(grad_conics + 3 * g + 2, v[5]);
+                    if (rgb) {
+                        // dL/dcolour of the entry: sum over the warp's pixels of w dL/dpixel, with w read
+                        // back from the stage's W operand (bf16 hi + lo) before the dF transpose reuses it.
+                        const uint8_t* wb = smem + (w_hi(s) - g_hi) + (lane >> 3) * 2048 + (lane & 7) * 2 + q4 * 32 * 16;
+                        float cr = 0.0f, cg = 0.0f, cb = 0.0f;
+#pragma unroll 4
+                        for (int i = 0; i < 32; i++) {
+                            const uint32_t h = *reinterpret_cast<const uint16_t*>(wb + i * 16);
+                            const uint32_t l = *reinterpret_cast<const uint16_t*>(wb + W_BYTES + i * 16);
+                            const float w = __uint_as_float(h << 16) + __uint_as_float(l << 16);
+                            const float* gp = s_gp[q4 * 32 + i];
+                            cr = fmaf(w, gp[0], cr);
+                            cg = fmaf(w, gp[1], cg);
+                            cb = fmaf(w, gp[2], cb);
+                        }
+                        if (cr != 0.0f) atomicAdd(grad_colors + 3 * g, cr);
+                        if (cg != 0.0f) atomicAdd(grad_colors + 3 * g + 1, cg);
+                        if (cb != 0.0f) atomicAdd(grad_colors + 3 * g + 2, cb);
+                    }
                 }
                 // dF of the chunk: wait for its MMA, then drain TMEM (lane = channel).
                 if (otid == 0) {
@@ -513,8 +541,23 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
         const float wy0 = (float)(y0 + (quad >> 1) * 4 + half16 * 2) + 0.5f, wy1 = wy0 + 1.0f;
         const size_t pix = (size_t)py * width + px;
         float T = inside ? final_T_in[pix] : 0.0f;
+        const float fT = T;  // final transmittance: the background's weight
         const int last = inside ? n_contrib[pix] : 0;
-        float behind = 0.0f;
+        float behind = 0.0f, behind_rgb = 0.0f;
+        float gpr = 0.0f, gpg = 0.0f, gpb = 0.0f, bgdot = 0.0f;
+        if (rgb) {
+            if (inside) {
+                gpr = grad_image[3 * pix];
+                gpg = grad_image[3 * pix + 1];
+                gpb = grad_image[3 * pix + 2];
+            }
+            bgdot = fmaf(background[2], gpb, fmaf(background[1], gpg, background[0] * gpr));
+            if (part == 0) {
+                s_gp[p][0] = gpr;
+                s_gp[p][1] = gpg;
+                s_gp[p][2] = gpb;
+            }
+        }
         const uint32_t lane_base = (uint32_t)(quad * 32 + half16 * 16) << 16;
 
         for (int c = 0;; c++) {
@@ -582,7 +625,14 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
 #pragma unroll
                     for (int i = 0; i < 8; i++) {
                         T = T * r8[i];
-                        const float dL_dalpha = T * (d8[i] - behind);
+                        float dL_dalpha = T * (d8[i] - behind);
+                        if (rgb) {  // uniform per block
+                            const float4 col = ch.col[k0 + i];
+                            const float drgb = fmaf(col.z, gpb, fmaf(col.y, gpg, col.x * gpr));
+                            // The background is seen through T_final, which this entry's alpha scales.
+                            dL_dalpha += T * (drgb - behind_rgb) - fT * r8[i] * bgdot;
+                            behind_rgb = fmaf(a8[i], drgb, (1.0f - a8[i]) * behind_rgb);
+                        }
                         if ((i >> 2) == part) {  // this thread's entry: a select, not a branch
                             w_own[i & 3] = T * a8[i];
                             u_own[i & 3] = dL_dalpha * g_own[i & 3];
@@ -616,18 +666,61 @@ template <int CK>
 int launch_backward(int D, int width, int height, const int32_t* tile_ranges, const int32_t* values,
                     const float* means2D, const float* conic4, const float* color_opacity, const float* features,
                     const float* final_T, const int32_t* n_contrib, const float* grad_output, float* grad_features,
-                    float* grad_means2D, float* grad_conics, float* grad_opacities, cudaStream_t stream) {
+                    float* grad_means2D, float* grad_conics, float* grad_opacities, const float* grad_image,
+                    const float* background, float* grad_colors, cudaStream_t stream) {
     using Cfg = BwdCfg<CK>;
-    auto kernel = feature_backward_kernel<CK>;
+    auto kernel = grad_image != nullptr ? feature_backward_kernel<CK, true> : feature_backward_kernel<CK, false>;
     HDS_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
     const int tx = tiles_for(width), ty = tiles_for(height), slices = D / CK;
     kernel<<<2 * tx * ty * slices, THREADS, Cfg::SMEM, stream>>>(
         D, width, height, tx, slices, reinterpret_cast<const int2*>(tile_ranges), values,
         reinterpret_cast<const float2*>(means2D), reinterpret_cast<const float4*>(conic4),
         reinterpret_cast<const float4*>(color_opacity), features, final_T, n_contrib, grad_output, grad_means2D,
-        grad_conics, grad_features, grad_opacities);
+        grad_conics, grad_features, grad_opacities, grad_image, background, grad_colors);
     HDS_CHECK_LAUNCH("feature_backward_kernel");
     return HDS_OK;
+}
+
+}  // namespace
+
+namespace {
+
+// grad_image (with background and grad_colors) adds the RGB backward to the same walk; NULL leaves
+// it out (the reference's rasterize_features_backward).
+int features_backward(int n, int channels, int slice_width, int width, int height, const float* grad_output,
+                      const float* features, const float* means2D, const float* conic4, const float* color_opacity,
+                      const int32_t* values_sorted, const int32_t* tile_ranges, const float* final_T,
+                      const int32_t* n_contrib, float* grad_features, float* grad_means2D, float* grad_conics,
+                      float* grad_opacities, bool accumulate_features, const float* grad_image,
+                      const float* background, float* grad_colors, cudaStream_t stream) {
+    clear_error();
+    HDS_REQUIRE(n >= 0 && width > 0 && height > 0, HDS_ERR_INVALID, "rasterize_features_backward: bad sizes");
+    HDS_REQUIRE((int64_t)channels * width * height <= INT32_MAX, HDS_ERR_TOO_LARGE,
+                "a %dx%d image of %d channels overflows the feature kernels' int indices", width, height, channels);
+    // The (channels, slice) pairs the reference dispatches (features.cu:601-612).
+    const int D = channels, Wd = slice_width;
+    const bool supported = (D == 32 && Wd == 32) || (D == 64 && (Wd == 64 || Wd == 32)) ||
+                           (D == 128 && (Wd == 128 || Wd == 64 || Wd == 32)) || (D == 256 && (Wd == 128 || Wd == 64)) ||
+                           (D == 512 && (Wd == 128 || Wd == 64));
+    HDS_REQUIRE(supported, HDS_ERR_UNSUPPORTED, "no feature backward for %d channels in slices of %d", D, Wd);
+    HDS_REQUIRE(((uintptr_t)features & 15) == 0 && ((uintptr_t)grad_output & 15) == 0 &&
+                    ((uintptr_t)grad_features & 15) == 0,
+                HDS_ERR_INVALID, "rasterize_features_backward: features, grad_output and grad_features must be 16-byte aligned");
+    HDS_REQUIRE(grad_image == nullptr || (background != nullptr && grad_colors != nullptr), HDS_ERR_INVALID,
+                "rasterize_backward_fused: grad_image needs background and grad_colors");
+    if (n == 0) return HDS_OK;
+    if (!accumulate_features) HDS_CHECK_CUDA(cudaMemsetAsync(grad_features, 0, sizeof(float) * (size_t)n * D, stream));
+    HDS_CHECK_CUDA(cudaMemsetAsync(grad_means2D, 0, sizeof(float) * 2 * (size_t)n, stream));
+    HDS_CHECK_CUDA(cudaMemsetAsync(grad_conics, 0, sizeof(float) * 3 * (size_t)n, stream));
+    HDS_CHECK_CUDA(cudaMemsetAsync(grad_opacities, 0, sizeof(float) * (size_t)n, stream));
+    if (grad_image != nullptr) HDS_CHECK_CUDA(cudaMemsetAsync(grad_colors, 0, sizeof(float) * 3 * (size_t)n, stream));
+    // The slice width only selects the reference's kernel instantiation; the sums are the same for
+    // any slicing, and these kernels always take slices of min(channels, 128).
+    switch (D) {
+        case 32: return launch_backward<32>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);
+        case 64: return launch_backward<64>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);
+        default: return launch_backward<128>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);
+    }
 }
 
 }  // namespace
@@ -643,42 +736,6 @@ int read_and_clear_backward_status(int* status, cudaStream_t stream) {
 
 using namespace hds;
 
-namespace {
-
-int features_backward(int n, int channels, int slice_width, int width, int height, const float* grad_output,
-                      const float* features, const float* means2D, const float* conic4, const float* color_opacity,
-                      const int32_t* values_sorted, const int32_t* tile_ranges, const float* final_T,
-                      const int32_t* n_contrib, float* grad_features, float* grad_means2D, float* grad_conics,
-                      float* grad_opacities, bool accumulate_features, cudaStream_t stream) {
-    clear_error();
-    HDS_REQUIRE(n >= 0 && width > 0 && height > 0, HDS_ERR_INVALID, "rasterize_features_backward: bad sizes");
-    HDS_REQUIRE((int64_t)channels * width * height <= INT32_MAX, HDS_ERR_TOO_LARGE,
-                "a %dx%d image of %d channels overflows the feature kernels' int indices", width, height, channels);
-    // The (channels, slice) pairs the reference dispatches (features.cu:601-612).
-    const int D = channels, Wd = slice_width;
-    const bool supported = (D == 32 && Wd == 32) || (D == 64 && (Wd == 64 || Wd == 32)) ||
-                           (D == 128 && (Wd == 128 || Wd == 64 || Wd == 32)) || (D == 256 && (Wd == 128 || Wd == 64)) ||
-                           (D == 512 && (Wd == 128 || Wd == 64));
-    HDS_REQUIRE(supported, HDS_ERR_UNSUPPORTED, "no feature backward for %d channels in slices of %d", D, Wd);
-    HDS_REQUIRE(((uintptr_t)features & 15) == 0 && ((uintptr_t)grad_output & 15) == 0 &&
-                    ((uintptr_t)grad_features & 15) == 0,
-                HDS_ERR_INVALID, "rasterize_features_backward: features, grad_output and grad_features must be 16-byte aligned");
-    if (n == 0) return HDS_OK;
-    if (!accumulate_features) HDS_CHECK_CUDA(cudaMemsetAsync(grad_features, 0, sizeof(float) * (size_t)n * D, stream));
-    HDS_CHECK_CUDA(cudaMemsetAsync(grad_means2D, 0, sizeof(float) * 2 * (size_t)n, stream));
-    HDS_CHECK_CUDA(cudaMemsetAsync(grad_conics, 0, sizeof(float) * 3 * (size_t)n, stream));
-    HDS_CHECK_CUDA(cudaMemsetAsync(grad_opacities, 0, sizeof(float) * (size_t)n, stream));
-    // The slice width only selects the reference's kernel instantiation; the sums are the same for
-    // any slicing, and these kernels always take slices of min(channels, 128).
-    switch (D) {
-        case 32: return launch_backward<32>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, stream);
-        case 64: return launch_backward<64>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, stream);
-        default: return launch_backward<128>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, stream);
-    }
-}
-
-}  // namespace
-
 extern "C" int hds_render_features_backward(int n, int channels, int slice_width, int width, int height,
                                             const float* grad_output, const float* features, const float* means2D,
                                             const float* conic4, const float* color_opacity,
@@ -688,7 +745,7 @@ extern "C" int hds_render_features_backward(int n, int channels, int slice_width
                                             hds_stream_t stream) {
     return features_backward(n, channels, slice_width, width, height, grad_output, features, means2D, conic4,
                              color_opacity, values_sorted, tile_ranges, final_T, n_contrib, grad_features,
-                             grad_means2D, grad_conics, grad_opacities, false, stream);
+                             grad_means2D, grad_conics, grad_opacities, false, nullptr, nullptr, nullptr, stream);
 }
 
 extern "C" int hds_render_features_backward_accumulate(int n, int channels, int slice_width, int width, int height,
@@ -701,5 +758,19 @@ extern "C" int hds_render_features_backward_accumulate(int n, int channels, int 
                                                        hds_stream_t stream) {
     return features_backward(n, channels, slice_width, width, height, grad_output, features, means2D, conic4,
                              color_opacity, values_sorted, tile_ranges, final_T, n_contrib, grad_features,
-                             grad_means2D, grad_conics, grad_opacities, true, stream);
+                             grad_means2D, grad_conics, grad_opacities, true, nullptr, nullptr, nullptr, stream);
+}
+
+extern "C" int hds_render_backward_fused(int n, int channels, int width, int height, const float* grad_image,
+                                         const float* background, const float* grad_feature_image,
+                                         const float* features, const float* means2D, const float* conic4,
+                                         const float* color_opacity, const int32_t* values_sorted,
+                                         const int32_t* tile_ranges, const float* final_T, const int32_t* n_contrib,
+                                         float* grad_colors, float* grad_features, float* grad_means2D,
+                                         float* grad_conics, float* grad_opacities, int accumulate_features,
+                                         hds_stream_t stream) {
+    return features_backward(n, channels, channels < 128 ? channels : 128, width, height, grad_feature_image, features,
+                             means2D, conic4, color_opacity, values_sorted, tile_ranges, final_T, n_contrib,
+                             grad_features, grad_means2D, grad_conics, grad_opacities, accumulate_features != 0,
+                             grad_image, background, grad_colors, stream);
 }

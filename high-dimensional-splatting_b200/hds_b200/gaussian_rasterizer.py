@@ -182,6 +182,41 @@ def rasterize_features_backward_into(grad_features, grad_output, features, means
     return gm, gc, go
 
 
+def rasterize_backward_fused(grad_image, background, grad_feature_image, features, means2D, conic, color_opacity,
+                             values_sorted, tile_ranges, final_transmittance, n_contrib, image_width: int,
+                             image_height: int, grad_features_into=None):
+    """The RGB and feature backward in one walk (no counterpart in the reference, which runs
+    rasterize_backward and rasterize_features_backward).  grad_image may be None (no RGB terms).
+    grad_features_into, if given, is an [N, D] fp32 buffer that dL/dfeatures is added to.
+
+    Returns (dL/dmeans2D [N,2], dL/dconics [N,3], dL/dcolors [N,3] or None, dL/dopacities [N,1],
+    dL/dfeatures [N,D] or None when added into grad_features_into)."""
+    if not (grad_feature_image.is_cuda and grad_feature_image.is_contiguous()):
+        raise RuntimeError("grad_feature_image must be a contiguous CUDA tensor")
+    if grad_image is not None and not grad_image.is_contiguous():
+        raise RuntimeError("grad_image must be contiguous")
+    n, d = features.shape
+    dev = features.device
+    if grad_features_into is not None:
+        if not (grad_features_into.is_contiguous() and grad_features_into.dtype == _F32
+                and tuple(grad_features_into.shape) == (n, d) and grad_features_into.device == dev):
+            raise RuntimeError("grad_features_into must be a contiguous float32 tensor shaped like features")
+        gf, accumulate = grad_features_into, 1
+    else:
+        gf, accumulate = torch.empty(n, d, dtype=_F32, device=dev), 0
+    gm = torch.empty(n, 2, dtype=_F32, device=dev)
+    gc = torch.empty(n, 3, dtype=_F32, device=dev)
+    go = torch.empty(n, 1, dtype=_F32, device=dev)
+    gcol = torch.empty(n, 3, dtype=_F32, device=dev) if grad_image is not None else None
+    check(lib.hds_render_backward_fused(
+        n, d, int(image_width), int(image_height), ptr(grad_image) if grad_image is not None else None,
+        ptr(background) if grad_image is not None else None, ptr(grad_feature_image), ptr(features), ptr(means2D),
+        ptr(conic), ptr(color_opacity), ptr(values_sorted), ptr(tile_ranges), ptr(final_transmittance),
+        ptr(n_contrib), ptr(gcol) if gcol is not None else None, ptr(gf), ptr(gm), ptr(gc), ptr(go), accumulate,
+        stream_of(dev)))
+    return gm, gc, gcol, go, (None if accumulate else gf)
+
+
 def eval_sh(sh_dc, sh_rest, dirs, degree: int, radii):
     """sh.cu:157-168.  Returns rgb [N,3]."""
     n = sh_dc.shape[0]

@@ -36,6 +36,7 @@ SIGNATURES = {
     "hds_render_features_backward": [c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, P, P, S],
     "hds_render_features_backward_accumulate": [c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, P,
                                                 P, S],
+    "hds_render_backward_fused": [c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, c_int, S],
     "hds_ssim_forward": [c_int, c_int, P, P, P, P, P, P, S],
     "hds_ssim_backward": [c_int, c_int, P, P, P, P, P, P, P, S],
     "hds_device_status": [ctypes.POINTER(c_int), S],

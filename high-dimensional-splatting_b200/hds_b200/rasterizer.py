@@ -11,8 +11,9 @@ import torch
 
 from . import gaussian_rasterizer as _ext
 
-# Channels each feature backward block owns; None takes the widest slice, at most 128
-# (the reference's __init__.py:11-12, 158).
+# Channels each feature backward block owns (the reference's __init__.py:11-12, 158); None takes the
+# widest slice, at most 128.  The slicing does not change the sums; up to 128 channels the fused
+# backward (one slice) is used regardless.
 FEATURE_SLICE_WIDTH: int | None = None
 
 # When true, the backward of a rasterize call whose features are a leaf that already holds a
@@ -76,36 +77,57 @@ class RasterizeGaussians(torch.autograd.Function):
         width, height = ctx.image_size
         ext = _get_rasterizer()
         means2D = means2D.contiguous()
+        # Frozen features still shape the geometry gradients (the reference's __init__.py:150-153).
+        if features is not None and grad_features is not None and any(ctx.needs_input_grad[i] for i in (0, 3, 5, 7)):
+            # One walk for both backward passes (the reference runs two); the forward was fused too.
+            leaf = getattr(ctx, "features_leaf", None)
+            target = leaf.grad if (leaf is not None and ctx.needs_input_grad[7]) else None
+            if not (target is not None and target.is_contiguous() and target.dtype == torch.float32
+                    and target.shape == features.shape and target.device == features.device
+                    and target.data_ptr() % 16 == 0):
+                target = None
+            if features.shape[1] <= 128:
+                # One channel slice: the RGB terms ride along in the same walk (one pass instead of two).
+                with torch.cuda.nvtx.range("rasterize_backward_fused"):
+                    grad_means2D, grad_conics, grad_colors, grad_opacities, grad_feats = ext.rasterize_backward_fused(
+                        grad_image.contiguous() if grad_image is not None else None, background,
+                        grad_features.contiguous(), features, means2D, conic, color_opacity, values, ranges,
+                        feature_T, feature_contrib, width, height, grad_features_into=target)
+                if grad_colors is None:
+                    grad_colors = torch.zeros(means2D.shape[0], 3, device=means2D.device)
+            else:
+                # Several slices: only one would carry the RGB terms and their blocks would lengthen the
+                # walk more than the separate RGB pass costs.
+                if grad_image is None:
+                    grad_image = torch.zeros(height, width, 3, device=means2D.device)
+                with torch.cuda.nvtx.range("rasterize_backward"):
+                    grad_means2D, grad_conics, grad_colors, grad_opacities = ext.rasterize_backward(
+                        grad_image.contiguous(), means2D, conic, color_opacity, values, ranges, final_T, n_contrib,
+                        background, width, height)
+                slice_width = FEATURE_SLICE_WIDTH or min(features.shape[1], 128)
+                with torch.cuda.nvtx.range("rasterize_features_backward"):
+                    if target is not None:
+                        f_means2D, f_conics, f_opacities = ext.rasterize_features_backward_into(
+                            target, grad_features.contiguous(), features, means2D, conic, color_opacity, values,
+                            ranges, feature_T, feature_contrib, width, height, slice_width)
+                        grad_feats = None
+                    else:
+                        grad_feats, f_means2D, f_conics, f_opacities = ext.rasterize_features_backward(
+                            grad_features.contiguous(), features, means2D, conic, color_opacity, values, ranges,
+                            feature_T, feature_contrib, width, height, slice_width)
+                grad_means2D += f_means2D
+                grad_conics += f_conics
+                grad_opacities += f_opacities
+            if not ctx.needs_input_grad[7]:
+                grad_feats = None
+            return grad_means2D, None, None, grad_conics, grad_colors, grad_opacities, None, grad_feats, None, None
         if grad_image is None:
             grad_image = torch.zeros(height, width, 3, device=means2D.device)
         with torch.cuda.nvtx.range("rasterize_backward"):
             grad_means2D, grad_conics, grad_colors, grad_opacities = ext.rasterize_backward(
                 grad_image.contiguous(), means2D, conic, color_opacity, values, ranges, final_T, n_contrib,
                 background, width, height)
-        grad_feats = None
-        # Frozen features still shape the geometry gradients (the reference's __init__.py:150-153).
-        if features is not None and grad_features is not None and any(ctx.needs_input_grad[i] for i in (0, 3, 5, 7)):
-            slice_width = FEATURE_SLICE_WIDTH or min(features.shape[1], 128)
-            leaf = getattr(ctx, "features_leaf", None)
-            target = leaf.grad if (leaf is not None and ctx.needs_input_grad[7]) else None
-            if (target is not None and target.is_contiguous() and target.dtype == torch.float32
-                    and target.shape == features.shape and target.device == features.device
-                    and target.data_ptr() % 16 == 0):
-                with torch.cuda.nvtx.range("rasterize_features_backward"):
-                    f_means2D, f_conics, f_opacities = ext.rasterize_features_backward_into(
-                        target, grad_features.contiguous(), features, means2D, conic, color_opacity, values, ranges,
-                        feature_T, feature_contrib, width, height, slice_width)
-            else:
-                with torch.cuda.nvtx.range("rasterize_features_backward"):
-                    grad_feats, f_means2D, f_conics, f_opacities = ext.rasterize_features_backward(
-                        grad_features.contiguous(), features, means2D, conic, color_opacity, values, ranges,
-                        feature_T, feature_contrib, width, height, slice_width)
-                if not ctx.needs_input_grad[7]:
-                    grad_feats = None
-            grad_means2D += f_means2D
-            grad_conics += f_conics
-            grad_opacities += f_opacities
-        return grad_means2D, None, None, grad_conics, grad_colors, grad_opacities, None, grad_feats, None, None
+        return grad_means2D, None, None, grad_conics, grad_colors, grad_opacities, None, None, None, None
 
 
 def rasterize(means2D: torch.Tensor, depths: torch.Tensor, radii: torch.Tensor, conics: torch.Tensor,

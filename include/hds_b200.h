@@ -170,6 +170,24 @@ int hds_render_features_backward_accumulate(int n, int channels, int slice_width
                                             float* grad_means2D, float* grad_conics, float* grad_opacities,
                                             hds_stream_t stream);
 
+/* The RGB backward and the feature backward in one walk of the lists; no counterpart in the
+ * reference, which runs rasterize_backward (backward.cu:7-164) and rasterize_features_backward
+ * (features.cu:350-616) as two passes over the same lists.  Valid when the forward was the fused
+ * one (hds_render_features_forward with image4), so both share final_T and n_contrib.
+ *  - grad_image [H,W,3] with background [3]: the RGB terms; NULL leaves them out (then grad_colors
+ *    is not touched and may be NULL).
+ *  - grad_feature_image [H,W,C]: the feature terms; channels as hds_render_features_backward.
+ *  - Outputs dL/dcolors [n,3], dL/dfeatures [n,C] (added to the buffer when accumulate_features is
+ *    non-zero, otherwise overwritten), dL/dmeans2D [n,2], dL/dconics [n,3], dL/dopacities [n]: the
+ *    sums of both passes. */
+int hds_render_backward_fused(int n, int channels, int width, int height, const float* grad_image,
+                              const float* background, const float* grad_feature_image, const float* features,
+                              const float* means2D, const float* conic4, const float* color_opacity,
+                              const int32_t* values_sorted, const int32_t* tile_ranges, const float* final_T,
+                              const int32_t* n_contrib, float* grad_colors, float* grad_features,
+                              float* grad_means2D, float* grad_conics, float* grad_opacities,
+                              int accumulate_features, hds_stream_t stream);
+
 /* ---------------------------------------------------------------------------------------------
  * SSIM (11x11 gaussian window, sigma 1.5).  Replace ssim_forward (ssim.cu:306-338) and
  * ssim_backward (ssim.cu:340-367); glue utils/loss.py:57-90.  Images [H,W,3]; grad_mean is a

@@ -151,6 +151,40 @@ def test_feature_backward(ext, golden, name, channels, slice_width):
         assert_grads_close(host(g), wv, nm)
 
 
+@pytest.mark.parametrize("channels", [32, 128, 512])
+@pytest.mark.parametrize("name", ["raster_ref_scene", "raster_config0", "dense_tile", "size3", "config1_20k"])
+@pytest.mark.parametrize("with_rgb", [True, False])
+def test_fused_backward(ext, golden, name, channels, with_rgb):
+    """hds_render_backward_fused: the RGB and feature backward in one walk, against the oracle run with
+    both gradients at once (and with the feature terms alone)."""
+    inputs, w, h = case(name, golden)
+    m2, dep, rad, con, col, opac = inputs
+    feats = features_for(len(dep), channels)
+    rng = np.random.default_rng(11)
+    grad_f = rng.random((h, w, channels), dtype=np.float32)
+    grad_i = rng.random((h, w, 3), dtype=np.float32) if with_rgb else None
+    want = oracle.rasterize(*inputs, w, h, background=BACKGROUND, features=feats)
+    gm, gc, gcol, go, gf = oracle.render_backward(want["ranges"], want["values"], m2, con, col, opac, w, h,
+                                                  want["final_T"], want["n_contrib"], grad_image=grad_i,
+                                                  background=BACKGROUND, features=feats, grad_features=grad_f)
+    t_in = cuda(*inputs, BACKGROUND)
+    f = cuda(feats)[0]
+    _, _, final_T, n_contrib, values, ranges, conic, co = ext.rasterize_with_features(*t_in, f, w, h)
+    got_m, got_c, got_col, got_o, got_f = ext.rasterize_backward_fused(
+        cuda(grad_i)[0] if with_rgb else None, t_in[6], cuda(grad_f)[0], f, t_in[0], conic, co, values, ranges,
+        final_T, n_contrib, w, h)
+    from hds_b200.native import device_status
+
+    assert device_status() == 0, "a bounded wait in the feature backward ran out"
+    for nm, g, wv in zip(("features", "means2D", "conics", "opacities"), (got_f, got_m, got_c, got_o),
+                         (gf, gm, gc, go)):
+        assert_grads_close(host(g), wv, nm)
+    if with_rgb:
+        assert_grads_close(host(got_col), gcol, "colors")
+    else:
+        assert got_col is None
+
+
 def test_unsupported_widths_are_rejected(ext, golden):
     inputs, w, h = case("raster_ref_scene", golden)
     t_in = cuda(*inputs, BACKGROUND)
