@@ -114,6 +114,22 @@ __device__ __forceinline__ PairAlpha pair_alpha(float px, float py, float mx, fl
     return r;
 }
 
+// pair_alpha with the hardware exponential (__expf, ~2 ulp) instead of expf_det, for the backward
+// walks: they compare within tolerance, and only a pair exactly on the MIN_ALPHA cutoff can change
+// side.  The forward walks, whose outputs are bit-exact against the CPU oracle, keep pair_alpha.
+__device__ __forceinline__ PairAlpha pair_alpha_fast(float px, float py, float mx, float my, float a, float b,
+                                                     float c, float opacity) {
+    PairAlpha r;
+    r.dx = __fsub_rn(px, mx);
+    r.dy = __fsub_rn(py, my);
+    float t1 = fmaf(b, r.dy, __fmul_rn(a, r.dx));
+    float t2 = fmaf(c, r.dy, __fmul_rn(b, r.dx));
+    float maha = fmaf(r.dy, t2, __fmul_rn(r.dx, t1));
+    r.G = __expf(__fmul_rn(-0.5f, maha));
+    r.raw = __fmul_rn(opacity, r.G);
+    return r;
+}
+
 // Conservative half-widths of the box where alpha can reach MIN_ALPHA: the binning extent widened
 // by 0.1% + 0.01 px so rounding never culls a pair the walk would blend (the reference's
 // features.cu:8-17).  Opacity <= MIN_ALPHA never blends (negative extent: hits nothing); a
