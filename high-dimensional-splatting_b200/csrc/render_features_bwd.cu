@@ -116,6 +116,7 @@ struct BwdChunk {
     float2 ext[KC];
     float4 conic[KC];  // a, b, c, opacity
     float4 col[KC];    // r, g, b, opacity (the RGB terms of slice 0)
+    unsigned warp_hits[8];  // bit k: entry k's box touches the 8 x 2 pixel block of pixel warp w
     int count;
 };
 
@@ -281,6 +282,21 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
                 filled += take;
             }
             if (lane == 0) ch.count = filled;
+            __syncwarp();
+            // Which entries touch each pixel warp's 8 x 2 block (the pixel warps skip the others).
+            {
+                const bool valid = lane < filled;
+                const float2 m = valid ? ch.mean[lane] : make_float2(0.0f, 0.0f);
+                const float2 e = valid ? ch.ext[lane] : make_float2(-1e30f, -1e30f);
+#pragma unroll
+                for (int w = 0; w < 8; w++) {
+                    const float bx0 = (float)(x0 + (w & 1) * 8) + 0.5f;
+                    const float by0 = (float)(y0 + ((w & 3) >> 1) * 4 + (w >> 2) * 2) + 0.5f;
+                    const unsigned mask =
+                        __ballot_sync(FULL_MASK, valid && box_hits(m, e, bx0, bx0 + 7.0f, by0, by0 + 1.0f));
+                    if (lane == 0) ch.warp_hits[w] = mask;
+                }
+            }
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&s_list_full[slot]);
             if (filled == 0) break;  // the empty chunk ends the list
@@ -537,8 +553,6 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
         const int px = x0 + lp.x, py = y0 + lp.y;
         const bool inside = px < width && py < height;
         const float cx = (float)px + 0.5f, cy = (float)py + 0.5f;
-        const float wx0 = (float)(x0 + (quad & 1) * 8) + 0.5f, wx1 = wx0 + 7.0f;
-        const float wy0 = (float)(y0 + (quad >> 1) * 4 + half16 * 2) + 0.5f, wy1 = wy0 + 1.0f;
         const size_t pix = (size_t)py * width + px;
         float T = inside ? final_T_in[pix] : 0.0f;
         const float fT = T;  // final transmittance: the background's weight
@@ -584,6 +598,7 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
             // half of the group's W block (bf16 hi + lo) and its u quad; the geometric partials
             // leave as u = dL/dalpha * G, summed by the operand warps.
             const uint32_t wh = w_hi(s), wl = wh + W_BYTES, ub = u_base(s) + p * 16;
+            const unsigned hits_w = ch.warp_hits[warp];  // entries whose box touches this warp's pixels
 #pragma unroll 1
             for (int k0 = 0; k0 < cnt; k0 += 8) {
                 const int kb = k0 + 4 * part;  // this thread's four entries
@@ -591,10 +606,9 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
                 tc::tmem_ld16x2_4(tmem + lane_base + s * 32 + k0, d_own);
                 bool hit[4];
 #pragma unroll
-                for (int i = 0; i < 4; i++)
-                    hit[i] = kb + i < cnt && box_hits(ch.mean[kb + i], ch.ext[kb + i], wx0, wx1, wy0, wy1);
+                for (int i = 0; i < 4; i++) hit[i] = (hits_w >> (kb + i)) & 1u;
                 float w_own[4] = {0.0f, 0.0f, 0.0f, 0.0f}, u_own[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                if (__any_sync(FULL_MASK, hit[0] || hit[1] || hit[2] || hit[3])) {  // uniform per warp
+                if ((hits_w >> k0) & 0xFFu) {  // uniform per warp
                     float a_own[4], r_own[4], g_own[4];
 #pragma unroll
                     for (int i = 0; i < 4; i++) {
