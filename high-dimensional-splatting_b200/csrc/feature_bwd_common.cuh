@@ -1,0 +1,177 @@
+// feature_bwd_common.cuh -- pieces shared by the two feature-backward kernels (one block per
+// half tile and channel slice, and the four-block cluster that walks each half tile once): the
+// chunk of list entries a list warp hands to the walk, the bf16 hi + lo split of the tensor-core
+// operands, and the list warp itself.
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include "hds_common.cuh"
+#include "tcgen05.cuh"
+
+namespace hds {
+namespace fbwd {
+
+constexpr uint32_t WAIT_LIMIT = 1u << 22;
+constexpr int KC = 32;         // list entries per chunk (the N of both MMAs)
+constexpr int PIX = 128;       // pixels per half tile (the TMEM lanes of the dot)
+constexpr int LIST_SLOTS = 6;  // list ring: the list warp runs up to three chunks past the operand stages
+
+// (a, b) -> bf16x2 hi and lo with a in the low half: a = hi.x + lo.x + O(2^-17 a).
+__device__ __forceinline__ void split_bf16(float a, float b, uint32_t& hi, uint32_t& lo) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    float2 hf = __bfloat1622float2(h);
+    __nv_bfloat162 l = __floats2bfloat162_rn(__fsub_rn(a, hf.x), __fsub_rn(b, hf.y));
+    hi = *reinterpret_cast<uint32_t*>(&h);
+    lo = *reinterpret_cast<uint32_t*>(&l);
+}
+
+__device__ __forceinline__ void st_shared_v2(uint32_t addr, uint32_t a, uint32_t b) {
+    asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
+}
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+// Pixel p (p < 128, the TMEM lane order) of the 16 x 8 half tile: quadrant p/32 is an 8 x 4 block.
+__device__ __forceinline__ int2 half_tile_pixel(int p) {
+    return make_int2(((p >> 5) & 1) * 8 + (p & 7), (p >> 6) * 4 + ((p & 31) >> 3));
+}
+
+// One stage's list entries, in walk order (descending list position).
+struct BwdChunk {
+    int id[KC];
+    int pos[KC];
+    float2 mean[KC];
+    float2 ext[KC];
+    float4 conic[KC];  // a, b, c, opacity
+    float4 col[KC];    // r, g, b, opacity (filled when the walk carries the RGB terms)
+    unsigned hits[8];  // bit k: entry k's box touches pixel group w (the kernel defines the groups)
+    int count;
+};
+
+// The list warp: fills s_list[c % LIST_SLOTS] with chunk c of the half tile's entries whose
+// opacity-aware box touches the half tile, arrives on s_list_full[slot], and ends with an empty
+// chunk.  mark_hits(ch, filled) runs on the whole warp once a chunk is filled and records the
+// per-group hit masks.  A slot is refilled only after s_list_free[slot] completes.
+template <bool RGB, class MarkHits>
+__device__ __forceinline__ void list_producer(int lane, int x0, int y0, int width, int height, int2 range,
+                                              const int32_t* __restrict__ values,
+                                              const float2* __restrict__ means2D,
+                                              const float4* __restrict__ conic4,
+                                              const float4* __restrict__ color_opacity,
+                                              const int32_t* __restrict__ n_contrib, BwdChunk* s_list,
+                                              uint64_t* s_list_full, uint64_t* s_list_free, int* s_fail_ptr,
+                                              MarkHits&& mark_hits) {
+    int& s_fail = *s_fail_ptr;
+    // Walks the tile's list back to front in batches of 32 positions (lane l: position
+    // top - 1 - l), software-pipelined over three batches: the sorted ids of batch A, the
+    // gathered means / conics / opacities of batch B, and the hit mask of batch C that chunks
+    // are cut from.  Hits left over when a chunk fills stay in C's mask for the next chunk.
+    // Entries past every pixel's last contributor cannot contribute: start there.
+    int m = 0;
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        const int2 lp = half_tile_pixel(q * 32 + lane);
+        const int px = x0 + lp.x, py = y0 + lp.y;
+        if (px < width && py < height) m = max(m, n_contrib[(size_t)py * width + px]);
+    }
+    int top = min(range.y - range.x, __reduce_max_sync(FULL_MASK, m));
+    const float hx0 = (float)x0 + 0.5f, hx1 = hx0 + 15.0f, hy0 = (float)y0 + 0.5f, hy1 = hy0 + 7.0f;
+    auto fetch_id = [&](int t) { return t - 1 - lane >= 0 ? values[range.x + t - 1 - lane] : -1; };
+    // Batch A: ids only.  Batch B: ids and gathered geometry.  Batch C: geometry and hits.
+    int top_a = top, id_a = fetch_id(top);
+    top -= 32;
+    int top_b = top, id_b = fetch_id(top);
+    top -= 32;
+    float2 m_b = make_float2(0.0f, 0.0f);
+    float4 q_b = make_float4(0.0f, 0.0f, 0.0f, 0.0f), col_b = q_b;
+    auto gather = [&](int g, float2& mm, float4& qq, float4& cc) {
+        if (g >= 0) {
+            mm = means2D[g];
+            const float4 cq = conic4[g];
+            cc = color_opacity[g];
+            qq = make_float4(cq.x, cq.y, cq.z, cc.w);
+        }
+    };
+    // Prime: B <- first batch (gathered), A <- second batch.
+    {
+        const int t = top_a, i = id_a;
+        top_a = top_b;
+        id_a = id_b;
+        top_b = t;
+        id_b = i;
+        gather(id_b, m_b, q_b, col_b);
+    }
+    int top_c = 0, id_c = -1;
+    float2 m_c = make_float2(0.0f, 0.0f), e_c = make_float2(0.0f, 0.0f);
+    float4 q_c = make_float4(0.0f, 0.0f, 0.0f, 0.0f), col_c = q_c;
+    unsigned mask_c = 0;
+    bool more = top_b > 0;  // does batch B hold any position?
+    for (int c = 0;; c++) {
+        const int slot = c % LIST_SLOTS;
+        BwdChunk& ch = s_list[slot];
+        if (c >= LIST_SLOTS) {  // the slot's previous chunk must be drained
+            bool ok = true;
+            if (lane == 0) {
+                ok = !*(volatile int*)&s_fail &&
+                     tc::mbar_wait_bounded(&s_list_free[slot], ((c - LIST_SLOTS) / LIST_SLOTS) & 1, WAIT_LIMIT);
+                if (!ok) s_fail = 1;
+            }
+            if (!__shfl_sync(FULL_MASK, ok, 0)) break;
+        }
+        int filled = 0;
+        while (filled < KC) {
+            if (mask_c == 0) {
+                if (!more) break;  // list exhausted
+                // Promote B to C (its gathers were issued a batch ago), A to B, and fetch a new A.
+                top_c = top_b;
+                id_c = id_b;
+                m_c = m_b;
+                q_c = q_b;
+                col_c = col_b;
+                e_c = id_c >= 0 ? cull_extent_fast(q_c.x, q_c.y, q_c.z, q_c.w) : make_float2(-1e30f, -1e30f);
+                mask_c = __ballot_sync(FULL_MASK, id_c >= 0 && box_hits(m_c, e_c, hx0, hx1, hy0, hy1));
+                more = top_a > 0;
+                top_b = top_a;
+                id_b = id_a;
+                m_b = make_float2(0.0f, 0.0f);
+                q_b = col_b = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                gather(id_b, m_b, q_b, col_b);
+                top_a = top;
+                id_a = fetch_id(top);
+                top -= 32;
+                continue;
+            }
+            const int hits = __popc(mask_c);
+            const int take = min(hits, KC - filled);
+            const int rank = __popc(mask_c & ((1u << lane) - 1u));
+            if (((mask_c >> lane) & 1u) && rank < take) {
+                const int k = filled + rank;
+                ch.id[k] = id_c;
+                ch.pos[k] = top_c - 1 - lane;
+                ch.mean[k] = m_c;
+                ch.ext[k] = e_c;
+                ch.conic[k] = q_c;
+                if (RGB) ch.col[k] = col_c;
+            }
+            // Clear the taken bits (the lowest `take` set bits: descending positions).
+            if (take == hits) {
+                mask_c = 0;
+            } else {
+                const int last_lane = nth_set_bit(mask_c, take - 1);
+                mask_c &= ~((2u << last_lane) - 1u);
+            }
+            filled += take;
+        }
+        if (lane == 0) ch.count = filled;
+        __syncwarp();
+        mark_hits(ch, filled);
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&s_list_full[slot]);
+        if (filled == 0) break;  // the empty chunk ends the list
+    }
+}
+
+}  // namespace fbwd
+}  // namespace hds

@@ -28,23 +28,24 @@
 // Every mbarrier wait is bounded; a group that sees one run out stops (decided group-uniformly at a
 // barrier), records HDS_ERR_DEVICE for hds_device_status, waits for its own MMAs, frees TMEM and
 // returns.
-#include <cuda_bf16.h>
+#include <cstdlib>
+#include <cstring>
 
-#include "hds_common.cuh"
-#include "tcgen05.cuh"
+#include "feature_bwd_common.cuh"
+
+namespace hds {
+__device__ int g_backward_status = 0;
+}  // namespace hds
+
+#include "feature_bwd_cluster.cuh"
 
 namespace hds {
 
-__device__ int g_backward_status = 0;
-
 namespace {
 
-constexpr uint32_t WAIT_LIMIT = 1u << 22;
+using namespace fbwd;
 constexpr int STAGES = 4;
-constexpr int KC = 32;      // list entries per chunk (the N of both MMAs)
-constexpr int PIX = 128;    // pixels per block
 constexpr int MAX_CK = 128; // channels per block (the M of the dF MMA)
-constexpr int LIST_SLOTS = 6;  // list ring: the list warp runs up to three chunks past the operand stages
 // Warp roles: pixel warps 0-7, list warp 8, operand warps 9-12, MMA warp 13.
 constexpr int PIXEL_WARPS = 8, LIST_WARP = 8, OPERAND_WARP0 = 9, OPERAND_WARPS = 4, MMA_WARP = 13;
 constexpr int THREADS = (MMA_WARP + 1) * 32, PIXEL_THREADS = PIXEL_WARPS * 32;
@@ -85,39 +86,6 @@ struct BwdCfg {
     //               B = W MN-major (SBO 2048 between entry blocks, LBO 128 between pixel groups).
     static constexpr uint32_t IDESC_DF = tc::idesc_bf16(128, KC, true, true);
     static_assert(CK == 32 || CK == 64 || CK == 128, "unsupported slice");
-};
-
-// (a, b) -> bf16x2 hi and lo with a in the low half: a = hi.x + lo.x + O(2^-17 a).
-__device__ __forceinline__ void split_bf16(float a, float b, uint32_t& hi, uint32_t& lo) {
-    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-    float2 hf = __bfloat1622float2(h);
-    __nv_bfloat162 l = __floats2bfloat162_rn(__fsub_rn(a, hf.x), __fsub_rn(b, hf.y));
-    hi = *reinterpret_cast<uint32_t*>(&h);
-    lo = *reinterpret_cast<uint32_t*>(&l);
-}
-
-__device__ __forceinline__ void st_shared_v2(uint32_t addr, uint32_t a, uint32_t b) {
-    asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
-}
-__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
-}
-
-// Pixel of block thread p (p < 128): warp p/32 covers an 8 x 4 block of the 16 x 8 half tile.
-__device__ __forceinline__ int2 half_tile_pixel(int p) {
-    return make_int2(((p >> 5) & 1) * 8 + (p & 7), (p >> 6) * 4 + ((p & 31) >> 3));
-}
-
-// One stage's list entries, in walk order (descending list position).
-struct BwdChunk {
-    int id[KC];
-    int pos[KC];
-    float2 mean[KC];
-    float2 ext[KC];
-    float4 conic[KC];  // a, b, c, opacity
-    float4 col[KC];    // r, g, b, opacity (the RGB terms of slice 0)
-    unsigned warp_hits[8];  // bit k: entry k's box touches the 8 x 2 pixel block of pixel warp w
-    int count;
 };
 
 template <int CK, bool RGB>
@@ -181,126 +149,21 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
     const Role role = role_of(warp);
     if (role == Role::List) {
         // ------------------------------------------------------------------ list warp 8
-        // Walks the tile's list back to front in batches of 32 positions (lane l: position
-        // top - 1 - l), software-pipelined over three batches: the sorted ids of batch A, the
-        // gathered means / conics / opacities of batch B, and the hit mask of batch C that chunks
-        // are cut from.  Hits left over when a chunk fills stay in C's mask for the next chunk.
-        // Entries past every pixel's last contributor cannot contribute: start there.
-        int m = 0;
+        // Hit masks: which entries touch each pixel warp's 8 x 2 block (the pixel warps skip the others).
+        list_producer<RGB>(lane, x0, y0, width, height, range, values, means2D, conic4, color_opacity, n_contrib,
+                           s_list, s_list_full, s_list_free, &s_fail, [&](BwdChunk& ch, int filled) {
+                               const bool valid = lane < filled;
+                               const float2 m = valid ? ch.mean[lane] : make_float2(0.0f, 0.0f);
+                               const float2 e = valid ? ch.ext[lane] : make_float2(-1e30f, -1e30f);
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-            const int2 lp = half_tile_pixel(q * 32 + lane);
-            const int px = x0 + lp.x, py = y0 + lp.y;
-            if (px < width && py < height) m = max(m, n_contrib[(size_t)py * width + px]);
-        }
-        int top = min(range.y - range.x, __reduce_max_sync(FULL_MASK, m));
-        const float hx0 = (float)x0 + 0.5f, hx1 = hx0 + 15.0f, hy0 = (float)y0 + 0.5f, hy1 = hy0 + 7.0f;
-        auto fetch_id = [&](int t) { return t - 1 - lane >= 0 ? values[range.x + t - 1 - lane] : -1; };
-        // Batch A: ids only.  Batch B: ids and gathered geometry.  Batch C: geometry and hits.
-        int top_a = top, id_a = fetch_id(top);
-        top -= 32;
-        int top_b = top, id_b = fetch_id(top);
-        top -= 32;
-        float2 m_b = make_float2(0.0f, 0.0f);
-        float4 q_b = make_float4(0.0f, 0.0f, 0.0f, 0.0f), col_b = q_b;
-        auto gather = [&](int g, float2& mm, float4& qq, float4& cc) {
-            if (g >= 0) {
-                mm = means2D[g];
-                const float4 cq = conic4[g];
-                cc = color_opacity[g];
-                qq = make_float4(cq.x, cq.y, cq.z, cc.w);
-            }
-        };
-        // Prime: B <- first batch (gathered), A <- second batch.
-        {
-            const int t = top_a, i = id_a;
-            top_a = top_b;
-            id_a = id_b;
-            top_b = t;
-            id_b = i;
-            gather(id_b, m_b, q_b, col_b);
-        }
-        int top_c = 0, id_c = -1;
-        float2 m_c = make_float2(0.0f, 0.0f), e_c = make_float2(0.0f, 0.0f);
-        float4 q_c = make_float4(0.0f, 0.0f, 0.0f, 0.0f), col_c = q_c;
-        unsigned mask_c = 0;
-        bool more = top_b > 0;  // does batch B hold any position?
-        for (int c = 0;; c++) {
-            const int slot = c % LIST_SLOTS;
-            BwdChunk& ch = s_list[slot];
-            if (c >= LIST_SLOTS) {  // the slot's previous chunk must be drained
-                bool ok = true;
-                if (lane == 0) {
-                    ok = !*(volatile int*)&s_fail &&
-                         tc::mbar_wait_bounded(&s_list_free[slot], ((c - LIST_SLOTS) / LIST_SLOTS) & 1, WAIT_LIMIT);
-                    if (!ok) s_fail = 1;
-                }
-                if (!__shfl_sync(FULL_MASK, ok, 0)) break;
-            }
-            int filled = 0;
-            while (filled < KC) {
-                if (mask_c == 0) {
-                    if (!more) break;  // list exhausted
-                    // Promote B to C (its gathers were issued a batch ago), A to B, and fetch a new A.
-                    top_c = top_b;
-                    id_c = id_b;
-                    m_c = m_b;
-                    q_c = q_b;
-                    col_c = col_b;
-                    e_c = id_c >= 0 ? cull_extent_fast(q_c.x, q_c.y, q_c.z, q_c.w) : make_float2(-1e30f, -1e30f);
-                    mask_c = __ballot_sync(FULL_MASK, id_c >= 0 && box_hits(m_c, e_c, hx0, hx1, hy0, hy1));
-                    more = top_a > 0;
-                    top_b = top_a;
-                    id_b = id_a;
-                    m_b = make_float2(0.0f, 0.0f);
-                    q_b = col_b = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                    gather(id_b, m_b, q_b, col_b);
-                    top_a = top;
-                    id_a = fetch_id(top);
-                    top -= 32;
-                    continue;
-                }
-                const int hits = __popc(mask_c);
-                const int take = min(hits, KC - filled);
-                const int rank = __popc(mask_c & ((1u << lane) - 1u));
-                if (((mask_c >> lane) & 1u) && rank < take) {
-                    const int k = filled + rank;
-                    ch.id[k] = id_c;
-                    ch.pos[k] = top_c - 1 - lane;
-                    ch.mean[k] = m_c;
-                    ch.ext[k] = e_c;
-                    ch.conic[k] = q_c;
-                    if (RGB) ch.col[k] = col_c;
-                }
-                // Clear the taken bits (the lowest `take` set bits: descending positions).
-                if (take == hits) {
-                    mask_c = 0;
-                } else {
-                    const int last_lane = nth_set_bit(mask_c, take - 1);
-                    mask_c &= ~((2u << last_lane) - 1u);
-                }
-                filled += take;
-            }
-            if (lane == 0) ch.count = filled;
-            __syncwarp();
-            // Which entries touch each pixel warp's 8 x 2 block (the pixel warps skip the others).
-            {
-                const bool valid = lane < filled;
-                const float2 m = valid ? ch.mean[lane] : make_float2(0.0f, 0.0f);
-                const float2 e = valid ? ch.ext[lane] : make_float2(-1e30f, -1e30f);
-#pragma unroll
-                for (int w = 0; w < 8; w++) {
-                    const float bx0 = (float)(x0 + (w & 1) * 8) + 0.5f;
-                    const float by0 = (float)(y0 + ((w & 3) >> 1) * 4 + (w >> 2) * 2) + 0.5f;
-                    const unsigned mask =
-                        __ballot_sync(FULL_MASK, valid && box_hits(m, e, bx0, bx0 + 7.0f, by0, by0 + 1.0f));
-                    if (lane == 0) ch.warp_hits[w] = mask;
-                }
-            }
-            __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&s_list_full[slot]);
-            if (filled == 0) break;  // the empty chunk ends the list
-        }
+                               for (int w = 0; w < 8; w++) {
+                                   const float bx0 = (float)(x0 + (w & 1) * 8) + 0.5f;
+                                   const float by0 = (float)(y0 + ((w & 3) >> 1) * 4 + (w >> 2) * 2) + 0.5f;
+                                   const unsigned mask = __ballot_sync(
+                                       FULL_MASK, valid && box_hits(m, e, bx0, bx0 + 7.0f, by0, by0 + 1.0f));
+                                   if (lane == 0) ch.hits[w] = mask;
+                               }
+                           });
     } else if (role == Role::Operand) {
         // ------------------------------------------------------------------ operand warps 9-12
         const int otid = tid - OPERAND_WARP0 * 32, ow = otid >> 5;
@@ -598,7 +461,7 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
             // half of the group's W block (bf16 hi + lo) and its u quad; the geometric partials
             // leave as u = dL/dalpha * G, summed by the operand warps.
             const uint32_t wh = w_hi(s), wl = wh + W_BYTES, ub = u_base(s) + p * 16;
-            const unsigned hits_w = ch.warp_hits[warp];  // entries whose box touches this warp's pixels
+            const unsigned hits_w = ch.hits[warp];  // entries whose box touches this warp's pixels
 #pragma unroll 1
             for (int k0 = 0; k0 < cnt; k0 += 8) {
                 const int kb = k0 + 4 * part;  // this thread's four entries
@@ -699,6 +562,11 @@ int launch_backward(int D, int width, int height, const int32_t* tile_ranges, co
 
 namespace {
 
+bool cluster_backward_enabled() {
+    const char* v = getenv("HDS_FEATURE_BWD_CLUSTER");  // read per call, so a process can switch
+    return v != nullptr && strcmp(v, "1") == 0;
+}
+
 // grad_image (with background and grad_colors) adds the RGB backward to the same walk; NULL leaves
 // it out (the reference's rasterize_features_backward).
 int features_backward(int n, int channels, int slice_width, int width, int height, const float* grad_output,
@@ -729,7 +597,14 @@ int features_backward(int n, int channels, int slice_width, int width, int heigh
     HDS_CHECK_CUDA(cudaMemsetAsync(grad_opacities, 0, sizeof(float) * (size_t)n, stream));
     if (grad_image != nullptr) HDS_CHECK_CUDA(cudaMemsetAsync(grad_colors, 0, sizeof(float) * 3 * (size_t)n, stream));
     // The slice width only selects the reference's kernel instantiation; the sums are the same for
-    // any slicing, and these kernels always take slices of min(channels, 128).
+    // any slicing.  One block per half tile and slice of min(D, 128) channels (one walk per slice);
+    // with HDS_FEATURE_BWD_CLUSTER=1, 256 and 512 channels run on four-block clusters instead (slices
+    // of D / 4, one walk per pixel).
+    if (D >= 256 && cluster_backward_enabled()) {
+        if (D == 256)
+            return clus::launch_backward_cluster<64>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);
+        return clus::launch_backward_cluster<128>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);
+    }
     switch (D) {
         case 32: return launch_backward<32>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);
         case 64: return launch_backward<64>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);

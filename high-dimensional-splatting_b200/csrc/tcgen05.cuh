@@ -147,6 +147,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking test of phase `parity` (try_wait may suspend the thread for a while; a thread that
+// polls several barriers in turn uses this so that one idle barrier does not delay the others).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t"
+        ".reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t"
+        "}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Waits for phase `parity` of the barrier to complete, giving up after `limit` polls (each poll
 // may itself suspend for a bounded, hardware-defined time).  Returns false on timeout.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t limit) {
@@ -205,6 +221,86 @@ __device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity
         }
     }
     return false;
+}
+
+// ---- bulk asynchronous reductions (the TMA unit adds shared-memory rows into global memory) ----
+
+// dst[i] += src[i] for bytes / 4 floats, element-wise atomic at L2; dst, src and bytes 16-byte
+// aligned.  The source may be reused once bulk_wait_read() returns in the issuing thread.
+__device__ __forceinline__ void bulk_reduce_add_f32(float* dst, uint32_t src_smem, uint32_t bytes) {
+    asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(dst),
+                 "r"(src_smem), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until every bulk operation this thread committed has finished reading its source.
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Waits until every bulk operation this thread committed has completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// ---- thread-block clusters: distributed shared memory and cluster-scope synchronisation ----
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// The shared::cluster address of this block's shared-memory address `addr` in block `rank` of the
+// cluster (a block's window is contiguous, so offsets may be added after mapping).
+__device__ __forceinline__ uint32_t map_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+
+// Asynchronous stores into a peer block's shared memory: each completes `bytes` of the transaction
+// count of the peer's mbarrier (its shared::cluster address), with release semantics at cluster
+// scope, so the peer sees the data once that barrier's phase completes; the sender never waits.
+__device__ __forceinline__ void st_async_v4(uint32_t addr, float a, float b, float c, float d, uint32_t mbar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                     addr),
+                 "f"(a), "f"(b), "f"(c), "f"(d), "r"(mbar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void st_async_v2(uint32_t addr, uint32_t a, uint32_t b, uint32_t mbar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.b32 [%0], {%1, %2}, [%3];" ::"r"(addr),
+                 "r"(a), "r"(b), "r"(mbar)
+                 : "memory");
+}
+
+// Arrives on this block's mbarrier and adds `bytes` to the transaction count its phase waits for.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// try_wait with cluster-scope acquire: for barriers that peers arrive on after writing this block's
+// shared memory.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t"
+        ".reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t"
+        "}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_t parity, uint32_t limit) {
+    for (uint32_t i = 0; i < limit; i++)
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+    return false;
+}
+
+// Every thread of every block of the cluster: arrive (release) and wait (acquire).
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
 
 __device__ __forceinline__ float to_tf32(float x) {

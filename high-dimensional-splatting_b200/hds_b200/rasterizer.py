@@ -5,6 +5,7 @@ its JIT-built extension), so a training loop written against the reference runs 
 """
 from __future__ import annotations
 
+import os
 from types import ModuleType
 
 import torch
@@ -12,9 +13,18 @@ import torch
 from . import gaussian_rasterizer as _ext
 
 # Channels each feature backward block owns (the reference's __init__.py:11-12, 158); None takes the
-# widest slice, at most 128.  The slicing does not change the sums; up to 128 channels the fused
-# backward (one slice) is used regardless.
+# widest slice, at most 128.  The slicing does not change the sums; it applies to 256 and 512 channels
+# on the one-block kernel, where the RGB backward is a pass of its own.
 FEATURE_SLICE_WIDTH: int | None = None
+
+
+def _fused_backward(channels: int) -> bool:
+    """Whether one walk carries both backward passes.  Up to 128 channels there is one channel slice,
+    and the RGB terms ride in its walk.  With 256 or 512 channels on the one-block kernel, only the
+    first of several slices would carry them, and that lengthens its walk by more than the separate
+    RGB pass costs; the four-block clusters (HDS_FEATURE_BWD_CLUSTER=1) walk each pixel once, so there
+    they ride along again."""
+    return channels <= 128 or os.environ.get("HDS_FEATURE_BWD_CLUSTER") == "1"
 
 # When true, the backward of a rasterize call whose features are a leaf that already holds a
 # contiguous float32 .grad of its shape adds dL/dfeatures straight into that .grad (and hands
@@ -86,8 +96,8 @@ class RasterizeGaussians(torch.autograd.Function):
                     and target.shape == features.shape and target.device == features.device
                     and target.data_ptr() % 16 == 0):
                 target = None
-            if features.shape[1] <= 128:
-                # One channel slice: the RGB terms ride along in the same walk (one pass instead of two).
+            if _fused_backward(features.shape[1]):
+                # The RGB terms ride along in the feature walk (one pass instead of two).
                 with torch.cuda.nvtx.range("rasterize_backward_fused"):
                     grad_means2D, grad_conics, grad_colors, grad_opacities, grad_feats = ext.rasterize_backward_fused(
                         grad_image.contiguous() if grad_image is not None else None, background,
@@ -96,8 +106,7 @@ class RasterizeGaussians(torch.autograd.Function):
                 if grad_colors is None:
                     grad_colors = torch.zeros(means2D.shape[0], 3, device=means2D.device)
             else:
-                # Several slices: only one would carry the RGB terms and their blocks would lengthen the
-                # walk more than the separate RGB pass costs.
+                # One walk per 128-channel slice: the RGB backward is a pass of its own.
                 if grad_image is None:
                     grad_image = torch.zeros(height, width, 3, device=means2D.device)
                 with torch.cuda.nvtx.range("rasterize_backward"):

@@ -151,7 +151,24 @@ def test_feature_backward(ext, golden, name, channels, slice_width):
         assert_grads_close(host(g), wv, nm)
 
 
-@pytest.mark.parametrize("channels", [32, 128, 512])
+@pytest.mark.parametrize("channels, slice_width", [(256, 128), (256, 64), (512, 128), (512, 64)])
+@pytest.mark.parametrize("name", ["raster_ref_scene", "dense_tile", "size3", "config1_20k"])
+def test_feature_backward_cluster_kernel(ext, golden, monkeypatch, name, channels, slice_width):
+    """256 and 512 channels on the four-block clusters (one walk per pixel, dot partials and weights
+    exchanged through distributed shared memory), which HDS_FEATURE_BWD_CLUSTER=1 selects."""
+    monkeypatch.setenv("HDS_FEATURE_BWD_CLUSTER", "1")
+    test_feature_backward(ext, golden, name, channels, slice_width)
+
+
+@pytest.mark.parametrize("channels", [256, 512])
+@pytest.mark.parametrize("name", ["raster_ref_scene", "dense_tile", "config1_20k"])
+@pytest.mark.parametrize("with_rgb", [True, False])
+def test_fused_backward_cluster_kernel(ext, golden, monkeypatch, name, channels, with_rgb):
+    monkeypatch.setenv("HDS_FEATURE_BWD_CLUSTER", "1")
+    test_fused_backward(ext, golden, name, channels, with_rgb)
+
+
+@pytest.mark.parametrize("channels", [32, 128, 256, 512])
 @pytest.mark.parametrize("name", ["raster_ref_scene", "raster_config0", "dense_tile", "size3", "config1_20k"])
 @pytest.mark.parametrize("with_rgb", [True, False])
 def test_fused_backward(ext, golden, name, channels, with_rgb):
