@@ -247,6 +247,14 @@ def tile_stats(wl, device):
             "visible": int((radii > 0).sum())}
 
 
+# DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one-pass ncu captures of
+# this bench's own workload: (call, channels, gaussians) -> (bytes, summary under profiles/).
+MEASURED_TRAFFIC = {
+    ("hds_render_features_backward_accumulate", 512, 1_180_000):
+        (2.59e9 + 0.595e9, "profiles/feature_backward_traffic_config2_1180k_c512.md"),
+}
+
+
 def roofline(name, ms_per_launch, stats, args, peaks, n):
     """Algorithmic bytes (or flops) per launch of the dominant call over its measured duration."""
     C = args.channels
@@ -272,8 +280,12 @@ def roofline(name, ms_per_launch, stats, args, peaks, n):
         return {"bound": "hbm", "achieved": None, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": None,
                 "traffic": None, "kernel": name}
     ach = nbytes / (ms_per_launch * 1e-3) / 1e9
-    return {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": ach / peaks["hbm_gbs"],
-            "traffic": None, "kernel": name, "algorithmic_bytes": nbytes}
+    out = {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": ach / peaks["hbm_gbs"],
+           "traffic": None, "kernel": name, "algorithmic_bytes": nbytes}
+    measured = MEASURED_TRAFFIC.get((name, C, args.gaussians))
+    if measured is not None:
+        out["traffic"], out["traffic_source"] = measured
+    return out
 
 
 def cpu_baseline(args, threads: int = 1):
