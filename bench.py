@@ -250,7 +250,9 @@ def tile_stats(wl, device):
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one-pass ncu captures of
 # this bench's own workload: (call, channels, gaussians) -> (bytes, summary under profiles/).
 MEASURED_TRAFFIC = {
-    ("hds_render_features_backward_accumulate", 512, 1_180_000):
+    ("hds_render_backward_fused", 512, 1_180_000):  # the four-block cluster kernel (the default at C = 512)
+        (2.88e9 + 0.832e9, "profiles/feature_backward_traffic_config2_1180k_c512.md"),
+    ("hds_render_features_backward_accumulate", 512, 1_180_000):  # the one-block kernel
         (2.59e9 + 0.595e9, "profiles/feature_backward_traffic_config2_1180k_c512.md"),
 }
 

@@ -63,7 +63,9 @@ constexpr int RECV_SLICE_BYTES = QPIX * KC * 4;
 constexpr int RECV_BYTES = CLUSTER * RECV_SLICE_BYTES;
 // u = dL/dalpha G of the quadrant: [pixel][entry] fp32, 16-byte groups permuted by 2 (pixel / 8).
 constexpr int U_BYTES = QPIX * KC * 4;
-constexpr uint32_t TMEM_COLS = 256;  // dots at s*32, dF^T at 128 + s*32
+// TMEM columns: dots at s*32, dF^T at 128 + s*32, and G as the dot's A operand from G_TMEM (lane =
+// pixel; hi: CK / 2 columns of channel pairs, then lo).
+constexpr uint32_t TMEM_COLS = 512, G_TMEM = 256;
 
 template <int CK>
 struct Cfg {
@@ -199,6 +201,30 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
             st_shared_v4(g_hi + i * 16, 0u, 0u, 0u, 0u);
             st_shared_v4(g_lo + i * 16, 0u, 0u, 0u, 0u);
         }
+        // G also goes to TMEM as the dot's A operand (lane = pixel, column = channel pair), so that
+        // the dot MMAs read only their B operand from shared memory.  Each warp copies the rows of
+        // its lane quadrant: pixel p's 16-byte block of eight channels is four columns.
+        tc::group_sync<OPERAND_BAR>();
+        {
+            const int p = q4 * 32 + lane;
+#pragma unroll
+            for (int half = 0; half < 2; half++) {
+                const uint32_t src = (half ? g_lo : g_hi) + p * 16;
+                const uint32_t dst = tmem + ((uint32_t)(q4 * 32) << 16) + G_TMEM + half * (CK / 2);
+#pragma unroll
+                for (int cb0 = 0; cb0 < CK / 8; cb0 += 4) {
+                    uint32_t r[16];
+#pragma unroll
+                    for (int b = 0; b < 4; b++)
+                        asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                                     : "=r"(r[4 * b]), "=r"(r[4 * b + 1]), "=r"(r[4 * b + 2]), "=r"(r[4 * b + 3])
+                                     : "r"(src + (cb0 + b) * 2048));
+                    tc::tmem_st16(dst + cb0 * 4, r);
+                }
+            }
+            tc::tmem_wait_st();
+        }
+        tc::fence_before_sync();
 
         int n_real = -1;  // number of non-empty chunks, known once the empty chunk arrives
         for (int c = 0;; c++) {
@@ -383,14 +409,13 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
                         const uint32_t fh = fw(s), fl = fh + K::F_BYTES;
 #pragma unroll
                         for (int ks = 0; ks < CK / 16; ks++) {
-                            const uint64_t ah = tc::smem_desc(g_hi + ks * 4096, 2048, 128);
-                            const uint64_t al = tc::smem_desc(g_lo + ks * 4096, 2048, 128);
+                            const uint32_t ah = tmem + G_TMEM + ks * 8, al = ah + CK / 2;  // A = G from TMEM
                             const uint64_t bh = tc::smem_desc(fh + ks * 2 * K::F_LBO, K::F_LBO, 128);
                             const uint64_t bl = tc::smem_desc(fl + ks * 2 * K::F_LBO, K::F_LBO, 128);
                             const uint32_t d = tmem + s * 32;
-                            tc::mma_bf16(d, ah, bh, K::IDESC_DOT, ks > 0 ? 1u : 0u);
-                            tc::mma_bf16(d, ah, bl, K::IDESC_DOT, 1u);
-                            tc::mma_bf16(d, al, bh, K::IDESC_DOT, 1u);
+                            tc::mma_bf16_ta(d, ah, bh, K::IDESC_DOT, ks > 0 ? 1u : 0u);
+                            tc::mma_bf16_ta(d, ah, bl, K::IDESC_DOT, 1u);
+                            tc::mma_bf16_ta(d, al, bh, K::IDESC_DOT, 1u);
                         }
                         tc::commit(&s_dot_full[s]);
                         last_bar = &s_dot_full[s];

@@ -587,9 +587,14 @@ int launch_backward(int D, int width, int height, const int32_t* tile_ranges, co
 
 namespace {
 
-bool cluster_backward_enabled() {
-    const char* v = getenv("HDS_FEATURE_BWD_CLUSTER");  // read per call, so a process can switch
-    return v != nullptr && strcmp(v, "1") == 0;
+// Whether D channels run on the four-block clusters: by default at 512 channels, where they are the
+// faster kernel (the RGB backward rides in their walk); HDS_FEATURE_BWD_CLUSTER=1 also selects them at
+// 256 channels and =0 never.  Read per call, so a process can switch.
+bool cluster_backward_enabled(int D) {
+    const char* v = getenv("HDS_FEATURE_BWD_CLUSTER");
+    if (v != nullptr && strcmp(v, "0") == 0) return false;
+    if (v != nullptr && strcmp(v, "1") == 0) return D >= 256;
+    return D == 512;
 }
 
 // grad_image (with background and grad_colors) adds the RGB backward to the same walk; NULL leaves
@@ -622,10 +627,9 @@ int features_backward(int n, int channels, int slice_width, int width, int heigh
     HDS_CHECK_CUDA(cudaMemsetAsync(grad_opacities, 0, sizeof(float) * (size_t)n, stream));
     if (grad_image != nullptr) HDS_CHECK_CUDA(cudaMemsetAsync(grad_colors, 0, sizeof(float) * 3 * (size_t)n, stream));
     // The slice width only selects the reference's kernel instantiation; the sums are the same for
-    // any slicing.  One block per half tile and slice of min(D, 128) channels (one walk per slice);
-    // with HDS_FEATURE_BWD_CLUSTER=1, 256 and 512 channels run on four-block clusters instead (slices
-    // of D / 4, one walk per pixel).
-    if (D >= 256 && cluster_backward_enabled()) {
+    // any slicing.  One block per half tile and slice of min(D, 128) channels (one walk per slice), or
+    // four-block clusters (slices of D / 4, one walk per pixel).
+    if (cluster_backward_enabled(D)) {
         if (D == 256)
             return clus::launch_backward_cluster<64>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);
         return clus::launch_backward_cluster<128>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);

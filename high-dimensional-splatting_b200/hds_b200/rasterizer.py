@@ -14,17 +14,21 @@ from . import gaussian_rasterizer as _ext
 
 # Channels each feature backward block owns (the reference's __init__.py:11-12, 158); None takes the
 # widest slice, at most 128.  The slicing does not change the sums; it applies to 256 and 512 channels
-# on the one-block kernel, where the RGB backward is a pass of its own.
+# on the one-block kernel (256 by default, 512 with HDS_FEATURE_BWD_CLUSTER=0), where the RGB backward
+# is a pass of its own.
 FEATURE_SLICE_WIDTH: int | None = None
 
 
 def _fused_backward(channels: int) -> bool:
     """Whether one walk carries both backward passes.  Up to 128 channels there is one channel slice,
-    and the RGB terms ride in its walk.  With 256 or 512 channels on the one-block kernel, only the
-    first of several slices would carry them, and that lengthens its walk by more than the separate
-    RGB pass costs; the four-block clusters (HDS_FEATURE_BWD_CLUSTER=1) walk each pixel once, so there
-    they ride along again."""
-    return channels <= 128 or os.environ.get("HDS_FEATURE_BWD_CLUSTER") == "1"
+    and the RGB terms ride in its walk.  The four-block clusters walk each pixel once, so the RGB terms
+    ride along there too; they run 512 channels by default and 256 with HDS_FEATURE_BWD_CLUSTER=1 (=0:
+    never).  With 256 or 512 channels on the one-block kernel, only the first of several slices would
+    carry the RGB terms, and that lengthens its walk by more than the separate RGB pass costs."""
+    if channels <= 128:
+        return True
+    switch = os.environ.get("HDS_FEATURE_BWD_CLUSTER")
+    return switch == "1" or (switch != "0" and channels == 512)
 
 # When true, the backward of a rasterize call whose features are a leaf that already holds a
 # contiguous float32 .grad of its shape adds dL/dfeatures straight into that .grad (and hands

@@ -160,6 +160,15 @@ def test_feature_backward_cluster_kernel(ext, golden, monkeypatch, name, channel
     test_feature_backward(ext, golden, name, channels, slice_width)
 
 
+@pytest.mark.parametrize("channels, slice_width", [(256, 128), (512, 128), (512, 64)])
+@pytest.mark.parametrize("name", ["raster_ref_scene", "dense_tile", "size3", "config1_20k"])
+def test_feature_backward_one_block_kernel(ext, golden, monkeypatch, name, channels, slice_width):
+    """256 and 512 channels on the one-block kernel (one walk per 128-channel slice), which
+    HDS_FEATURE_BWD_CLUSTER=0 selects."""
+    monkeypatch.setenv("HDS_FEATURE_BWD_CLUSTER", "0")
+    test_feature_backward(ext, golden, name, channels, slice_width)
+
+
 @pytest.mark.parametrize("channels", [256, 512])
 @pytest.mark.parametrize("name", ["raster_ref_scene", "dense_tile", "config1_20k"])
 @pytest.mark.parametrize("with_rgb", [True, False])
