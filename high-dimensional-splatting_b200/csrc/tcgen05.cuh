@@ -126,17 +126,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
-// 32 lanes x 32 bits, 8 consecutive columns.
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
-    uint32_t r[8];
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-                 : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 8; i++) v[i] = __uint_as_float(r[i]);
-}
-
 // 32 lanes x 32 bits, 32 consecutive columns.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
     uint32_t r[32];
@@ -165,22 +154,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         "{\n\t"
         ".reg .pred p;\n\t"
         "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t"
-        "}\n"
-        : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-// Non-blocking test of phase `parity` (try_wait may suspend the thread for a while; a thread that
-// polls several barriers in turn uses this so that one idle barrier does not delay the others).
-__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t"
-        ".reg .pred p;\n\t"
-        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t"
         "}\n"
         : "=r"(ok)
@@ -232,21 +205,6 @@ __device__ __forceinline__ void tmem_ld16x2_4(uint32_t taddr, float* v) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 4; i++) v[i] = __uint_as_float(r[i]);
-}
-
-// As mbar_wait_bounded, for waits off the critical path: after a few polls the thread sleeps
-// between polls (up to 256 ns), leaving issue slots to the warps that do the work.  Gives up after
-// `limit` polls.
-__device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, uint32_t limit) {
-    uint32_t ns = 0;
-    for (uint32_t i = 0; i < limit; i++) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if (i >= 4) {
-            ns = ns < 256 ? ns + 32 : 256;
-            __nanosleep(ns);
-        }
-    }
-    return false;
 }
 
 // ---- bulk asynchronous reductions (the TMA unit adds shared-memory rows into global memory) ----
