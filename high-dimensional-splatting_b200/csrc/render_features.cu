@@ -403,7 +403,8 @@ struct Cfg {
     static_assert(C == 256 || C == 512, "the warp-specialised forward is for 256 or 512 channels");
     // The gather's 8 x GATHER_THREADS item sweeps tile the chunk exactly (and the loop bound guards
     // any other count as well).
-    static_assert((KC * (C / 4)) % (8 * GATHER_THREADS) == 0, "gather sweep must tile the chunk");
+    static constexpr int GATHER_UNROLL = 16;  // float4 loads in flight per gather thread
+    static_assert((KC * (C / 4)) % (GATHER_UNROLL * GATHER_THREADS) == 0, "gather sweep must tile the chunk");
 };
 
 // One list slot: chunk entries in list order.
@@ -589,17 +590,17 @@ __global__ void __launch_bounds__(THREADS, 1) feature_forward_ws_kernel(
             // Item (k, j): entry k's channels 4j .. 4j + 3; a warp reads 512 contiguous bytes of a row.
             const uint32_t b_stage = b_base + s * K::B_BYTES;
 #pragma unroll 1
-            for (int i0 = 0; i0 < (stopped ? 0 : KC * (C / 4)); i0 += 8 * GATHER_THREADS) {
-                float4 v[8];
+            for (int i0 = 0; i0 < (stopped ? 0 : KC * (C / 4)); i0 += K::GATHER_UNROLL * GATHER_THREADS) {
+                float4 v[K::GATHER_UNROLL];
 #pragma unroll
-                for (int u = 0; u < 8; u++) {
+                for (int u = 0; u < K::GATHER_UNROLL; u++) {
                     const int i = i0 + u * GATHER_THREADS + gtid, k = i / (C / 4), j = i % (C / 4);
                     v[u] = k < cnt && k < KC
                                ? __ldg(reinterpret_cast<const float4*>(features + (size_t)ch.id[k] * C) + j)
                                : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                 }
 #pragma unroll
-                for (int u = 0; u < 8; u++) {
+                for (int u = 0; u < K::GATHER_UNROLL; u++) {
                     const int i = i0 + u * GATHER_THREADS + gtid, k = i / (C / 4), j = i % (C / 4);
                     if (k >= KC) continue;  // past the chunk: no slot of this stage
                     const uint32_t off = (k >> 2) * K::B_SBO + (j >> 3) * 512 + (k & 3) * 128 +
