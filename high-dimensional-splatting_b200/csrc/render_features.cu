@@ -762,12 +762,25 @@ __global__ void __launch_bounds__(THREADS, 1) feature_forward_ws_kernel(
         const bool have = tc::group_sync_count<PIX_BAR>(ok, PIXEL_THREADS) != 0;
         tc::fence_after_sync();
         {
-            const int pe = quad * 32 + lane;
-            const int2 le = half_tile_pixel(pe);
-            const int ex = x0 + le.x, ey = y0 + le.y;
-            const bool e_inside = ex < width && ey < height;
-            float* dst = feature_image + ((size_t)ey * width + ex) * C;
+            // Lane = pixel in TMEM, channels innermost in the image: each block of 16 columns goes
+            // through this warp's 2 KB of the (now idle) stage buffers, so that every store
+            // instruction writes 8 pixels x 64 contiguous bytes instead of 32 scattered 16-byte pieces.
+            // Scratch row r (64 bytes) holds pixel r's 16 channels, its 16-byte quads permuted by
+            // (r / 2) % 4 so that both the writes and the reads are conflict-free.
+            const uint32_t scratch = a_base + warp * 2048;
             const uint32_t lane_addr = tmem + ((uint32_t)(quad * 32) << 16);
+            // Reading: lane -> pixel 8 g + lane / 4 of the warp's 32, quad lane % 4.
+            const int rq = lane & 3;
+            float* rdst[4];
+            bool rin[4];
+#pragma unroll
+            for (int g = 0; g < 4; g++) {
+                const int r = 8 * g + (lane >> 2);
+                const int2 le = half_tile_pixel(quad * 32 + r);
+                const int ex = x0 + le.x, ey = y0 + le.y;
+                rin[g] = ex < width && ey < height;
+                rdst[g] = feature_image + ((size_t)(rin[g] ? ey : 0) * width + (rin[g] ? ex : 0)) * C + 4 * rq;
+            }
 #pragma unroll 1
             for (int col = half16 * (C / 2); col < (half16 + 1) * (C / 2); col += 16) {
                 float v[16];
@@ -777,11 +790,21 @@ __global__ void __launch_bounds__(THREADS, 1) feature_forward_ws_kernel(
 #pragma unroll
                     for (int i = 0; i < 16; i++) v[i] = 0.0f;
                 }
-                if (e_inside) {
 #pragma unroll
-                    for (int i = 0; i < 16; i += 4)
-                        *reinterpret_cast<float4*>(dst + col + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                for (int qd = 0; qd < 4; qd++)
+                    st_shared_v4f(scratch + lane * 64 + ((qd ^ ((lane >> 1) & 3)) << 4),
+                                  make_float4(v[4 * qd], v[4 * qd + 1], v[4 * qd + 2], v[4 * qd + 3]));
+                __syncwarp();
+#pragma unroll
+                for (int g = 0; g < 4; g++) {
+                    const int r = 8 * g + (lane >> 2);
+                    float4 o;
+                    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                                 : "=f"(o.x), "=f"(o.y), "=f"(o.z), "=f"(o.w)
+                                 : "r"(scratch + r * 64 + ((rq ^ ((r >> 1) & 3)) << 4)));
+                    if (rin[g]) *reinterpret_cast<float4*>(rdst[g] + col) = o;
                 }
+                __syncwarp();
             }
         }
         if (inside && part == 0) {
