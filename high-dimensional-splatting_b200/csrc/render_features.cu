@@ -73,6 +73,11 @@ struct Chunk {
     int count;
 };
 
+__device__ __forceinline__ void st_shared_v4f(uint32_t addr, float4 v) {
+    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+
 template <int C>
 __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
     int width, int height, int tiles_x, const int2* __restrict__ ranges, const int32_t* __restrict__ values,
@@ -323,21 +328,49 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
         const bool have = tc::group_sync_count<PIXEL_BAR>(ok) != 0;
         tc::fence_after_sync();
         const size_t p = (size_t)py * width + px;
-        float* dst = feature_image + p * C;
-        const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-#pragma unroll 1
-        for (int col = 0; col < C; col += 16) {
-            float v[16];
-            if (have) {
-                tc::tmem_ld16(lane_addr + col, v);  // warp-collective: every lane executes it
-            } else {
+        {
+            // Lane = pixel in TMEM, channels innermost in the image: each block of 16 columns goes
+            // through this warp's 2 KB of the (now idle) A stages, so that every store instruction
+            // writes 8 pixels x 64 contiguous bytes instead of 32 scattered 16-byte pieces.  Scratch
+            // row r (64 bytes) holds pixel r's 16 channels, its 16-byte quads permuted by (r / 2) % 4
+            // so that both the writes and the reads are conflict-free.
+            const uint32_t scratch = a_base + warp * 2048;
+            const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+            // Reading: lane -> pixel 8 g + lane / 4 of the warp's 32 (an 8 x 4 block), quad lane % 4.
+            const int rq = lane & 3;
+            float* rdst[4];
+            bool rin[4];
 #pragma unroll
-                for (int i = 0; i < 16; i++) v[i] = 0.0f;
+            for (int g = 0; g < 4; g++) {
+                const int r = 8 * g + (lane >> 2);
+                const int ex = x0 + (warp & 1) * 8 + (r & 7), ey = y0 + (warp >> 1) * 4 + (r >> 3);
+                rin[g] = ex < width && ey < height;
+                rdst[g] = feature_image + ((size_t)(rin[g] ? ey : 0) * width + (rin[g] ? ex : 0)) * C + 4 * rq;
             }
-            if (inside) {
+#pragma unroll 1
+            for (int col = 0; col < C; col += 16) {
+                float v[16];
+                if (have) {
+                    tc::tmem_ld16(lane_addr + col, v);  // warp-collective: every lane executes it
+                } else {
 #pragma unroll
-                for (int i = 0; i < 16; i += 4)
-                    *reinterpret_cast<float4*>(dst + col + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                    for (int i = 0; i < 16; i++) v[i] = 0.0f;
+                }
+#pragma unroll
+                for (int qd = 0; qd < 4; qd++)
+                    st_shared_v4f(scratch + lane * 64 + ((qd ^ ((lane >> 1) & 3)) << 4),
+                                  make_float4(v[4 * qd], v[4 * qd + 1], v[4 * qd + 2], v[4 * qd + 3]));
+                __syncwarp();
+#pragma unroll
+                for (int g = 0; g < 4; g++) {
+                    const int r = 8 * g + (lane >> 2);
+                    float4 o;
+                    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                                 : "=f"(o.x), "=f"(o.y), "=f"(o.z), "=f"(o.w)
+                                 : "r"(scratch + r * 64 + ((rq ^ ((r >> 1) & 3)) << 4)));
+                    if (rin[g]) *reinterpret_cast<float4*>(rdst[g] + col) = o;
+                }
+                __syncwarp();
             }
         }
         if (inside) {
@@ -417,11 +450,6 @@ struct List {
     float4 col[KC];    // r, g, b, opacity
     int count;
 };
-
-__device__ __forceinline__ void st_shared_v4f(uint32_t addr, float4 v) {
-    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
-                 : "memory");
-}
 
 __device__ __forceinline__ int2 half_tile_pixel(int p) {
     return make_int2(((p >> 5) & 1) * 8 + (p & 7), (p >> 6) * 4 + ((p & 31) >> 3));
