@@ -448,6 +448,7 @@ struct List {
     float2 ext[KC];
     float4 conic[KC];  // a, b, c, opacity
     float4 col[KC];    // r, g, b, opacity
+    unsigned hits[8];  // bit k: entry k's box touches the 8 x 2 pixel block of pixel warp w
     int count;
 };
 
@@ -590,6 +591,21 @@ __global__ void __launch_bounds__(THREADS, 1) feature_forward_ws_kernel(
             }
             if (lane == 0) ch.count = filled;
             __syncwarp();
+            {
+                // Which entries touch each pixel warp's 8 x 2 block: the pixel warps test bits.
+                const bool valid = lane < filled;
+                const float2 m = valid ? ch.mean[lane] : make_float2(0.0f, 0.0f);
+                const float2 e = valid ? ch.ext[lane] : make_float2(-1e30f, -1e30f);
+#pragma unroll
+                for (int w = 0; w < PIXEL_WARPS; w++) {
+                    const float bx0 = (float)(x0 + ((w & 3) & 1) * 8) + 0.5f;
+                    const float by0 = (float)(y0 + ((w & 3) >> 1) * 4 + (w >> 2) * 2) + 0.5f;
+                    const unsigned mask =
+                        __ballot_sync(FULL_MASK, valid && box_hits(m, e, bx0, bx0 + 7.0f, by0, by0 + 1.0f));
+                    if (lane == 0) ch.hits[w] = mask;
+                }
+            }
+            __syncwarp();
             if (lane == 0) tc::mbar_arrive(&s_list_full[slot]);
             if (filled == 0) break;
         }
@@ -694,8 +710,6 @@ __global__ void __launch_bounds__(THREADS, 1) feature_forward_ws_kernel(
         const int px = x0 + lp.x, py = y0 + lp.y;
         const bool inside = px < width && py < height;
         const float cx = (float)px + 0.5f, cy = (float)py + 0.5f;
-        const float wx0 = (float)(x0 + (quad & 1) * 8) + 0.5f, wx1 = wx0 + 7.0f;
-        const float wy0 = (float)(y0 + (quad >> 1) * 4 + half16 * 2) + 0.5f, wy1 = wy0 + 1.0f;
         const bool rgb = image4 != nullptr;
         float T = 1.0f, ar = 0.0f, ag = 0.0f, ab = 0.0f;
         int last = 0;
@@ -719,15 +733,15 @@ __global__ void __launch_bounds__(THREADS, 1) feature_forward_ws_kernel(
             // A row of pixel p: K-quad q at q*A_LBO + (p/8)*128 + (p%8)*16; this thread owns quad 2g + part
             // of group g.
             const uint32_t a_row = a_base + s * K::A_BYTES + (p >> 3) * 128 + (p & 7) * 16;
+            const unsigned hits_w = ch.hits[warp];  // entries whose box touches this warp's pixels
 #pragma unroll 1
             for (int k0 = 0; k0 < (all_done ? 0 : KC); k0 += 8) {
                 const int kb = k0 + 4 * part;
                 float w_own[4] = {0.0f, 0.0f, 0.0f, 0.0f};
                 bool hit[4];
 #pragma unroll
-                for (int i = 0; i < 4; i++)
-                    hit[i] = kb + i < cnt && box_hits(ch.mean[kb + i], ch.ext[kb + i], wx0, wx1, wy0, wy1);
-                const bool any = __any_sync(FULL_MASK, hit[0] || hit[1] || hit[2] || hit[3]);
+                for (int i = 0; i < 4; i++) hit[i] = (hits_w >> (kb + i)) & 1u;
+                const bool any = ((hits_w >> k0) & 0xFFu) != 0;  // uniform per warp
                 if (any && !__all_sync(FULL_MASK, done)) {  // uniform per warp
                     float a_own[4];
 #pragma unroll
