@@ -70,6 +70,7 @@ struct Chunk {
     float2 ext[32];
     float4 conic[32];  // a, b, c, 0
     float4 col[32];    // r, g, b, opacity
+    unsigned hits[4];  // bit k: entry k's box touches the 8 x 4 pixel block of pixel warp w
     int count;
 };
 
@@ -185,6 +186,22 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
                     }
                 }
                 if (lane == 0) ch.count = filled;
+                __syncwarp();
+                {
+                    // Which entries touch each pixel warp's 8 x 4 block: the pixel warps test bits.
+                    const bool valid = lane < filled;
+                    const float2 mm = valid ? ch.mean[lane] : make_float2(0.0f, 0.0f);
+                    const float2 ee = valid ? ch.ext[lane] : make_float2(-1e30f, -1e30f);
+#pragma unroll
+                    for (int w = 0; w < 4; w++) {
+                        const float bx0 = (float)(x0 + (w & 1) * 8) + 0.5f;
+                        const float by0 = (float)(y0 + (w >> 1) * 4) + 0.5f;
+                        const unsigned mask =
+                            __ballot_sync(FULL_MASK, valid && box_hits(mm, ee, bx0, bx0 + 7.0f, by0, by0 + 3.0f));
+                        if (lane == 0) ch.hits[w] = mask;
+                    }
+                }
+                __syncwarp();
                 tc::mbar_arrive(&s_geo_full[s]);  // every lane, after its own writes
                 cursor = min(cur, count);
             }
@@ -228,8 +245,6 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
         const int py = y0 + (warp >> 1) * 4 + (lane >> 3);
         const bool inside = px < width && py < height;
         const float cx = (float)px + 0.5f, cy = (float)py + 0.5f;
-        const float wx0 = (float)(x0 + (warp & 1) * 8) + 0.5f, wx1 = wx0 + 7.0f;
-        const float wy0 = (float)(y0 + (warp >> 1) * 4) + 0.5f, wy1 = wy0 + 3.0f;
         const bool rgb = image4 != nullptr;
 
         float T = 1.0f, ar = 0.0f, ag = 0.0f, ab = 0.0f;
@@ -254,6 +269,7 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
             // A operand (K-major, no swizzle): row m = tid, K-quad qd at qd*A_LBO + (m/8)*128 + (m%8)*16.
             float* a_row = reinterpret_cast<float*>(smem + s * Cfg::A_BYTES + (tid >> 3) * 128 + (tid & 7) * 16);
             const bool warp_done = __all_sync(FULL_MASK, done);
+            const unsigned hits_w = ch.hits[warp];  // entries whose box touches this warp's pixels
 #pragma unroll 1
             for (int qd = 0; qd < Cfg::KC / 4; qd++) {
                 float w4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -262,7 +278,7 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
                     for (int e = 0; e < 4; e++) {
                         const int k = qd * 4 + e;
                         float w = 0.0f;
-                        if (k < valid && !done && box_hits(ch.mean[k], ch.ext[k], wx0, wx1, wy0, wy1)) {
+                        if (((hits_w >> k) & 1u) && !done) {
                             const float2 m = ch.mean[k];
                             const float4 q = ch.conic[k];
                             const float4 col = ch.col[k];
