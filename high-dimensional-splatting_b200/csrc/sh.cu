@@ -11,6 +11,9 @@ namespace hds {
 namespace {
 
 constexpr int SH_BLOCK = 128;
+// One gaussian's 48 SH values per shared-memory row, plus one pad word: with an odd stride the threads
+// of a warp, each reading its own row, hit 32 different banks (a stride of 48 puts them on two).
+constexpr int SH_STRIDE = 49;
 
 // Real SH normalisation constants of degrees 0-3 (the standard table of the 3DGS code base).
 __constant__ float SHC[16] = {
@@ -57,14 +60,15 @@ __device__ __forceinline__ void basis_grad(float x, float y, float z, float* bx,
 __global__ void __launch_bounds__(SH_BLOCK) sh_forward_kernel(int n, int k, const float* __restrict__ sh_dc,
                                                               const float* __restrict__ sh_rest, const float* __restrict__ dirs,
                                                               const float* __restrict__ radii, float* __restrict__ rgb) {
-    __shared__ float s_w[SH_BLOCK * 48];
+    __shared__ float s_w[SH_BLOCK * SH_STRIDE];
     const int first = blockIdx.x * SH_BLOCK;
     const int count = min(SH_BLOCK, n - first);
-    // Interleave dc and rest per gaussian in shared memory: w[j][c] at s_w[i*48 + j*3 + c].
-    for (int t = threadIdx.x; t < count * 3; t += SH_BLOCK) s_w[(t / 3) * 48 + t % 3] = sh_dc[(size_t)first * 3 + t];
+    // Interleave dc and rest per gaussian in shared memory: w[j][c] at s_w[i*SH_STRIDE + j*3 + c].
+    for (int t = threadIdx.x; t < count * 3; t += SH_BLOCK)
+        s_w[(t / 3) * SH_STRIDE + t % 3] = sh_dc[(size_t)first * 3 + t];
     if (k > 1)
         for (int t = threadIdx.x; t < count * 45; t += SH_BLOCK)
-            s_w[(t / 45) * 48 + 3 + t % 45] = sh_rest[(size_t)first * 45 + t];
+            s_w[(t / 45) * SH_STRIDE + 3 + t % 45] = sh_rest[(size_t)first * 45 + t];
     __syncthreads();
     int i = first + threadIdx.x;
     if (threadIdx.x >= count) return;
@@ -72,7 +76,7 @@ __global__ void __launch_bounds__(SH_BLOCK) sh_forward_kernel(int n, int k, cons
     if (radii[i] > 0.0f) {
         float b[16];
         basis(dirs[3 * i], dirs[3 * i + 1], dirs[3 * i + 2], b);
-        const float* w = s_w + threadIdx.x * 48;
+        const float* w = s_w + threadIdx.x * SH_STRIDE;
         float v[3];
 #pragma unroll
         for (int c = 0; c < 3; c++) {
@@ -87,7 +91,8 @@ __global__ void __launch_bounds__(SH_BLOCK) sh_forward_kernel(int n, int k, cons
     rgb[3 * i + 2] = out.z;
 }
 
-// Gradients of one gaussian into shared memory (g[j*3+c], j < 16) and dL/ddir into registers.
+// Gradients of one gaussian into shared memory (g[j*3+c], j < 16) and dL/ddir into registers.  g may
+// be w itself: every w[j*3+c] is read before g[j*3+c] is written.
 __device__ __forceinline__ float3 sh_grads(int i, int k, const float* w, const float* __restrict__ grad_rgb,
                                            const float* __restrict__ dirs, const float* __restrict__ radii, float* g) {
     float3 dd = make_float3(0.0f, 0.0f, 0.0f);
@@ -111,8 +116,9 @@ __device__ __forceinline__ float3 sh_grads(int i, int k, const float* w, const f
         float t = 0.0f;
 #pragma unroll
         for (int c = 0; c < 3; c++) {
+            const float wv = j < k ? w[j * 3 + c] : 0.0f;
             g[j * 3 + c] = j < k ? b[j] * gc[c] : 0.0f;
-            if (j < k) t += w[j * 3 + c] * gc[c];
+            t += wv * gc[c];
         }
         if (j < k) { dd.x += t * bx[j]; dd.y += t * by[j]; dd.z += t * bz[j]; }
     }
@@ -146,31 +152,34 @@ __global__ void __launch_bounds__(SH_BLOCK) sh_backward_kernel(int n, int k, con
                                                                float* __restrict__ grad_rest, float* __restrict__ grad_dirs,
                                                                float* m_dc, float* v_dc, float* m_rest, float* v_rest,
                                                                const float* step_dc, const float* step_rest, Adam adam) {
-    __shared__ float s_w[SH_BLOCK * 48];
-    __shared__ float s_g[SH_BLOCK * 48];
+    // Each row holds a gaussian's SH values, then (in place) their gradients.
+    __shared__ float s_w[SH_BLOCK * SH_STRIDE];
+    float* s_g = s_w;
     const int first = blockIdx.x * SH_BLOCK;
     const int count = min(SH_BLOCK, n - first);
-    for (int t = threadIdx.x; t < count * 3; t += SH_BLOCK) s_w[(t / 3) * 48 + t % 3] = sh_dc[(size_t)first * 3 + t];
+    for (int t = threadIdx.x; t < count * 3; t += SH_BLOCK)
+        s_w[(t / 3) * SH_STRIDE + t % 3] = sh_dc[(size_t)first * 3 + t];
     for (int t = threadIdx.x; t < count * 45; t += SH_BLOCK)
-        s_w[(t / 45) * 48 + 3 + t % 45] = sh_rest[(size_t)first * 45 + t];
+        s_w[(t / 45) * SH_STRIDE + 3 + t % 45] = sh_rest[(size_t)first * 45 + t];
     __syncthreads();
     if (threadIdx.x < count) {
         int i = first + threadIdx.x;
-        float3 dd = sh_grads(i, k, s_w + threadIdx.x * 48, grad_rgb, dirs, radii, s_g + threadIdx.x * 48);
+        float3 dd = sh_grads(i, k, s_w + threadIdx.x * SH_STRIDE, grad_rgb, dirs, radii, s_g + threadIdx.x * SH_STRIDE);
         grad_dirs[3 * i] = dd.x;
         grad_dirs[3 * i + 1] = dd.y;
         grad_dirs[3 * i + 2] = dd.z;
     }
     __syncthreads();
     if (ADAM) {
-        adam_slice(sh_dc + (size_t)first * 3, m_dc + (size_t)first * 3, v_dc + (size_t)first * 3, s_g, 48, 0, 3, count,
+        adam_slice(sh_dc + (size_t)first * 3, m_dc + (size_t)first * 3, v_dc + (size_t)first * 3, s_g, SH_STRIDE, 0, 3, count,
                    *step_dc, adam.lr_dc, adam);
-        adam_slice(sh_rest + (size_t)first * 45, m_rest + (size_t)first * 45, v_rest + (size_t)first * 45, s_g, 48, 3, 45,
+        adam_slice(sh_rest + (size_t)first * 45, m_rest + (size_t)first * 45, v_rest + (size_t)first * 45, s_g, SH_STRIDE, 3, 45,
                    count, *step_rest, adam.lr_rest, adam);
     } else {
-        for (int t = threadIdx.x; t < count * 3; t += SH_BLOCK) grad_dc[(size_t)first * 3 + t] = s_g[(t / 3) * 48 + t % 3];
+        for (int t = threadIdx.x; t < count * 3; t += SH_BLOCK)
+            grad_dc[(size_t)first * 3 + t] = s_g[(t / 3) * SH_STRIDE + t % 3];
         for (int t = threadIdx.x; t < count * 45; t += SH_BLOCK)
-            grad_rest[(size_t)first * 45 + t] = s_g[(t / 45) * 48 + 3 + t % 45];
+            grad_rest[(size_t)first * 45 + t] = s_g[(t / 45) * SH_STRIDE + 3 + t % 45];
     }
 }
 
