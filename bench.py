@@ -177,21 +177,22 @@ def render_view(wl, i, pose, gt_u8):
     from hds_b200.loss import l1_loss, ssim
     from hds_b200.projection import project_gaussians
     from hds_b200.rasterizer import accumulate_leaf_grads, rasterize
-    from hds_b200.sh import eval_sh_grad
+    from hds_b200.sh import view_colors
 
     cam = wl["cams"][wl["views"][i]]
     L = wl["leaves"]
     means2D, depths, radii, conics = project_gaussians(L["means"], L["scales"], L["quats"], L["opacities"], pose,
                                                        cam.fx, cam.fy, cam.cx, cam.cy, cam.width, cam.height)
     center = -(pose[:3, :3].T @ pose[:3, 3])
-    dirs = torch.nn.functional.normalize(L["means"] - center, dim=-1)
-    colors = eval_sh_grad(L["sh_dc"], L["sh_rest"], dirs, 3, radii)
-    # The views of a step accumulate into the gradient bucket: the feature backward adds straight into it.
+    # The views of a step accumulate into the gradient bucket: the SH and feature backward passes add
+    # straight into it.  view_colors forms normalize(means - center) inside the SH kernels.
     with accumulate_leaf_grads():
+        colors = view_colors(L["sh_dc"], L["sh_rest"], L["means"], center, 3, radii)
         image, feat = rasterize(means2D, depths, radii, conics, colors, L["opacities"], cam.width, cam.height,
                                 wl["bg"], L["features"])
     gt = gt_u8.float() / 255.0
     loss = 0.8 * l1_loss(image, gt) + 0.2 * (1.0 - ssim(image, gt))
+    wl["bucket"].ready()  # the step's gradient clear ran on a side stream during the forward
     torch.autograd.backward([loss, feat], [None, wl["feat_grad"]])
     return loss.detach()
 
@@ -216,7 +217,7 @@ def run_step(wl, dist, e2e: bool):
 
 
 def zero_grads(wl):
-    wl["bucket"].zero()
+    wl["bucket"].zero_async()
 
 
 def tile_stats(wl, device):

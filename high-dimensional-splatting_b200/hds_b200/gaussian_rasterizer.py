@@ -3,9 +3,10 @@
 Exports the ten entry points of gaussian_splatting/rasterizer/bindings.cpp:4-43 with the same
 argument order, tensor layouts, return tuples and error messages, implemented on libhds_b200.so.
 Outputs are allocated with torch's caching allocator on the inputs' device and all work is queued
-on the current CUDA stream.  Two additive entry points serve this package's own autograd layer:
-``rasterize_with_features`` (one walk producing RGB and features) and ``eval_sh_backward`` (plain
-SH gradients, for data-parallel training that all-reduces them).
+on the current CUDA stream.  Additive entry points serve this package's own autograd layer:
+``rasterize_with_features`` (one walk producing RGB and features), ``rasterize_backward_fused`` (one
+walk for both backward passes), ``eval_sh_backward`` (plain SH gradients, for data-parallel training
+that all-reduces them) and the ``*_into`` forms that add a gradient into a caller's buffer.
 """
 from __future__ import annotations
 
@@ -247,6 +248,48 @@ def eval_sh_backward(grad_rgb, sh_dc, sh_rest, dirs, degree: int, radii):
     check(lib.hds_eval_sh_backward(n, int(degree), ptr(grad_rgb), ptr(sh_dc), ptr(sh_rest), ptr(dirs), ptr(radii),
                                    ptr(gdc), ptr(grest), ptr(gd), stream_of(sh_dc.device)))
     return gdc, grest, gd
+
+
+def eval_sh_backward_into(grad_sh_dc, grad_sh_rest, grad_rgb, sh_dc, sh_rest, dirs, degree: int, radii):
+    """Plain SH backward that adds dL/dsh_dc and dL/dsh_rest into the given contiguous float32 buffers
+    (shaped like sh_dc and sh_rest); returns dL/ddirs [N,3]."""
+    n = sh_dc.shape[0]
+    for name, buf, like in (("grad_sh_dc", grad_sh_dc, sh_dc), ("grad_sh_rest", grad_sh_rest, sh_rest)):
+        if buf.shape != like.shape or buf.dtype != _F32 or not buf.is_contiguous() or buf.device != like.device:
+            raise ValueError(f"{name} must be a contiguous float32 tensor of shape {tuple(like.shape)}")
+    gd = torch.empty_like(dirs)
+    check(lib.hds_eval_sh_backward_accumulate(n, int(degree), ptr(grad_rgb), ptr(sh_dc), ptr(sh_rest), ptr(dirs),
+                                              ptr(radii), ptr(grad_sh_dc), ptr(grad_sh_rest), ptr(gd),
+                                              stream_of(sh_dc.device)))
+    return gd
+
+
+def eval_sh_view(sh_dc, sh_rest, means, camera_center, degree: int, radii):
+    """eval_sh of the directions normalize(means - camera_center) formed in the kernel (the reference's
+    Gaussian.colors, utils/gaussian.py:100-112, in one launch).  camera_center: [3] on the device."""
+    n = sh_dc.shape[0]
+    rgb = torch.empty(n, 3, dtype=_F32, device=sh_dc.device)
+    check(lib.hds_eval_sh_forward_view(n, int(degree), ptr(sh_dc), ptr(sh_rest), ptr(means), ptr(camera_center),
+                                       ptr(radii), ptr(rgb), stream_of(sh_dc.device)))
+    return rgb
+
+
+def eval_sh_view_backward(grad_rgb, sh_dc, sh_rest, means, camera_center, degree: int, radii, into=None):
+    """Backward of eval_sh_view: (dL/dsh_dc, dL/dsh_rest, dL/dmeans).  With into = (grad_sh_dc,
+    grad_sh_rest, grad_means), contiguous float32 buffers shaped like sh_dc, sh_rest and means, the
+    three gradients are added to them instead, and those buffers are returned."""
+    n = sh_dc.shape[0]
+    if into is None:
+        bufs, accumulate = (torch.empty_like(sh_dc), torch.empty_like(sh_rest), torch.empty_like(means)), 0
+    else:
+        bufs, accumulate = tuple(into), 1
+        for name, buf, like in zip(("grad_sh_dc", "grad_sh_rest", "grad_means"), bufs, (sh_dc, sh_rest, means)):
+            if buf.shape != like.shape or buf.dtype != _F32 or not buf.is_contiguous() or buf.device != like.device:
+                raise ValueError(f"{name} must be a contiguous float32 tensor of shape {tuple(like.shape)}")
+    check(lib.hds_eval_sh_backward_view(n, int(degree), ptr(grad_rgb), ptr(sh_dc), ptr(sh_rest), ptr(means),
+                                        ptr(camera_center), ptr(radii), ptr(bufs[0]), ptr(bufs[1]), ptr(bufs[2]),
+                                        accumulate, stream_of(sh_dc.device)))
+    return bufs
 
 
 def project_gaussians(means, scales, quats, opacities, world_to_camera, fx: float, fy: float, cx: float, cy: float,

@@ -26,6 +26,9 @@ SIGNATURES = {
     "hds_eval_sh_backward_adam": [c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, c_float, c_float, c_float, c_float,
                                   c_float, c_float, c_float, P, S],
     "hds_eval_sh_backward": [c_int, c_int, P, P, P, P, P, P, P, P, S],
+    "hds_eval_sh_backward_accumulate": [c_int, c_int, P, P, P, P, P, P, P, P, S],
+    "hds_eval_sh_forward_view": [c_int, c_int, P, P, P, P, P, P, S],
+    "hds_eval_sh_backward_view": [c_int, c_int, P, P, P, P, P, P, P, P, P, c_int, S],
     "hds_rasterize_prepare_scratch_bytes": [c_int],
     "hds_rasterize_prepare": [c_int, P, P, P, P, P, P, c_int, c_int, P, P, P, c_size_t, ctypes.POINTER(c_int64), S],
     "hds_rasterize_sort_scratch_bytes": [c_int, c_int64, c_int, c_int],

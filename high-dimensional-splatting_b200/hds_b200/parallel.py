@@ -77,18 +77,45 @@ class GradBucket:
         for p in params:
             self.views.append(self.flat[off:off + p.numel()].view_as(p))
             off += p.numel()
+        self._side = None      # stream of zero_async
+        self._pending = False  # a zero_async clear that the current stream has not waited for yet
 
     def attach(self) -> None:
         for p, v in zip(self.params, self.views):
             p.grad = v
 
     def zero(self) -> None:
+        self.ready()
         self.flat.zero_()
         self.attach()
+
+    def zero_async(self) -> None:
+        """zero() on a side stream, so that the clear overlaps the work queued after it (the forward
+        pass, which writes no gradient).  The clear starts once the current stream's earlier work is
+        done; ready() makes the current stream wait for it and must run before anything writes or
+        reads a gradient (the backward, all_reduce).  On a CPU bucket this is zero()."""
+        if self.flat.device.type != "cuda":
+            self.zero()
+            return
+        current = torch.cuda.current_stream(self.flat.device)
+        if self._side is None:
+            self._side = torch.cuda.Stream(self.flat.device)
+        self._side.wait_stream(current)
+        with torch.cuda.stream(self._side):
+            self.flat.zero_()
+        self._pending = True
+        self.attach()
+
+    def ready(self) -> None:
+        """Makes the current stream wait for a clear started by zero_async (no-op otherwise)."""
+        if self._pending:
+            torch.cuda.current_stream(self.flat.device).wait_stream(self._side)
+            self._pending = False
 
     def all_reduce(self, group=None) -> None:
         import torch.distributed as dist
 
+        self.ready()
         dist.all_reduce(self.flat, group=group)
         for p, v in zip(self.params, self.views):
             if p.grad is None or p.grad.data_ptr() != v.data_ptr():

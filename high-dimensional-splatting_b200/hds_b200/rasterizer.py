@@ -33,8 +33,9 @@ def _fused_backward(channels: int) -> bool:
 # When true, the backward of a rasterize call whose features are a leaf that already holds a
 # contiguous float32 .grad of its shape adds dL/dfeatures straight into that .grad (and hands
 # autograd no gradient for it), instead of returning a fresh [N, D] tensor that autograd then adds.
-# For loops that accumulate several views into one gradient buffer.  Hooks registered on the
-# features tensor are not run for that gradient.  Off by default (the reference's behaviour).
+# hds_b200.sh.eval_sh_grad does the same for sh_dc and sh_rest.  The flag is read when the forward
+# runs.  For loops that accumulate several views into one gradient buffer.  Hooks registered on
+# those tensors are not run for that gradient.  Off by default (the reference's behaviour).
 ACCUMULATE_INTO_LEAF_GRAD: bool = False
 
 

@@ -63,29 +63,99 @@ class EvalSH(torch.autograd.Function):
 eval_sh = EvalSH.apply
 
 
+def _grad_buffer(leaf, like):
+    """leaf.grad when it can take an in-place add of a gradient shaped like `like`, else None."""
+    g = leaf.grad
+    if (g is not None and g.is_contiguous() and g.dtype == torch.float32 and g.shape == like.shape
+            and g.device == like.device):
+        return g
+    return None
+
+
 class EvalSHGrad(torch.autograd.Function):
-    """Same colour as EvalSH; the backward returns dL/dsh_dc, dL/dsh_rest and dL/ddirs."""
+    """Same colour as EvalSH; the backward returns dL/dsh_dc, dL/dsh_rest and dL/ddirs.
+
+    Under hds_b200.rasterizer.accumulate_leaf_grads() (active during this forward), when sh_dc and
+    sh_rest are leaves that already hold float32 .grad buffers of their shapes, the backward adds the
+    SH gradients into those buffers and hands autograd none for them (hooks on the two tensors do not
+    see that gradient)."""
 
     @staticmethod
     def forward(ctx, sh_dc, sh_rest, dirs, degree, radii):
-        from .rasterizer import _get_rasterizer
+        from . import rasterizer
 
+        ctx.leaves = ((sh_dc, sh_rest) if (rasterizer.ACCUMULATE_INTO_LEAF_GRAD and sh_dc.is_leaf and sh_rest.is_leaf)
+                      else None)
         sh_dc, sh_rest, dirs, radii = sh_dc.contiguous(), sh_rest.contiguous(), dirs.contiguous(), radii.contiguous()
         ctx.save_for_backward(sh_dc, sh_rest, dirs, radii)
         ctx.degree = degree
-        return _get_rasterizer().eval_sh(sh_dc, sh_rest, dirs, degree, radii)
+        return rasterizer._get_rasterizer().eval_sh(sh_dc, sh_rest, dirs, degree, radii)
 
     @staticmethod
     def backward(ctx, grad_rgb):
         from .rasterizer import _get_rasterizer
 
         sh_dc, sh_rest, dirs, radii = ctx.saved_tensors
-        gdc, grest, gd = _get_rasterizer().eval_sh_backward(grad_rgb.contiguous(), sh_dc, sh_rest, dirs, ctx.degree,
-                                                            radii)
+        ext = _get_rasterizer()
+        if ctx.leaves is not None and ctx.needs_input_grad[0] and ctx.needs_input_grad[1]:
+            buf_dc, buf_rest = _grad_buffer(ctx.leaves[0], sh_dc), _grad_buffer(ctx.leaves[1], sh_rest)
+            if buf_dc is not None and buf_rest is not None:
+                gd = ext.eval_sh_backward_into(buf_dc, buf_rest, grad_rgb.contiguous(), sh_dc, sh_rest, dirs,
+                                               ctx.degree, radii)
+                return None, None, gd, None, None
+        gdc, grest, gd = ext.eval_sh_backward(grad_rgb.contiguous(), sh_dc, sh_rest, dirs, ctx.degree, radii)
         return gdc, grest, gd, None, None
 
 
 eval_sh_grad = EvalSHGrad.apply
+
+
+class ViewColors(torch.autograd.Function):
+    """RGB of every gaussian seen from camera_center: eval_sh of normalize(means - camera_center), with
+    the normalisation inside the SH kernels (the reference's Gaussian.colors, utils/gaussian.py:100-112,
+    runs it as torch glue).  The backward returns dL/dsh_dc, dL/dsh_rest, dL/dmeans and, when asked
+    for, dL/dcamera_center = -sum dL/dmeans.
+
+    Under hds_b200.rasterizer.accumulate_leaf_grads() (active during this forward), when sh_dc,
+    sh_rest and means are leaves that hold float32 .grad buffers of their shapes and the camera centre
+    needs no gradient, the backward adds its three gradients into those buffers and hands autograd
+    none for them (hooks on the three tensors do not see that gradient)."""
+
+    @staticmethod
+    def forward(ctx, sh_dc, sh_rest, means, camera_center, degree, radii):
+        from . import rasterizer
+
+        leaves = (sh_dc, sh_rest, means)
+        ctx.leaves = leaves if (rasterizer.ACCUMULATE_INTO_LEAF_GRAD and all(t.is_leaf for t in leaves)) else None
+        sh_dc, sh_rest, means, radii = sh_dc.contiguous(), sh_rest.contiguous(), means.contiguous(), radii.contiguous()
+        center = camera_center.detach().reshape(3).to(torch.float32).contiguous()
+        ctx.center_shape, ctx.center_dtype = camera_center.shape, camera_center.dtype
+        ctx.save_for_backward(sh_dc, sh_rest, means, center, radii)
+        ctx.degree = degree
+        return rasterizer._get_rasterizer().eval_sh_view(sh_dc, sh_rest, means, center, degree, radii)
+
+    @staticmethod
+    def backward(ctx, grad_rgb):
+        from .rasterizer import _get_rasterizer
+
+        sh_dc, sh_rest, means, center, radii = ctx.saved_tensors
+        ext = _get_rasterizer()
+        args = (grad_rgb.contiguous(), sh_dc, sh_rest, means, center, ctx.degree, radii)
+        if ctx.leaves is not None and all(ctx.needs_input_grad[:3]) and not ctx.needs_input_grad[3]:
+            bufs = [_grad_buffer(leaf, like) for leaf, like in zip(ctx.leaves, (sh_dc, sh_rest, means))]
+            if all(b is not None for b in bufs):
+                ext.eval_sh_view_backward(*args, into=bufs)
+                return None, None, None, None, None, None
+        gdc, grest, gmeans = ext.eval_sh_view_backward(*args)
+        gcenter = None
+        if ctx.needs_input_grad[3]:
+            gcenter = (-gmeans.sum(dim=0)).reshape(ctx.center_shape).to(ctx.center_dtype)
+        return gdc, grest, gmeans, gcenter, None, None
+
+
+def view_colors(sh_dc, sh_rest, means, camera_center, degree: int, radii):
+    """[N, 3] colours of the gaussians seen from camera_center [3] (zero where radii <= 0)."""
+    return ViewColors.apply(sh_dc, sh_rest, means, camera_center, degree, radii)
 
 
 def rgb_to_sh(rgb: torch.Tensor) -> torch.Tensor:

@@ -94,6 +94,26 @@ int hds_eval_sh_backward(int n, int degree, const float* grad_rgb, const float* 
                          const float* dirs, const float* radii, float* grad_sh_dc, float* grad_sh_rest,
                          float* grad_dirs, hds_stream_t stream);
 
+/* hds_eval_sh_backward that adds dL/dsh_dc and dL/dsh_rest to what grad_sh_dc and grad_sh_rest hold
+ * (dL/ddirs is written).  For loops that accumulate several views into one gradient buffer: it saves
+ * a fresh [n,16,3] gradient and the separate add into the buffer.  No counterpart in the reference. */
+int hds_eval_sh_backward_accumulate(int n, int degree, const float* grad_rgb, const float* sh_dc,
+                                    const float* sh_rest, const float* dirs, const float* radii, float* grad_sh_dc,
+                                    float* grad_sh_rest, float* grad_dirs, hds_stream_t stream);
+
+/* SH colour with the viewing directions formed in the kernel: dirs = normalize(means - camera_center)
+ * = x / max(|x|, 1e-12), the torch glue of the reference's Gaussian.colors (utils/gaussian.py:100-112)
+ * fused into eval_sh.  means [n,3]; camera_center: 3 floats in device memory. */
+int hds_eval_sh_forward_view(int n, int degree, const float* sh_dc, const float* sh_rest, const float* means,
+                             const float* camera_center, const float* radii, float* rgb, hds_stream_t stream);
+
+/* Backward of hds_eval_sh_forward_view: dL/dsh_dc, dL/dsh_rest and dL/dmeans (through the
+ * normalisation).  accumulate != 0 adds all three to what the buffers hold; 0 writes them.  The
+ * camera centre gets no gradient here (it is -sum dL/dmeans when the caller needs it). */
+int hds_eval_sh_backward_view(int n, int degree, const float* grad_rgb, const float* sh_dc, const float* sh_rest,
+                              const float* means, const float* camera_center, const float* radii, float* grad_sh_dc,
+                              float* grad_sh_rest, float* grad_means, int accumulate, hds_stream_t stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Binning + RGB blend.  Together these three calls replace rasterize (forward.cu:239-435).
  *

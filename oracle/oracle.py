@@ -142,6 +142,27 @@ def eval_sh_backward(grad_rgb, sh_dc, sh_rest, dirs, degree, radii):
     return gdc, grest, gd
 
 
+def view_dirs(means, camera_center):
+    """Viewing directions of the reference's Gaussian.colors (utils/gaussian.py:110):
+    torch.nn.functional.normalize(means - camera_center, dim=-1) = x / max(|x|, 1e-12), in float32 with
+    one rounding per operation and the squares summed x, y, z in order.  Returns (dirs [N,3], the
+    divisor s [N])."""
+    x = f32(means) - f32(camera_center).reshape(1, 3)
+    s = np.sqrt(x[:, 0] * x[:, 0] + x[:, 1] * x[:, 1] + x[:, 2] * x[:, 2])
+    s = np.maximum(s, np.float32(1e-12)).astype(np.float32)
+    return (x / s[:, None]).astype(np.float32), s
+
+
+def view_dirs_backward(grad_dirs, dirs, s):
+    """dL/dmeans of view_dirs from dL/ddirs: (g - dir (dir . g)) / s above the 1e-12 clamp, g / s at it
+    (the derivative of x / |x|; at the clamp the divisor is a constant)."""
+    g, d = f32(grad_dirs), f32(dirs)
+    dot = d[:, 0] * g[:, 0] + d[:, 1] * g[:, 1] + d[:, 2] * g[:, 2]
+    above = (s > np.float32(1e-12))[:, None]
+    out = np.where(above, (g - d * dot[:, None]) / s[:, None], g / s[:, None])
+    return out.astype(np.float32)
+
+
 def adam(p, m, v, g, step, lr, beta1, beta2, eps):
     """sh.cu:86-102, in place on copies; returns (p, m, v)."""
     p, m, v = f32(p).copy(), f32(m).copy(), f32(v).copy()

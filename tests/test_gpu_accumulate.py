@@ -70,3 +70,20 @@ def test_accumulate_requires_matching_grad_buffer():
     with pytest.raises(RuntimeError, match="shaped like features"):
         ext.rasterize_features_backward_into(bad, torch.zeros(4, 4, 32, device="cuda"), f, None, None, None, None,
                                              None, None, None, 4, 4, 32)
+
+
+def test_bucket_zero_async_clears_before_the_backward():
+    """GradBucket.zero_async clears on a side stream; after ready() the current stream sees zeros, and
+    gradients added afterwards land on the cleared buffer."""
+    from hds_b200 import parallel
+
+    params = [torch.randn(300_000, 3, device="cuda", requires_grad=True),
+              torch.randn(1000, 16, device="cuda", requires_grad=True)]
+    bucket = parallel.GradBucket(params)
+    for _ in range(3):
+        bucket.flat.fill_(7.0)
+        bucket.zero_async()
+        bucket.ready()
+        (params[0].sum() + 2.0 * params[1].sum()).backward()
+        assert torch.equal(params[0].grad, torch.ones_like(params[0]))
+        assert torch.equal(params[1].grad, torch.full_like(params[1], 2.0))

@@ -293,6 +293,168 @@ def test_sh_adam_matches_oracle_and_torch(ext, golden):
     np.testing.assert_allclose(host(v_rest), g["adam_v_rest"], rtol=1e-5, atol=1e-7)
 
 
+def _sh_inputs(n, seed):
+    rng = np.random.default_rng(seed)
+    sh = (0.5 * rng.standard_normal((n, 16, 3))).astype(np.float32)
+    d = rng.standard_normal((n, 3))
+    dirs = (d / np.linalg.norm(d, axis=1, keepdims=True)).astype(np.float32)
+    radii = rng.integers(0, 3, n).astype(np.float32)  # about a third culled
+    grad_rgb = rng.standard_normal((n, 3)).astype(np.float32)
+    return np.ascontiguousarray(sh[:, :1]), np.ascontiguousarray(sh[:, 1:]), dirs, radii, grad_rgb
+
+
+def _placed(a, offset):
+    """A CUDA copy of `a` that starts `offset` floats into a larger buffer (offset 1 breaks 16-byte
+    alignment and sends the SH kernels down their element-by-element path)."""
+    flat = torch.zeros(a.size + offset, dtype=torch.float32, device="cuda")
+    flat[offset:] = torch.from_numpy(np.ascontiguousarray(a).reshape(-1)).cuda()
+    return flat[offset:].view(a.shape)
+
+
+@pytest.mark.parametrize("n,offset", [(1000, 0), (1000, 1), (128, 0), (37, 0)])
+@pytest.mark.parametrize("degree", [0, 3])
+def test_sh_blocks_and_alignment(ext, n, offset, degree):
+    """Whole 128-gaussian blocks (vector loads), a partial last block and unaligned inputs (element
+    loads) give the oracle's colours and gradients bit for bit; the accumulating backward adds
+    exactly the plain gradient to what its buffers hold."""
+    dc, rest, dirs, radii, grad_rgb = _sh_inputs(n, 7 * n + offset)
+    t_dc, t_rest = _placed(dc, offset), _placed(rest, offset)
+    t_dirs, t_radii, t_grad = cuda(dirs, radii, grad_rgb)
+    assert np.array_equal(host(ext.eval_sh(t_dc, t_rest, t_dirs, degree, t_radii)),
+                          oracle.eval_sh(dc, rest, dirs, degree, radii))
+    want = oracle.eval_sh_backward(grad_rgb, dc, rest, dirs, degree, radii)
+    got = ext.eval_sh_backward(t_grad, t_dc, t_rest, t_dirs, degree, t_radii)
+    for nm, a, b in zip(("dc", "rest", "dirs"), got, want):
+        assert np.array_equal(host(a), b), f"grad {nm} differs"
+    rng = np.random.default_rng(n)
+    base_dc = rng.standard_normal(dc.shape).astype(np.float32)
+    base_rest = rng.standard_normal(rest.shape).astype(np.float32)
+    buf_dc, buf_rest = _placed(base_dc, offset), _placed(base_rest, offset)
+    gd = ext.eval_sh_backward_into(buf_dc, buf_rest, t_grad, t_dc, t_rest, t_dirs, degree, t_radii)
+    assert np.array_equal(host(buf_dc), base_dc + want[0])
+    assert np.array_equal(host(buf_rest), base_rest + want[1])
+    assert np.array_equal(host(gd), want[2])
+
+
+@pytest.mark.parametrize("n,offset", [(1000, 0), (1000, 1)])
+def test_sh_adam_blocks_and_alignment(ext, n, offset):
+    """The fused Adam step on whole blocks (float4 parameter and moment traffic), a partial block and
+    unaligned buffers, against the oracle's gradient and Adam."""
+    dc, rest, dirs, radii, _ = _sh_inputs(n, 11 * n + offset)
+    t_dc, t_rest = _placed(dc, offset), _placed(rest, offset)
+    t_dirs, t_radii = cuda(dirs, radii)
+    m_dc, v_dc = _placed(np.zeros_like(dc), offset), _placed(np.zeros_like(dc), offset)
+    m_rest, v_rest = _placed(np.zeros_like(rest), offset), _placed(np.zeros_like(rest), offset)
+    step = torch.zeros((), device="cuda")
+    o_dc, o_rest = (np.zeros_like(dc), np.zeros_like(dc)), (np.zeros_like(rest), np.zeros_like(rest))
+    rng = np.random.default_rng(n + offset)
+    for k in range(1, 4):
+        grad_rgb = rng.standard_normal((n, 3)).astype(np.float32)
+        step += 1
+        ext.eval_sh_backward_adam(cuda(grad_rgb)[0], t_dc, t_rest, t_dirs, 3, t_radii, m_dc, v_dc, m_rest, v_rest,
+                                  step, step, 0.0025, 0.0025 / 20, 0.9, 0.999, 1e-15)
+        gdc, grest, _ = oracle.eval_sh_backward(grad_rgb, dc, rest, dirs, 3, radii)
+        dc, *o_dc = oracle.adam(dc, *o_dc, gdc, k, 0.0025, 0.9, 0.999, 1e-15)
+        rest, *o_rest = oracle.adam(rest, *o_rest, grest, k, 0.0025 / 20, 0.9, 0.999, 1e-15)
+    np.testing.assert_allclose(host(t_dc), dc, rtol=1e-6, atol=1e-7)
+    np.testing.assert_allclose(host(t_rest), rest, rtol=1e-6, atol=1e-7)
+    np.testing.assert_allclose(host(m_rest), o_rest[0], rtol=1e-6, atol=1e-7)
+    np.testing.assert_allclose(host(v_rest), o_rest[1], rtol=1e-6, atol=1e-7)
+
+
+def _view_inputs(n, seed):
+    dc, rest, _, radii, grad_rgb = _sh_inputs(n, seed)
+    rng = np.random.default_rng(seed + 1)
+    center = rng.standard_normal(3).astype(np.float32)
+    means = (center + 5.0 * rng.standard_normal((n, 3))).astype(np.float32)
+    means[3] = center  # |means - center| = 0: the 1e-12 clamp of normalize
+    radii[3] = 1.0
+    return dc, rest, means, center, radii, grad_rgb
+
+
+@pytest.mark.parametrize("n", [1000, 128, 37])
+@pytest.mark.parametrize("degree", [0, 3])
+def test_sh_view_bit_exact(ext, n, degree):
+    """eval_sh_view forms normalize(means - camera_center) in the kernel: colours, SH gradients and
+    dL/dmeans equal the oracle's float32 restatement bit for bit, including a mean at the centre."""
+    dc, rest, means, center, radii, grad_rgb = _view_inputs(n, 5 * n + degree)
+    dirs, s = oracle.view_dirs(means, center)
+    t_dc, t_rest, t_means, t_center, t_radii, t_grad = cuda(dc, rest, means, center, radii, grad_rgb)
+    assert np.array_equal(host(ext.eval_sh_view(t_dc, t_rest, t_means, t_center, degree, t_radii)),
+                          oracle.eval_sh(dc, rest, dirs, degree, radii))
+    gdc, grest, gdirs = oracle.eval_sh_backward(grad_rgb, dc, rest, dirs, degree, radii)
+    gmeans = oracle.view_dirs_backward(gdirs, dirs, s)
+    got = ext.eval_sh_view_backward(t_grad, t_dc, t_rest, t_means, t_center, degree, t_radii)
+    for nm, a, b in zip(("dc", "rest", "means"), got, (gdc, grest, gmeans)):
+        assert np.array_equal(host(a), b), f"grad {nm} differs"
+    rng = np.random.default_rng(n)
+    bases = [rng.standard_normal(a.shape).astype(np.float32) for a in (dc, rest, means)]
+    bufs = cuda(*bases)
+    ext.eval_sh_view_backward(t_grad, t_dc, t_rest, t_means, t_center, degree, t_radii, into=bufs)
+    for nm, buf, base, g in zip(("dc", "rest", "means"), bufs, bases, (gdc, grest, gmeans)):
+        assert np.array_equal(host(buf), base + g), f"accumulated grad {nm} differs"
+
+
+@pytest.mark.parametrize("accumulate", [False, True])
+def test_view_colors_matches_torch_normalize(ext, accumulate):
+    """view_colors against the reference's composition, F.normalize(means - camera_center) followed by
+    the SH node, through autograd: same colours, and gradients within the gradient tolerance (torch's
+    normalize backward rounds differently).  With accumulate_leaf_grads the gradients land in the
+    leaves' existing .grad buffers; a camera centre that needs a gradient gets -sum dL/dmeans."""
+    import torch.nn.functional as F
+
+    from hds_b200.rasterizer import accumulate_leaf_grads
+    from hds_b200.sh import eval_sh_grad, view_colors
+
+    dc, rest, means, center, radii, grad_rgb = _view_inputs(3000, 17)
+    means[3] += 1.0  # keep the reference composition away from its clamp, where torch's gradient is 0 * inf
+    t_radii, t_grad = cuda(radii, grad_rgb)
+
+    def leaves(center_grad):
+        out = [torch.from_numpy(a).cuda().requires_grad_(True) for a in (dc, rest, means)]
+        return out + [torch.from_numpy(center).cuda().requires_grad_(center_grad)]
+
+    r_dc, r_rest, r_means, r_center = leaves(True)
+    ref = eval_sh_grad(r_dc, r_rest, F.normalize(r_means - r_center, dim=-1), 3, t_radii)
+    ref.backward(t_grad)
+
+    o_dc, o_rest, o_means, o_center = leaves(not accumulate)
+    if accumulate:
+        for t in (o_dc, o_rest, o_means):
+            t.grad = torch.zeros_like(t)
+    with accumulate_leaf_grads() if accumulate else torch.enable_grad():
+        rgb = view_colors(o_dc, o_rest, o_means, o_center, 3, t_radii)
+    rgb.backward(t_grad)
+    np.testing.assert_allclose(host(rgb), host(ref), rtol=0, atol=1e-5)
+    for nm, a, b in (("sh_dc", o_dc, r_dc), ("sh_rest", o_rest, r_rest), ("means", o_means, r_means)):
+        assert_grads_close(host(a.grad), host(b.grad), nm)
+    if not accumulate:
+        assert_grads_close(host(o_center.grad), host(r_center.grad), "camera_center")
+
+
+def test_sh_grad_accumulates_into_leaf_grads(ext):
+    """eval_sh_grad under accumulate_leaf_grads adds its SH gradients into existing leaf .grad buffers
+    (and returns the same dL/ddirs); without buffers it falls back to autograd's own accumulation."""
+    from hds_b200.rasterizer import accumulate_leaf_grads
+    from hds_b200.sh import eval_sh_grad
+
+    dc, rest, dirs, radii, grad_rgb = _sh_inputs(700, 3)
+    want = oracle.eval_sh_backward(grad_rgb, dc, rest, dirs, 3, radii)
+    for preset in (True, False):
+        t_dc, t_rest = (torch.from_numpy(a).cuda().requires_grad_(True) for a in (dc, rest))
+        t_dirs = torch.from_numpy(dirs).cuda().requires_grad_(True)
+        t_radii, t_grad = cuda(radii, grad_rgb)
+        if preset:
+            t_dc.grad, t_rest.grad = torch.ones_like(t_dc), torch.ones_like(t_rest)
+        with accumulate_leaf_grads():
+            rgb = eval_sh_grad(t_dc, t_rest, t_dirs, 3, t_radii)
+        rgb.backward(t_grad)
+        base = 1.0 if preset else 0.0
+        assert np.array_equal(host(t_dc.grad), want[0] + np.float32(base))
+        assert np.array_equal(host(t_rest.grad), want[1] + np.float32(base))
+        assert np.array_equal(host(t_dirs.grad), want[2])
+
+
 @pytest.mark.parametrize("size", ["64x64", "37x53", "11x11", "546x979"])
 def test_ssim_bit_exact(ext, golden, size):
     if size == "546x979":

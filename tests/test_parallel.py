@@ -34,6 +34,16 @@ def test_row_bands_partition_whole_tile_rows(height, world):
             assert y0 % 16 == 0 and y1 > y0
 
 
+def test_bucket_zero_async_on_cpu_is_zero():
+    params = [torch.randn(10, 3, requires_grad=True), torch.randn(4, requires_grad=True)]
+    bucket = parallel.GradBucket(params)
+    bucket.flat.fill_(3.0)
+    bucket.zero_async()
+    bucket.ready()
+    assert all(p.grad is v for p, v in zip(params, bucket.views))
+    assert torch.count_nonzero(bucket.flat) == 0
+
+
 def band_render_np(inputs, width, y0, y1, background):
     m2, dep, rad, con, col, opac = inputs
     shifted = m2 - np.array([0.0, y0], np.float32)
