@@ -2,13 +2,18 @@
 // tile ranges.  Restates forward.cu:13-139 and 284-404 of the reference, replacing its thrust scan
 // and CUB onesweep sort with this file's own kernels.
 //
-// Keys are tile << 32 | float bits of the (positive) depth, so sorting them stably orders every
-// tile's list front to back with equal depths kept in gaussian order -- the order the reference's
-// stable CUB sort produces and the CPU oracle's stable sort reproduces bit for bit.
+// The reference sorts one 64-bit key per (tile, gaussian) pair, tile << 32 | float bits of the
+// depth, stably from gaussian order: every tile's list runs front to back, equal depths in gaussian
+// order.  This file reaches the same order in two smaller sorts:
+//   1. the gaussians that touch a tile are sorted stably by their 32 depth bits (4 passes over n
+//      keys; gaussians that touch none get the largest key and sit, unused, at the end);
+//   2. the pairs are emitted in that depth order and sorted stably by tile id alone (ceil(log2
+//      tiles) bits, 2 passes for up to 65536 tiles, over the pairs).
+// Stability carries the (depth, gaussian) order of step 1 into every tile's list.  Against a single
+// 64-bit sort of the pairs this moves 4 n + 2 P keys instead of 6 P (P = pairs, about 3 n here).
 //
-// Sort: least-significant-digit radix sort, 8 bits per pass over bits [0, 32 + ceil(log2 tiles)).
-// Each pass is (1) a per-block digit histogram, (2) an exclusive scan of the digit-major count
-// table, (3) a stable scatter that ranks each key among equal digits of its block with
+// Each radix pass is (1) a per-block digit histogram, (2) an exclusive scan of the digit-major
+// count table, (3) a stable scatter that ranks each key among equal digits of its block with
 // __match_any_sync.  No inter-block waits, so nothing can spin.
 #include "hds_common.cuh"
 
@@ -113,6 +118,22 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_apply_kernel(const T* __res
 
 inline int64_t scan_blocks(int64_t n) { return (n + SCAN_TILE - 1) / SCAN_TILE; }
 
+// Sum of n items into *total_out (device): the first two launches of exclusive_scan.
+template <typename T>
+int reduce_total(const T* in, int64_t n, T* block_sums, T* total_out, cudaStream_t stream) {
+    int64_t nb = scan_blocks(n);
+    HDS_REQUIRE(nb <= SCAN_TILE, HDS_ERR_TOO_LARGE, "sum of %lld items exceeds %d", (long long)n, SCAN_TILE * SCAN_TILE);
+    if (n == 0) {
+        HDS_CHECK_CUDA(cudaMemsetAsync(total_out, 0, sizeof(T), stream));
+        return HDS_OK;
+    }
+    scan_reduce_kernel<T><<<(unsigned)nb, SCAN_THREADS, 0, stream>>>(in, n, block_sums);
+    scan_block_sums_kernel<T><<<1, SCAN_THREADS, 0, stream>>>(block_sums, (int)nb, total_out);
+    note_launches(1);
+    HDS_CHECK_LAUNCH("reduce_total");
+    return HDS_OK;
+}
+
 // Exclusive scan of n items; block_sums holds scan_blocks(n) entries; *total_out (device) gets the sum.
 template <typename T>
 int exclusive_scan(const T* in, T* out, int64_t n, T* block_sums, T* total_out, cudaStream_t stream) {
@@ -156,30 +177,87 @@ __global__ void __launch_bounds__(256) prepare_kernel(int n, const float2* __res
 }
 
 // ---------------------------------------------------------------------------------------------
-// key emission (forward.cu:63-113): one thread per pair, owner found by binary search
+// depth sort of the gaussians, then pair emission in depth order (forward.cu:63-113)
 // ---------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) emit_kernel(int64_t total, int n, const int64_t* __restrict__ offsets,
-                                                   const int4* __restrict__ rect, int tiles_x, uint64_t* __restrict__ keys,
-                                                   int32_t* __restrict__ values) {
-    int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (o >= total) return;
-    int lo = 0, hi = n - 1;
-    while (lo < hi) {  // largest g with offsets[g] <= o
+constexpr uint32_t NO_TILES_KEY = 0xffffffffu;
+
+__global__ void __launch_bounds__(256) gaussian_keys_kernel(int n, const int4* __restrict__ rect,
+                                                            const int64_t* __restrict__ touched,
+                                                            uint32_t* __restrict__ keys, int32_t* __restrict__ values) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    keys[i] = touched[i] > 0 ? (uint32_t)rect[i].w : NO_TILES_KEY;
+    values[i] = i;
+}
+
+// Pair counts in depth order, for the scan that places each gaussian's pairs.
+__global__ void __launch_bounds__(256) sorted_counts_kernel(int n, const int32_t* __restrict__ order,
+                                                            const int64_t* __restrict__ touched,
+                                                            int64_t* __restrict__ counts) {
+    int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j < n) counts[j] = touched[order[j]];
+}
+
+// Largest j in [lo, hi] with offsets[j] <= o: the owner of pair o (gaussians without pairs share
+// their successor's offset and are skipped).
+template <typename T>
+__device__ __forceinline__ int owner_of(const T* offsets, int lo, int hi, int64_t o) {
+    while (lo < hi) {
         int mid = (lo + hi + 1) >> 1;
         if (offsets[mid] <= o) lo = mid; else hi = mid - 1;
     }
-    int4 r = rect[lo];
-    int local = (int)(o - offsets[lo]);
-    int tx = r.x + local % r.z, ty = r.y + local / r.z;
-    keys[o] = ((uint64_t)(uint32_t)(ty * tiles_x + tx) << 32) | (uint32_t)r.w;
-    values[o] = lo;
+    return lo;
+}
+
+constexpr int EMIT_THREADS = 256;
+constexpr int EMIT_TILE = 2048;  // pairs per block
+
+// One block per 2048 consecutive pairs: the owners of its first and last pair bound the gaussians it
+// needs, whose offsets it stages in shared memory and searches there.  Every gaussian strictly
+// between two owners has at least one pair, so a block spans at most 2048 gaussians; a longer span
+// (which would need pairless gaussians among the pair owners) searches global memory instead.
+__global__ void __launch_bounds__(EMIT_THREADS) emit_kernel(int64_t total, int n, const int64_t* __restrict__ offsets,
+                                                            const int32_t* __restrict__ order,
+                                                            const int4* __restrict__ rect, int tiles_x,
+                                                            uint32_t* __restrict__ tile_keys,
+                                                            int32_t* __restrict__ values) {
+    __shared__ int64_t s_off[EMIT_TILE];
+    __shared__ int s_owner[2];
+    const int64_t o0 = (int64_t)blockIdx.x * EMIT_TILE;
+    const int64_t o1 = min(total, o0 + EMIT_TILE);
+    if (threadIdx.x < 2) s_owner[threadIdx.x] = owner_of(offsets, 0, n - 1, threadIdx.x == 0 ? o0 : o1 - 1);
+    __syncthreads();
+    const int j0 = s_owner[0], span = s_owner[1] - j0 + 1;
+    const bool staged = span <= EMIT_TILE;
+    if (staged)
+        for (int t = threadIdx.x; t < span; t += EMIT_THREADS) s_off[t] = offsets[j0 + t];
+    __syncthreads();
+    for (int64_t o = o0 + threadIdx.x; o < o1; o += EMIT_THREADS) {
+        int j;
+        int64_t start;
+        if (staged) {
+            const int r = owner_of(s_off, 0, span - 1, o);
+            j = j0 + r;
+            start = s_off[r];
+        } else {
+            j = owner_of(offsets, j0, j0 + span - 1, o);
+            start = offsets[j];
+        }
+        const int g = order[j];
+        const int4 r = rect[g];
+        const int local = (int)(o - start);
+        const int tx = r.x + local % r.z, ty = r.y + local / r.z;
+        tile_keys[o] = (uint32_t)(ty * tiles_x + tx);
+        values[o] = g;
+    }
 }
 
 // ---------------------------------------------------------------------------------------------
-// radix sort passes
+// radix sort passes (32-bit keys)
 // ---------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(SORT_THREADS) radix_histogram_kernel(const uint64_t* __restrict__ keys, int64_t n, int shift,
-                                                                       uint32_t* __restrict__ counts, int nblocks) {
+__global__ void __launch_bounds__(SORT_THREADS) radix_histogram_kernel(const uint32_t* __restrict__ keys, int64_t n,
+                                                                       int shift, uint32_t* __restrict__ counts,
+                                                                       int nblocks) {
     __shared__ uint32_t hist[RADIX];
     hist[threadIdx.x] = 0;
     __syncthreads();
@@ -188,7 +266,7 @@ __global__ void __launch_bounds__(SORT_THREADS) radix_histogram_kernel(const uin
     const int lane = threadIdx.x & 31;
     for (int64_t r = begin; r < end; r += SORT_THREADS) {
         int64_t i = r + threadIdx.x;
-        uint32_t d = i < end ? (uint32_t)(keys[i] >> shift) & (RADIX - 1) : RADIX;
+        uint32_t d = i < end ? (keys[i] >> shift) & (RADIX - 1) : RADIX;
         // Warp-aggregated: one shared atomic per distinct digit of the warp.
         uint32_t peers = __match_any_sync(FULL_MASK, d);
         if (d < RADIX && lane == __ffs(peers) - 1) atomicAdd(&hist[d], __popc(peers));
@@ -197,10 +275,11 @@ __global__ void __launch_bounds__(SORT_THREADS) radix_histogram_kernel(const uin
     counts[threadIdx.x * nblocks + blockIdx.x] = hist[threadIdx.x];
 }
 
-__global__ void __launch_bounds__(SORT_THREADS) radix_scatter_kernel(const uint64_t* __restrict__ keys_in,
-                                                                     const int32_t* __restrict__ vals_in, int64_t n, int shift,
-                                                                     const uint32_t* __restrict__ offsets, int nblocks,
-                                                                     uint64_t* __restrict__ keys_out, int32_t* __restrict__ vals_out) {
+__global__ void __launch_bounds__(SORT_THREADS) radix_scatter_kernel(const uint32_t* __restrict__ keys_in,
+                                                                     const int32_t* __restrict__ vals_in, int64_t n,
+                                                                     int shift, const uint32_t* __restrict__ offsets,
+                                                                     int nblocks, uint32_t* __restrict__ keys_out,
+                                                                     int32_t* __restrict__ vals_out) {
     constexpr int WARPS = SORT_THREADS / 32;
     __shared__ uint32_t s_base[RADIX];
     __shared__ uint32_t s_warp[WARPS][RADIX];
@@ -215,9 +294,9 @@ __global__ void __launch_bounds__(SORT_THREADS) radix_scatter_kernel(const uint6
         __syncthreads();
         int64_t i = r + tid;
         bool valid = i < end;
-        uint64_t key = valid ? keys_in[i] : 0;
+        uint32_t key = valid ? keys_in[i] : 0;
         int32_t val = valid ? vals_in[i] : 0;
-        uint32_t d = valid ? (uint32_t)(key >> shift) & (RADIX - 1) : RADIX;
+        uint32_t d = valid ? (key >> shift) & (RADIX - 1) : RADIX;
         uint32_t peers = __match_any_sync(FULL_MASK, d);
         uint32_t rank = __popc(peers & ((1u << lane) - 1u));
         if (valid && lane == __ffs(peers) - 1) s_warp[warp][d] = __popc(peers);
@@ -241,24 +320,52 @@ __global__ void __launch_bounds__(SORT_THREADS) radix_scatter_kernel(const uint6
     }
 }
 
-__global__ void __launch_bounds__(256) tile_ranges_kernel(int64_t total, const uint64_t* __restrict__ keys,
+int sort_blocks(int64_t n) { return (int)((n + SORT_TILE - 1) / SORT_TILE); }
+
+// Stable LSD sort of (key, value) pairs on bits [0, 8 passes): ping-pongs between the a and b
+// buffers, so the result is in a after an even number of passes and in b after an odd one.
+int radix_sort(uint32_t* keys_a, uint32_t* keys_b, int32_t* vals_a, int32_t* vals_b, int64_t n, int passes,
+               uint32_t* counts, uint32_t* count_sums, cudaStream_t stream) {
+    const int nblocks = sort_blocks(n);
+    const int64_t table = (int64_t)RADIX * nblocks;
+    for (int p = 0; p < passes; p++) {
+        radix_histogram_kernel<<<nblocks, SORT_THREADS, 0, stream>>>(keys_a, n, 8 * p, counts, nblocks);
+        HDS_CHECK_LAUNCH("radix_histogram_kernel");
+        if (int rc = exclusive_scan<uint32_t>(counts, counts, table, count_sums, nullptr, stream)) return rc;
+        radix_scatter_kernel<<<nblocks, SORT_THREADS, 0, stream>>>(keys_a, vals_a, n, 8 * p, counts, nblocks, keys_b,
+                                                                   vals_b);
+        HDS_CHECK_LAUNCH("radix_scatter_kernel");
+        uint32_t* tk = keys_a; keys_a = keys_b; keys_b = tk;
+        int32_t* tv = vals_a; vals_a = vals_b; vals_b = tv;
+    }
+    return HDS_OK;
+}
+
+__global__ void __launch_bounds__(256) tile_ranges_kernel(int64_t total, const uint32_t* __restrict__ tile_keys,
                                                           int2* __restrict__ ranges) {
     int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (k >= total) return;
-    uint32_t tile = (uint32_t)(keys[k] >> 32);
-    if (k == 0 || (uint32_t)(keys[k - 1] >> 32) != tile) ranges[tile].x = (int)k;
-    if (k == total - 1 || (uint32_t)(keys[k + 1] >> 32) != tile) ranges[tile].y = (int)(k + 1);
+    uint32_t tile = tile_keys[k];
+    if (k == 0 || tile_keys[k - 1] != tile) ranges[tile].x = (int)k;
+    if (k == total - 1 || tile_keys[k + 1] != tile) ranges[tile].y = (int)(k + 1);
+}
+
+// The reference's 64-bit keys of the sorted pairs, tile << 32 | depth bits, for callers that ask.
+__global__ void __launch_bounds__(256) full_keys_kernel(int64_t total, const uint32_t* __restrict__ tile_keys,
+                                                        const int32_t* __restrict__ values,
+                                                        const int4* __restrict__ rect, uint64_t* __restrict__ keys) {
+    int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (k < total) keys[k] = ((uint64_t)tile_keys[k] << 32) | (uint32_t)rect[values[k]].w;
 }
 
 // Scratch layouts --------------------------------------------------------------------------------
 struct PrepareLayout {
-    size_t rect, touched, offsets, block_sums, total, bytes;
+    size_t rect, touched, block_sums, total, bytes;
     explicit PrepareLayout(int n) {
         size_t nn = (size_t)(n > 0 ? n : 1);
         rect = 0;
         touched = rect + align256(nn * sizeof(int4));
-        offsets = touched + align256(nn * sizeof(int64_t));
-        block_sums = offsets + align256(nn * sizeof(int64_t));
+        block_sums = touched + align256(nn * sizeof(int64_t));
         total = block_sums + align256((size_t)scan_blocks((int64_t)nn) * sizeof(int64_t));
         bytes = total + 256;
     }
@@ -271,18 +378,28 @@ int tile_bits_for(int tiles) {
 }
 
 struct SortLayout {
-    size_t keys_a, keys_b, vals_other, counts, count_sums, bytes;
-    int nblocks, passes;
-    SortLayout(int64_t dups, int tiles) {
-        size_t d = (size_t)(dups > 0 ? dups : 1);
-        nblocks = (int)((d + SORT_TILE - 1) / SORT_TILE);
-        passes = (32 + tile_bits_for(tiles) + 7) / 8;
-        keys_a = 0;
-        keys_b = keys_a + align256(d * sizeof(uint64_t));
-        vals_other = keys_b + align256(d * sizeof(uint64_t));
-        counts = vals_other + align256(d * sizeof(int32_t));
-        count_sums = counts + align256((size_t)RADIX * nblocks * sizeof(uint32_t));
-        bytes = count_sums + align256((size_t)scan_blocks((int64_t)RADIX * nblocks) * sizeof(uint32_t)) + 256;
+    // Gaussian depth sort: keys and values in two buffers each, then the depth-ordered pair counts and
+    // their offsets.  Pair sort: tile keys in two buffers, values in values_sorted and one more.
+    size_t g_keys_a, g_keys_b, g_vals_a, g_vals_b, g_counts, g_offsets, g_block_sums;
+    size_t p_keys_a, p_keys_b, p_vals_other, counts, count_sums, bytes;
+    int pair_passes;
+    SortLayout(int n, int64_t dups, int tiles) {
+        const size_t nn = (size_t)(n > 0 ? n : 1), d = (size_t)(dups > 0 ? dups : 1);
+        pair_passes = (tile_bits_for(tiles) + 7) / 8;
+        g_keys_a = 0;
+        g_keys_b = g_keys_a + align256(nn * sizeof(uint32_t));
+        g_vals_a = g_keys_b + align256(nn * sizeof(uint32_t));
+        g_vals_b = g_vals_a + align256(nn * sizeof(int32_t));
+        g_counts = g_vals_b + align256(nn * sizeof(int32_t));
+        g_offsets = g_counts + align256(nn * sizeof(int64_t));
+        g_block_sums = g_offsets + align256(nn * sizeof(int64_t));
+        p_keys_a = g_block_sums + align256((size_t)scan_blocks((int64_t)nn) * sizeof(int64_t));
+        p_keys_b = p_keys_a + align256(d * sizeof(uint32_t));
+        p_vals_other = p_keys_b + align256(d * sizeof(uint32_t));
+        counts = p_vals_other + align256(d * sizeof(int32_t));
+        const size_t table = (size_t)RADIX * (size_t)max(sort_blocks((int64_t)nn), sort_blocks((int64_t)d));
+        count_sums = counts + align256(table * sizeof(uint32_t));
+        bytes = count_sums + align256((size_t)scan_blocks((int64_t)table) * sizeof(uint32_t)) + 256;
     }
 };
 
@@ -311,7 +428,6 @@ extern "C" int hds_rasterize_prepare(int n, const float* means2D, const float* d
     char* s = static_cast<char*>(scratch);
     auto* rect = reinterpret_cast<int4*>(s + L.rect);
     auto* touched = reinterpret_cast<int64_t*>(s + L.touched);
-    auto* offsets = reinterpret_cast<int64_t*>(s + L.offsets);
     auto* block_sums = reinterpret_cast<int64_t*>(s + L.block_sums);
     auto* total = reinterpret_cast<int64_t*>(s + L.total);
     int tx = tiles_for(width), ty = tiles_for(height);
@@ -319,7 +435,7 @@ extern "C" int hds_rasterize_prepare(int n, const float* means2D, const float* d
                                                         colors, opacities, tx, ty, reinterpret_cast<float4*>(conic4),
                                                         reinterpret_cast<float4*>(color_opacity), rect, touched);
     HDS_CHECK_LAUNCH("prepare_kernel");
-    if (int rc = exclusive_scan<int64_t>(touched, offsets, n, block_sums, total, stream)) return rc;
+    if (int rc = reduce_total<int64_t>(touched, n, block_sums, total, stream)) return rc;
     int64_t host_total = 0;
     HDS_CHECK_CUDA(cudaMemcpyAsync(&host_total, total, sizeof(int64_t), cudaMemcpyDeviceToHost, stream));
     HDS_CHECK_CUDA(cudaStreamSynchronize(stream));
@@ -330,8 +446,7 @@ extern "C" int hds_rasterize_prepare(int n, const float* means2D, const float* d
 }
 
 extern "C" size_t hds_rasterize_sort_scratch_bytes(int n, int64_t num_duplicates, int width, int height) {
-    (void)n;
-    return SortLayout(num_duplicates, tiles_for(width) * tiles_for(height)).bytes;
+    return SortLayout(n, num_duplicates, tiles_for(width) * tiles_for(height)).bytes;
 }
 
 extern "C" int hds_rasterize_sort(int n, int64_t num_duplicates, int width, int height, const void* prepare_scratch,
@@ -341,45 +456,56 @@ extern "C" int hds_rasterize_sort(int n, int64_t num_duplicates, int width, int 
     int tiles = tiles_for(width) * tiles_for(height);
     HDS_REQUIRE(n > 0 && num_duplicates > 0 && num_duplicates <= INT_MAX && width > 0 && height > 0, HDS_ERR_INVALID,
                 "rasterize: bad sort arguments (n=%d, pairs=%lld)", n, (long long)num_duplicates);
-    SortLayout L(num_duplicates, tiles);
+    SortLayout L(n, num_duplicates, tiles);
     HDS_REQUIRE(scratch && scratch_bytes >= L.bytes && ((uintptr_t)scratch & 255) == 0, HDS_ERR_SCRATCH,
                 "rasterize: sort scratch needs %zu bytes, 256-byte aligned", L.bytes);
     PrepareLayout P(n);
     const char* ps = static_cast<const char*>(prepare_scratch);
     const auto* rect = reinterpret_cast<const int4*>(ps + P.rect);
-    const auto* offsets = reinterpret_cast<const int64_t*>(ps + P.offsets);
+    const auto* touched = reinterpret_cast<const int64_t*>(ps + P.touched);
     char* s = static_cast<char*>(scratch);
-    auto* keys_a = reinterpret_cast<uint64_t*>(s + L.keys_a);
-    auto* keys_b = reinterpret_cast<uint64_t*>(s + L.keys_b);
     auto* counts = reinterpret_cast<uint32_t*>(s + L.counts);
     auto* count_sums = reinterpret_cast<uint32_t*>(s + L.count_sums);
-    // The last pass must land in values_sorted: with an odd number of passes the emission buffer is
-    // the scratch one, with an even number it is values_sorted itself.
-    int32_t* vals_other = reinterpret_cast<int32_t*>(s + L.vals_other);
-    int32_t* vals_a = (L.passes % 2 == 0) ? values_sorted : vals_other;
-    int32_t* vals_b = (L.passes % 2 == 0) ? vals_other : values_sorted;
-    int64_t total = num_duplicates;
-    unsigned blocks = (unsigned)((total + 255) / 256);
-    emit_kernel<<<blocks, 256, 0, stream>>>(total, n, offsets, rect, tiles_for(width), keys_a, vals_a);
+
+    // 1. Gaussians by depth (4 passes: the result is back in the a buffers).
+    auto* g_keys_a = reinterpret_cast<uint32_t*>(s + L.g_keys_a);
+    auto* g_vals_a = reinterpret_cast<int32_t*>(s + L.g_vals_a);
+    gaussian_keys_kernel<<<(n + 255) / 256, 256, 0, stream>>>(n, rect, touched, g_keys_a, g_vals_a);
+    HDS_CHECK_LAUNCH("gaussian_keys_kernel");
+    if (int rc = radix_sort(g_keys_a, reinterpret_cast<uint32_t*>(s + L.g_keys_b), g_vals_a,
+                            reinterpret_cast<int32_t*>(s + L.g_vals_b), n, 4, counts, count_sums, stream))
+        return rc;
+    const int32_t* order = g_vals_a;
+    auto* g_counts = reinterpret_cast<int64_t*>(s + L.g_counts);
+    auto* g_offsets = reinterpret_cast<int64_t*>(s + L.g_offsets);
+    sorted_counts_kernel<<<(n + 255) / 256, 256, 0, stream>>>(n, order, touched, g_counts);
+    HDS_CHECK_LAUNCH("sorted_counts_kernel");
+    if (int rc = exclusive_scan<int64_t>(g_counts, g_offsets, n, reinterpret_cast<int64_t*>(s + L.g_block_sums),
+                                         nullptr, stream))
+        return rc;
+
+    // 2. Pairs in depth order, then stably by tile.  The last pass must land in values_sorted: with an
+    // even number of passes the emission buffer is values_sorted itself, with an odd one the scratch one.
+    const int64_t total = num_duplicates;
+    int32_t* vals_other = reinterpret_cast<int32_t*>(s + L.p_vals_other);
+    int32_t* vals_a = (L.pair_passes % 2 == 0) ? values_sorted : vals_other;
+    int32_t* vals_b = (L.pair_passes % 2 == 0) ? vals_other : values_sorted;
+    auto* keys_a = reinterpret_cast<uint32_t*>(s + L.p_keys_a);
+    auto* keys_b = reinterpret_cast<uint32_t*>(s + L.p_keys_b);
+    emit_kernel<<<(unsigned)((total + EMIT_TILE - 1) / EMIT_TILE), EMIT_THREADS, 0, stream>>>(
+        total, n, g_offsets, order, rect, tiles_for(width), keys_a, vals_a);
     HDS_CHECK_LAUNCH("emit_kernel");
-    uint64_t* kin = keys_a;
-    uint64_t* kout = keys_b;
-    int32_t* vin = vals_a;
-    int32_t* vout = vals_b;
-    int64_t table = (int64_t)RADIX * L.nblocks;
-    for (int p = 0; p < L.passes; p++) {
-        radix_histogram_kernel<<<L.nblocks, SORT_THREADS, 0, stream>>>(kin, total, 8 * p, counts, L.nblocks);
-        HDS_CHECK_LAUNCH("radix_histogram_kernel");
-        if (int rc = exclusive_scan<uint32_t>(counts, counts, table, count_sums, nullptr, stream)) return rc;
-        radix_scatter_kernel<<<L.nblocks, SORT_THREADS, 0, stream>>>(kin, vin, total, 8 * p, counts, L.nblocks, kout, vout);
-        HDS_CHECK_LAUNCH("radix_scatter_kernel");
-        uint64_t* tk = kin; kin = kout; kout = tk;
-        int32_t* tv = vin; vin = vout; vout = tv;
-    }
+    if (int rc = radix_sort(keys_a, keys_b, vals_a, vals_b, total, L.pair_passes, counts, count_sums, stream))
+        return rc;
+    const uint32_t* tile_keys = (L.pair_passes % 2 == 0) ? keys_a : keys_b;
+
+    const unsigned blocks = (unsigned)((total + 255) / 256);
     HDS_CHECK_CUDA(cudaMemsetAsync(tile_ranges, 0, sizeof(int32_t) * 2 * (size_t)tiles, stream));
-    tile_ranges_kernel<<<blocks, 256, 0, stream>>>(total, kin, reinterpret_cast<int2*>(tile_ranges));
+    tile_ranges_kernel<<<blocks, 256, 0, stream>>>(total, tile_keys, reinterpret_cast<int2*>(tile_ranges));
     HDS_CHECK_LAUNCH("tile_ranges_kernel");
-    if (keys_sorted)
-        HDS_CHECK_CUDA(cudaMemcpyAsync(keys_sorted, kin, sizeof(uint64_t) * (size_t)total, cudaMemcpyDeviceToDevice, stream));
+    if (keys_sorted) {
+        full_keys_kernel<<<blocks, 256, 0, stream>>>(total, tile_keys, values_sorted, rect, keys_sorted);
+        HDS_CHECK_LAUNCH("full_keys_kernel");
+    }
     return HDS_OK;
 }

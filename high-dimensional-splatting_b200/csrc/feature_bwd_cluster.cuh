@@ -98,7 +98,8 @@ __device__ __forceinline__ float4 ld_shared_f4(uint32_t addr) {
 
 template <int CK, bool RGB>
 __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) feature_backward_cluster_kernel(
-    int C, int width, int height, int tiles_x, const int2* __restrict__ ranges, const int32_t* __restrict__ values,
+    int C, int width, int height, int tiles_x, int helper_every, const int2* __restrict__ ranges,
+    const int32_t* __restrict__ values,
     const float2* __restrict__ means2D, const float4* __restrict__ conic4, const float4* __restrict__ color_opacity,
     const float* __restrict__ features, const float* __restrict__ final_T_in, const int32_t* __restrict__ n_contrib,
     const float* __restrict__ grad_out, float* __restrict__ grad_means2D, float* __restrict__ grad_conics,
@@ -116,7 +117,10 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int rank = (int)tc::cluster_rank();
-    const int half_id = blockIdx.x / CLUSTER;
+    // With a helper kernel taking every helper_every-th half tile (M > 1), cluster c takes the c-th of
+    // the others: half tiles j M .. j M + M - 2 for j = c / (M - 1).
+    const int cidx = blockIdx.x / CLUSTER;
+    const int half_id = helper_every > 1 ? (cidx / (helper_every - 1)) * helper_every + cidx % (helper_every - 1) : cidx;
     const int tile = half_id >> 1;
     const int c0 = rank * CK;
     const int x0 = (tile % tiles_x) * TILE;
@@ -678,14 +682,16 @@ int launch_backward_cluster(int D, int width, int height, const int32_t* tile_ra
                             const float* features, const float* final_T, const int32_t* n_contrib,
                             const float* grad_output, float* grad_features, float* grad_means2D, float* grad_conics,
                             float* grad_opacities, const float* grad_image, const float* background,
-                            float* grad_colors, cudaStream_t stream) {
+                            float* grad_colors, cudaStream_t stream, int helper_every = 0) {
     using K = Cfg<CK>;
     auto kernel = grad_image != nullptr ? feature_backward_cluster_kernel<CK, true>
                                         : feature_backward_cluster_kernel<CK, false>;
     HDS_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, K::SMEM));
     const int tx = tiles_for(width), ty = tiles_for(height);
-    kernel<<<2 * tx * ty * CLUSTER, THREADS, K::SMEM, stream>>>(
-        D, width, height, tx, reinterpret_cast<const int2*>(tile_ranges), values,
+    const int halves = 2 * tx * ty;
+    const int clusters = halves - (helper_every > 1 ? halves / helper_every : 0);
+    kernel<<<clusters * CLUSTER, THREADS, K::SMEM, stream>>>(
+        D, width, height, tx, helper_every, reinterpret_cast<const int2*>(tile_ranges), values,
         reinterpret_cast<const float2*>(means2D), reinterpret_cast<const float4*>(conic4),
         reinterpret_cast<const float4*>(color_opacity), features, final_T, n_contrib, grad_output, grad_means2D,
         grad_conics, grad_features, grad_opacities, grad_image, background, grad_colors);

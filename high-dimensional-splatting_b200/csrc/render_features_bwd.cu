@@ -30,6 +30,7 @@
 // returns.
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 
 #include "feature_bwd_common.cuh"
 
@@ -92,7 +93,7 @@ struct BwdCfg {
 
 template <int CK, bool RGB>
 __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
-    int C, int width, int height, int tiles_x, int slices, const int2* __restrict__ ranges,
+    int C, int width, int height, int tiles_x, int slices, int helper_every, const int2* __restrict__ ranges,
     const int32_t* __restrict__ values, const float2* __restrict__ means2D, const float4* __restrict__ conic4,
     const float4* __restrict__ color_opacity, const float* __restrict__ features, const float* __restrict__ final_T_in,
     const int32_t* __restrict__ n_contrib, const float* __restrict__ grad_out, float* __restrict__ grad_means2D,
@@ -112,7 +113,10 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
     // With grad_image, the first slice's blocks also carry the RGB backward: its dot is colour . dL/dpixel
     // and its recurrence the same as the features' (backward.cu:7-164), plus the background term.
     const bool rgb = RGB && slice == 0;
-    const int half_id = blockIdx.x / slices;
+    // As the helper of the cluster kernel (helper_every = M > 0), block group j takes half tile
+    // j M + M - 1, the half tiles the clusters skip.
+    const int half_id = helper_every > 0 ? (int)(blockIdx.x / slices) * helper_every + helper_every - 1
+                                         : (int)(blockIdx.x / slices);
     const int tile = half_id >> 1;
     const int c0 = slice * CK;
     const int x0 = (tile % tiles_x) * TILE;
@@ -569,13 +573,16 @@ int launch_backward(int D, int width, int height, const int32_t* tile_ranges, co
                     const float* means2D, const float* conic4, const float* color_opacity, const float* features,
                     const float* final_T, const int32_t* n_contrib, const float* grad_output, float* grad_features,
                     float* grad_means2D, float* grad_conics, float* grad_opacities, const float* grad_image,
-                    const float* background, float* grad_colors, cudaStream_t stream) {
+                    const float* background, float* grad_colors, cudaStream_t stream, int helper_every = 0) {
     using Cfg = BwdCfg<CK>;
     auto kernel = grad_image != nullptr ? feature_backward_kernel<CK, true> : feature_backward_kernel<CK, false>;
     HDS_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
     const int tx = tiles_for(width), ty = tiles_for(height), slices = D / CK;
-    kernel<<<2 * tx * ty * slices, THREADS, Cfg::SMEM, stream>>>(
-        D, width, height, tx, slices, reinterpret_cast<const int2*>(tile_ranges), values,
+    const int halves = 2 * tx * ty;
+    const int groups = helper_every > 0 ? halves / helper_every : halves;
+    if (groups == 0) return HDS_OK;
+    kernel<<<groups * slices, THREADS, Cfg::SMEM, stream>>>(
+        D, width, height, tx, slices, helper_every, reinterpret_cast<const int2*>(tile_ranges), values,
         reinterpret_cast<const float2*>(means2D), reinterpret_cast<const float4*>(conic4),
         reinterpret_cast<const float4*>(color_opacity), features, final_T, n_contrib, grad_output, grad_means2D,
         grad_conics, grad_features, grad_opacities, grad_image, background, grad_colors);
@@ -595,6 +602,51 @@ bool cluster_backward_enabled(int D) {
     if (v != nullptr && strcmp(v, "0") == 0) return false;
     if (v != nullptr && strcmp(v, "1") == 0) return D >= 256;
     return D == 512;
+}
+
+// The four-block clusters of the 512-channel backward fit 33 at a time on a B200 (132 SMs): its
+// GPCs do not all hold a multiple of four SMs.  A helper launch of the one-block kernel on a second
+// stream takes every M-th half tile; its single-SM blocks run on the SMs no cluster can use, and
+// after the clusters drain, on all of them.  HDS_FEATURE_BWD_HELPER: unset = every 14th half tile
+// (on the 1.18M-gaussian bench view the backward takes 7.42 ms without a helper and 7.26, 7.19 and
+// 7.16 ms with M = 6, 10 and 14), "0" = no helper, an integer M >= 2 = every M-th.  Read per call.
+int helper_every() {
+    const char* v = getenv("HDS_FEATURE_BWD_HELPER");
+    if (v == nullptr || *v == '\0') return 14;
+    const int m = atoi(v);
+    return m >= 2 ? m : 0;
+}
+
+// The helper's stream and its fork / join events, one set per device, created on first use and kept
+// for the life of the process.  The stream does not synchronise with the legacy default stream, so
+// only the events order it.  The mutex keeps each call's fork, launches and join together.
+constexpr int kMaxDevices = 64;
+struct HelperStream {
+    cudaStream_t stream = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+};
+std::mutex g_helper_mutex;
+HelperStream g_helper[kMaxDevices];
+
+template <class ClusterLaunch, class HelperLaunch>
+int launch_with_helper(cudaStream_t stream, ClusterLaunch&& clusters, HelperLaunch&& helper) {
+    int dev = -1;
+    HDS_CHECK_CUDA(cudaGetDevice(&dev));
+    HDS_REQUIRE(dev >= 0 && dev < kMaxDevices, HDS_ERR_INVALID, "feature backward: device %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_helper_mutex);
+    HelperStream& h = g_helper[dev];
+    if (h.stream == nullptr) {
+        HDS_CHECK_CUDA(cudaStreamCreateWithFlags(&h.stream, cudaStreamNonBlocking));
+        HDS_CHECK_CUDA(cudaEventCreateWithFlags(&h.fork, cudaEventDisableTiming));
+        HDS_CHECK_CUDA(cudaEventCreateWithFlags(&h.join, cudaEventDisableTiming));
+    }
+    HDS_CHECK_CUDA(cudaEventRecord(h.fork, stream));
+    if (int rc = clusters(stream)) return rc;  // launched first: its clusters take the SMs they can
+    HDS_CHECK_CUDA(cudaStreamWaitEvent(h.stream, h.fork, 0));
+    if (int rc = helper(h.stream)) return rc;
+    HDS_CHECK_CUDA(cudaEventRecord(h.join, h.stream));
+    HDS_CHECK_CUDA(cudaStreamWaitEvent(stream, h.join, 0));
+    return HDS_OK;
 }
 
 // grad_image (with background and grad_colors) adds the RGB backward to the same walk; NULL leaves
@@ -630,6 +682,17 @@ int features_backward(int n, int channels, int slice_width, int width, int heigh
     // any slicing.  One block per half tile and slice of min(D, 128) channels (one walk per slice), or
     // four-block clusters (slices of D / 4, one walk per pixel).
     if (cluster_backward_enabled(D)) {
+        const int m = helper_every();
+        if (D == 512 && m > 0 && (2 * tiles_for(width) * tiles_for(height)) / m > 0) {
+            return launch_with_helper(
+                stream,
+                [&](cudaStream_t st) {
+                    return clus::launch_backward_cluster<128>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, st, m);
+                },
+                [&](cudaStream_t st) {
+                    return launch_backward<128>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, st, m);
+                });
+        }
         if (D == 256)
             return clus::launch_backward_cluster<64>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);
         return clus::launch_backward_cluster<128>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);

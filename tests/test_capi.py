@@ -41,7 +41,9 @@ def test_abi_version_and_scratch_queries():
     small = native.lib.hds_rasterize_prepare_scratch_bytes(10)
     big = native.lib.hds_rasterize_prepare_scratch_bytes(1_000_000)
     assert 0 < small < big and big % 256 == 0
-    assert native.lib.hds_rasterize_sort_scratch_bytes(10, 2_000_000, 979, 546) > 2_000_000 * 20
+    # 12 bytes per pair (two tile-key buffers, one value buffer) and 32 per gaussian (depth sort).
+    assert native.lib.hds_rasterize_sort_scratch_bytes(10, 2_000_000, 979, 546) > 2_000_000 * 12
+    assert native.lib.hds_rasterize_sort_scratch_bytes(1_000_000, 2_000_000, 979, 546) > 1_000_000 * 32 + 2_000_000 * 12
 
 
 def test_bad_arguments_are_rejected_on_the_host():

@@ -177,6 +177,18 @@ def test_fused_backward_cluster_kernel(ext, golden, monkeypatch, name, channels,
     test_fused_backward(ext, golden, name, channels, with_rgb)
 
 
+@pytest.mark.parametrize("helper", ["0", "2", "3", "7"])
+@pytest.mark.parametrize("name", ["raster_ref_scene", "dense_tile", "size3", "config1_20k"])
+@pytest.mark.parametrize("with_rgb", [True, False])
+def test_fused_backward_cluster_helper_split(ext, golden, monkeypatch, name, helper, with_rgb):
+    """At 512 channels the one-block kernel, on a second stream, takes every M-th half tile
+    (HDS_FEATURE_BWD_HELPER=M) while the clusters take the rest; "0" runs the clusters alone.  Every
+    split gives the oracle's gradients, the RGB terms included (the helper's first slice carries
+    them)."""
+    monkeypatch.setenv("HDS_FEATURE_BWD_HELPER", helper)
+    test_fused_backward(ext, golden, name, 512, with_rgb)
+
+
 @pytest.mark.parametrize("channels", [32, 128, 256, 512])
 @pytest.mark.parametrize("name", ["raster_ref_scene", "raster_config0", "dense_tile", "size3", "config1_20k"])
 @pytest.mark.parametrize("with_rgb", [True, False])

@@ -71,7 +71,7 @@ def test_no_alloc_binning_refuses_requests_beyond_its_limits():
     rc, *_ = bin_noalloc(native, inputs, cam.width, cam.height, capacity=10)
     assert rc == 5  # HDS_ERR_TOO_LARGE
     assert b"exceed values_sorted capacity" in native.lib.hds_last_error()
-    huge = 5_000_000  # needs ~160 MB of prepare scratch, more than the fixed array
+    huge = 5_000_000  # needs ~120 MB of prepare scratch, more than the fixed array
     z = torch.zeros(huge, 4, device="cuda")
     rc = native.lib.hds_rasterize_bin_noalloc(huge, *(native.ptr(z),) * 6, 64, 64, native.ptr(z), native.ptr(z),
                                               native.ptr(z), 1, native.ptr(z), ctypes.byref(ctypes.c_int64()),
