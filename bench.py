@@ -4,11 +4,12 @@
 Workload (BASELINE config 2 scene, config 3 views): 1.18M gaussians with the config-1 distribution,
 C-channel features (default 512), SH degree 3, 979x546 views on the 64-view orbit (radius 8,
 elevation 10-30 deg).  One step = every rank renders --views views (default 8) through the full
-hot path -- projection, SH colour, binning, the fused RGB + feature blend, 0.8 L1 + 0.2 (1 - SSIM)
-on RGB, a fixed random gradient on the feature image (the reference harness's scope,
-bench/harness.py:42-50) -- and backpropagates into every gaussian parameter, accumulating over its
-views; with N > 1 ranks the per-gaussian gradients (59 + C floats each) are then all-reduced over
-NCCL.  Scaling is weak: every rank renders its own views.  value = views / s over all ranks.
+hot path -- the model's parameter activations and projection, SH colour, binning, the fused RGB +
+feature blend, 0.8 L1 + 0.2 (1 - SSIM) on RGB, a fixed random gradient on the feature image (the
+reference harness's scope, bench/harness.py:42-50, plus the activations of utils/gaussian.py:73-98
+that its training loop runs) -- and backpropagates into every raw gaussian parameter, accumulating
+over its views; with N > 1 ranks the per-gaussian gradients (59 + C floats each) are then
+all-reduced over NCCL.  Scaling is weak: every rank renders its own views.  value = views / s over all ranks.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--channels C] [--views V]
     python bench.py --impl reference ...   # the CPU oracle on a bounded sample of the same workload
@@ -162,8 +163,13 @@ def make_workload(args, device, rank, world):
     gt_host = [torch.randint(0, 256, (h, w, 3), dtype=torch.uint8, generator=gen).pin_memory() for _ in views]
     pose_host = [cams[v].world_to_camera.clone().pin_memory() for v in views]
     feat_grad = torch.rand(h, w, args.channels, generator=gen).to(device) / (h * w)
-    leaves = {k: getattr(scene, k).to(device).contiguous().requires_grad_(True)
-              for k in ("means", "scales", "quats", "opacities", "sh_dc", "sh_rest", "features")}
+    # The model's raw parameters (the reference's Gaussian.params): log-scales, quaternions, opacity
+    # logits; their activations run inside the projection kernels.
+    op = scene.opacities.clamp(1e-6, 1 - 1e-6)
+    raw = {"means": scene.means, "log_scales": torch.log(scene.scales), "quats": scene.quats,
+           "opacity_logits": torch.log(op / (1 - op)), "sh_dc": scene.sh_dc, "sh_rest": scene.sh_rest,
+           "features": scene.features}
+    leaves = {k: v.to(device).contiguous().requires_grad_(True) for k, v in raw.items()}
     bucket = parallel.GradBucket(list(leaves.values()))
     return {"bucket": bucket, "scene": scene, "cams": cams, "views": views, "gt_host": gt_host, "pose_host": pose_host,
             "gt_dev": [g.to(device) for g in gt_host], "pose_dev": [p.to(device) for p in pose_host],
@@ -175,20 +181,22 @@ def render_view(wl, i, pose, gt_u8):
     import torch
 
     from hds_b200.loss import l1_loss, ssim
-    from hds_b200.projection import project_gaussians
+    from hds_b200.projection import project_gaussians_raw
     from hds_b200.rasterizer import accumulate_leaf_grads, rasterize
     from hds_b200.sh import view_colors
 
     cam = wl["cams"][wl["views"][i]]
     L = wl["leaves"]
-    means2D, depths, radii, conics = project_gaussians(L["means"], L["scales"], L["quats"], L["opacities"], pose,
-                                                       cam.fx, cam.fy, cam.cx, cam.cy, cam.width, cam.height)
     center = -(pose[:3, :3].T @ pose[:3, 3])
-    # The views of a step accumulate into the gradient bucket: the SH and feature backward passes add
-    # straight into it.  view_colors forms normalize(means - center) inside the SH kernels.
+    # The views of a step accumulate into the gradient bucket: the projection, SH and feature backward
+    # passes add straight into it.  The projection applies the parameter activations and view_colors
+    # forms normalize(means - center) inside the SH kernels.
     with accumulate_leaf_grads():
+        means2D, depths, radii, conics, opacities = project_gaussians_raw(
+            L["means"], L["log_scales"], L["quats"], L["opacity_logits"], pose, cam.fx, cam.fy, cam.cx, cam.cy,
+            cam.width, cam.height)
         colors = view_colors(L["sh_dc"], L["sh_rest"], L["means"], center, 3, radii)
-        image, feat = rasterize(means2D, depths, radii, conics, colors, L["opacities"], cam.width, cam.height,
+        image, feat = rasterize(means2D, depths, radii, conics, colors, opacities, cam.width, cam.height,
                                 wl["bg"], L["features"])
     gt = gt_u8.float() / 255.0
     loss = 0.8 * l1_loss(image, gt) + 0.2 * (1.0 - ssim(image, gt))
@@ -226,16 +234,16 @@ def tile_stats(wl, device):
     import torch
 
     from hds_b200 import gaussian_rasterizer as ext
-    from hds_b200.projection import project_gaussians
+    from hds_b200.projection import project_gaussians_raw
 
     L = wl["leaves"]
     cam = wl["cams"][wl["views"][0]]
     with torch.no_grad():
-        means2D, depths, radii, conics = project_gaussians(L["means"], L["scales"], L["quats"], L["opacities"],
-                                                           wl["pose_dev"][0], cam.fx, cam.fy, cam.cx, cam.cy,
-                                                           cam.width, cam.height)
+        means2D, depths, radii, conics, opacities = project_gaussians_raw(
+            L["means"], L["log_scales"], L["quats"], L["opacity_logits"], wl["pose_dev"][0], cam.fx, cam.fy, cam.cx,
+            cam.cy, cam.width, cam.height)
         colors = torch.zeros_like(L["means"])
-        _, _, n_contrib, values, ranges, _, _ = ext.rasterize(means2D, depths, radii, conics, colors, L["opacities"],
+        _, _, n_contrib, values, ranges, _, _ = ext.rasterize(means2D, depths, radii, conics, colors, opacities,
                                                              wl["bg"], cam.width, cam.height)
         h, w = cam.height, cam.width
         tx, ty = (w + 15) // 16, (h + 15) // 16

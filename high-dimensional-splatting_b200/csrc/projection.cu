@@ -86,11 +86,32 @@ __device__ __forceinline__ void load_row3(const float* p, int i, float out[3]) {
     out[0] = p[3 * i]; out[1] = p[3 * i + 1]; out[2] = p[3 * i + 2];
 }
 
+// The model's parameter activations (the reference's utils/gaussian.py:73-98), applied in the kernel
+// when the projection takes raw parameters: scale = exp(log_scale), quat = q / max(|q|, 1e-12) with
+// |q| summed w, x, y, z in order (torch.nn.functional.normalize), opacity = 1 / (1 + exp(-logit)).
+// expf_det rounds like the CPU oracle's exp.
+struct Activated {
+    float scale[3], q[4], qlen, opacity;
+};
+
+__device__ __forceinline__ void activate(const float log_scale[3], const float raw_q[4], float logit, Activated& a) {
+#pragma unroll
+    for (int k = 0; k < 3; k++) a.scale[k] = expf_det(log_scale[k]);
+    const float w = raw_q[0], x = raw_q[1], y = raw_q[2], z = raw_q[3];
+    a.qlen = fmaxf(sqrtf(w * w + x * x + y * y + z * z), 1e-12f);
+#pragma unroll
+    for (int c = 0; c < 4; c++) a.q[c] = raw_q[c] / a.qlen;
+    a.opacity = 1.0f / (1.0f + expf_det(-logit));
+}
+
+// RAW: scales, quats and opacities hold the raw parameters (log-scales, unnormalised quaternions,
+// opacity logits), activated here; the activated opacity is written to opacities_out.
+template <bool RAW>
 __global__ void __launch_bounds__(256) project_forward_kernel(int n, Camera cam, const float* __restrict__ w2c, const float* __restrict__ means,
                                                               const float* __restrict__ scales, const float* __restrict__ quats,
                                                               const float* __restrict__ opacities, float* __restrict__ means2D,
                                                               float* __restrict__ depths, float* __restrict__ radii,
-                                                              float* __restrict__ conics) {
+                                                              float* __restrict__ conics, float* __restrict__ opacities_out) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const Pose pose(w2c);
@@ -99,6 +120,17 @@ __global__ void __launch_bounds__(256) project_forward_kernel(int n, Camera cam,
     load_row3(scales, i, scale);
     float4 q = reinterpret_cast<const float4*>(quats)[i];
     float qa[4] = {q.x, q.y, q.z, q.w};
+    float opacity = opacities[i];
+    if (RAW) {
+        Activated act;
+        activate(scale, qa, opacity, act);
+#pragma unroll
+        for (int k = 0; k < 3; k++) scale[k] = act.scale[k];
+#pragma unroll
+        for (int c = 0; c < 4; c++) qa[c] = act.q[c];
+        opacity = act.opacity;
+        opacities_out[i] = opacity;
+    }
     Projected g;
     project_one(cam, pose, mean, scale, qa, g);
     float u = cam.fx * g.p[0] / g.z + cam.cx;
@@ -114,15 +146,22 @@ __global__ void __launch_bounds__(256) project_forward_kernel(int n, Camera cam,
     float radius = 3.0f * sqrtf(0.5f * (trace + sqrtf(fmaxf(trace * trace - 4.0f * g.det, 0.0f))));
     int x0, y0, x1, y1;
     bool visible = !g.behind && g.det > 0.0f &&
-                   tile_rect(u, v, ca, cb, cc, opacities[i], tiles_for(cam.width), tiles_for(cam.height), x0, y0, x1, y1);
+                   tile_rect(u, v, ca, cb, cc, opacity, tiles_for(cam.width), tiles_for(cam.height), x0, y0, x1, y1);
     radii[i] = visible ? radius : 0.0f;
 }
 
+// RAW: as in the forward, the inputs are raw parameters and the gradients go to them (through the
+// activations); grad_opacities (may be null: zero) is dL/d(activated opacity), and grad_logits
+// receives dL/dlogit.  ACCUMULATE adds every gradient to what its buffer holds.
+template <bool RAW, bool ACCUMULATE>
 __global__ void __launch_bounds__(256) project_backward_kernel(int n, Camera cam, const float* __restrict__ w2c, const float* __restrict__ grad_means2D,
                                                                const float* __restrict__ grad_conics,
                                                                const float* __restrict__ means, const float* __restrict__ scales,
                                                                const float* __restrict__ quats, float* __restrict__ grad_means,
-                                                               float* __restrict__ grad_scales, float* __restrict__ grad_quats) {
+                                                               float* __restrict__ grad_scales, float* __restrict__ grad_quats,
+                                                               const float* __restrict__ logits,
+                                                               const float* __restrict__ grad_opacities,
+                                                               float* __restrict__ grad_logits) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const Pose pose(w2c);
@@ -131,6 +170,14 @@ __global__ void __launch_bounds__(256) project_backward_kernel(int n, Camera cam
     load_row3(scales, i, scale);
     float4 q4 = reinterpret_cast<const float4*>(quats)[i];
     float q[4] = {q4.x, q4.y, q4.z, q4.w};
+    Activated act;
+    if (RAW) {
+        activate(scale, q, logits[i], act);
+#pragma unroll
+        for (int k = 0; k < 3; k++) scale[k] = act.scale[k];
+#pragma unroll
+        for (int c = 0; c < 4; c++) q[c] = act.q[c];
+    }
     Projected g;
     project_one(cam, pose, mean, scale, q, g);
 
@@ -173,6 +220,33 @@ __global__ void __launch_bounds__(256) project_backward_kernel(int n, Camera cam
                    - drot[2][0] * w + drot[2][1] * z - 2.0f * drot[2][2] * y);
     gq.w = 2.0f * (-2.0f * drot[0][0] * z - drot[0][1] * w + drot[0][2] * x + drot[1][0] * w - 2.0f * drot[1][1] * z
                    + drot[1][2] * y + drot[2][0] * x + drot[2][1] * y);
+    if (RAW) {
+        // Through q / |q|: (g - q (q . g)) / |q| above the clamp, g / |q| at it; through exp: times
+        // the scale; through the sigmoid: times s (1 - s).
+        const float qv[4] = {q[0], q[1], q[2], q[3]};
+        const float gv[4] = {gq.x, gq.y, gq.z, gq.w};
+        float out[4];
+        if (act.qlen > 1e-12f) {
+            const float dot = qv[0] * gv[0] + qv[1] * gv[1] + qv[2] * gv[2] + qv[3] * gv[3];
+#pragma unroll
+            for (int c = 0; c < 4; c++) out[c] = (gv[c] - qv[c] * dot) / act.qlen;
+        } else {
+#pragma unroll
+            for (int c = 0; c < 4; c++) out[c] = gv[c] / act.qlen;
+        }
+        gq = make_float4(out[0], out[1], out[2], out[3]);
+#pragma unroll
+        for (int k = 0; k < 3; k++) dscale[k] = dscale[k] * scale[k];
+        const float gop = grad_opacities != nullptr ? grad_opacities[i] : 0.0f;
+        const float dlogit = gop * (act.opacity * (1.0f - act.opacity));
+        grad_logits[i] = ACCUMULATE ? grad_logits[i] + dlogit : dlogit;
+    }
+    if (ACCUMULATE) {
+        const float4 old = reinterpret_cast<const float4*>(grad_quats)[i];
+        gq = make_float4(old.x + gq.x, old.y + gq.y, old.z + gq.z, old.w + gq.w);
+#pragma unroll
+        for (int k = 0; k < 3; k++) dscale[k] = grad_scales[3 * i + k] + dscale[k];
+    }
     reinterpret_cast<float4*>(grad_quats)[i] = gq;
 #pragma unroll
     for (int k = 0; k < 3; k++) grad_scales[3 * i + k] = dscale[k];
@@ -199,7 +273,10 @@ __global__ void __launch_bounds__(256) project_backward_kernel(int n, Camera cam
     dz += dz_inv * (-zz_inv);
     if (!g.behind) dp[2] += dz;
 #pragma unroll
-    for (int k = 0; k < 3; k++) grad_means[3 * i + k] = g.R[0][k] * dp[0] + g.R[1][k] * dp[1] + g.R[2][k] * dp[2];
+    for (int k = 0; k < 3; k++) {
+        const float gm = g.R[0][k] * dp[0] + g.R[1][k] * dp[1] + g.R[2][k] * dp[2];
+        grad_means[3 * i + k] = ACCUMULATE ? grad_means[3 * i + k] + gm : gm;
+    }
 }
 
 bool aligned(const void* p, uintptr_t bytes) { return (reinterpret_cast<uintptr_t>(p) & (bytes - 1)) == 0; }
@@ -220,8 +297,8 @@ extern "C" int hds_project_forward(int n, const float* means, const float* scale
     HDS_REQUIRE(aligned(quats, 16) && aligned(means2D, 8), HDS_ERR_INVALID,
                 "project_forward: quats must be 16-byte and means2D 8-byte aligned");
     Camera cam{fx, fy, cx, cy, width, height, near_plane, low_pass, fov_scale};
-    project_forward_kernel<<<(n + 255) / 256, 256, 0, stream>>>(n, cam, world_to_camera, means, scales, quats, opacities, means2D,
-                                                                depths, radii, conics);
+    project_forward_kernel<false><<<(n + 255) / 256, 256, 0, stream>>>(n, cam, world_to_camera, means, scales, quats,
+                                                                       opacities, means2D, depths, radii, conics, nullptr);
     HDS_CHECK_LAUNCH("project_forward_kernel");
     return HDS_OK;
 }
@@ -237,8 +314,54 @@ extern "C" int hds_project_backward(int n, const float* grad_means2D, const floa
     HDS_REQUIRE(aligned(quats, 16) && aligned(grad_quats, 16), HDS_ERR_INVALID,
                 "project_backward: quats and grad_quats must be 16-byte aligned");
     Camera cam{fx, fy, cx, cy, width, height, near_plane, low_pass, fov_scale};
-    project_backward_kernel<<<(n + 255) / 256, 256, 0, stream>>>(n, cam, world_to_camera, grad_means2D, grad_conics, means, scales,
-                                                                 quats, grad_means, grad_scales, grad_quats);
+    project_backward_kernel<false, false><<<(n + 255) / 256, 256, 0, stream>>>(
+        n, cam, world_to_camera, grad_means2D, grad_conics, means, scales, quats, grad_means, grad_scales, grad_quats,
+        nullptr, nullptr, nullptr);
+    HDS_CHECK_LAUNCH("project_backward_kernel");
+    return HDS_OK;
+}
+
+extern "C" int hds_project_forward_raw(int n, const float* means, const float* log_scales, const float* quats,
+                                       const float* opacity_logits, const float* world_to_camera, float fx, float fy,
+                                       float cx, float cy, int width, int height, float near_plane, float low_pass,
+                                       float fov_scale, float* means2D, float* depths, float* radii, float* conics,
+                                       float* opacities, hds_stream_t stream) {
+    clear_error();
+    HDS_REQUIRE(n >= 0 && width > 0 && height > 0, HDS_ERR_INVALID, "project_forward_raw: bad sizes n=%d %dx%d", n,
+                width, height);
+    if (n == 0) return HDS_OK;
+    HDS_REQUIRE(aligned(quats, 16) && aligned(means2D, 8), HDS_ERR_INVALID,
+                "project_forward_raw: quats must be 16-byte and means2D 8-byte aligned");
+    Camera cam{fx, fy, cx, cy, width, height, near_plane, low_pass, fov_scale};
+    project_forward_kernel<true><<<(n + 255) / 256, 256, 0, stream>>>(n, cam, world_to_camera, means, log_scales, quats,
+                                                                      opacity_logits, means2D, depths, radii, conics,
+                                                                      opacities);
+    HDS_CHECK_LAUNCH("project_forward_kernel");
+    return HDS_OK;
+}
+
+extern "C" int hds_project_backward_raw(int n, const float* grad_means2D, const float* grad_conics,
+                                        const float* grad_opacities, const float* means, const float* log_scales,
+                                        const float* quats, const float* opacity_logits, const float* world_to_camera,
+                                        float fx, float fy, float cx, float cy, int width, int height,
+                                        float near_plane, float low_pass, float fov_scale, float* grad_means,
+                                        float* grad_log_scales, float* grad_quats, float* grad_opacity_logits,
+                                        int accumulate, hds_stream_t stream) {
+    clear_error();
+    HDS_REQUIRE(n >= 0 && width > 0 && height > 0, HDS_ERR_INVALID, "project_backward_raw: bad sizes");
+    if (n == 0) return HDS_OK;
+    HDS_REQUIRE(aligned(quats, 16) && aligned(grad_quats, 16), HDS_ERR_INVALID,
+                "project_backward_raw: quats and grad_quats must be 16-byte aligned");
+    Camera cam{fx, fy, cx, cy, width, height, near_plane, low_pass, fov_scale};
+    const unsigned blocks = (unsigned)((n + 255) / 256);
+    if (accumulate)
+        project_backward_kernel<true, true><<<blocks, 256, 0, stream>>>(
+            n, cam, world_to_camera, grad_means2D, grad_conics, means, log_scales, quats, grad_means, grad_log_scales,
+            grad_quats, opacity_logits, grad_opacities, grad_opacity_logits);
+    else
+        project_backward_kernel<true, false><<<blocks, 256, 0, stream>>>(
+            n, cam, world_to_camera, grad_means2D, grad_conics, means, log_scales, quats, grad_means, grad_log_scales,
+            grad_quats, opacity_logits, grad_opacities, grad_opacity_logits);
     HDS_CHECK_LAUNCH("project_backward_kernel");
     return HDS_OK;
 }

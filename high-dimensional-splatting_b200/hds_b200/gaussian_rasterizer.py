@@ -326,6 +326,53 @@ def project_gaussians_backward(grad_means2D, grad_conics, means, scales, quats, 
     return gm, gs, gq
 
 
+def project_gaussians_raw(means, log_scales, quats, opacity_logits, world_to_camera, fx: float, fy: float, cx: float,
+                          cy: float, width: int, height: int, near_plane: float, low_pass: float, fov_scale: float):
+    """project_gaussians of the model's raw parameters, activated in the kernel (exp of the log-scales,
+    normalised quats, sigmoid of the opacity logits).  Returns (means2D [N,2], depths [N], radii [N],
+    conics [N,3], opacities shaped like opacity_logits)."""
+    n = means.shape[0]
+    dev = means.device
+    pose = world_to_camera.contiguous()
+    logits = opacity_logits.contiguous()
+    means2D = torch.empty(n, 2, dtype=_F32, device=dev)
+    depths = torch.empty(n, dtype=_F32, device=dev)
+    radii = torch.empty(n, dtype=_F32, device=dev)
+    conics = torch.empty(n, 3, dtype=_F32, device=dev)
+    opacities = torch.empty_like(logits)
+    check(lib.hds_project_forward_raw(n, ptr(means), ptr(log_scales), ptr(quats), ptr(logits), ptr(pose), float(fx),
+                                      float(fy), float(cx), float(cy), int(width), int(height), float(near_plane),
+                                      float(low_pass), float(fov_scale), ptr(means2D), ptr(depths), ptr(radii),
+                                      ptr(conics), ptr(opacities), stream_of(dev)))
+    return means2D, depths, radii, conics, opacities
+
+
+def project_gaussians_raw_backward(grad_means2D, grad_conics, grad_opacities, means, log_scales, quats, opacity_logits,
+                                   world_to_camera, fx: float, fy: float, cx: float, cy: float, width: int,
+                                   height: int, near_plane: float, low_pass: float, fov_scale: float, into=None):
+    """Backward of project_gaussians_raw: (dL/dmeans, dL/dlog_scales, dL/dquats, dL/dopacity_logits).
+    grad_opacities may be None.  With into = four contiguous float32 buffers shaped like the raw
+    parameters, the gradients are added to them instead, and those buffers are returned."""
+    n = means.shape[0]
+    dev = means.device
+    pose = world_to_camera.contiguous()
+    like = (means, log_scales, quats, opacity_logits)
+    if into is None:
+        bufs, accumulate = tuple(torch.empty_like(t) for t in like), 0
+    else:
+        bufs, accumulate = tuple(into), 1
+        for name, buf, t in zip(("grad_means", "grad_log_scales", "grad_quats", "grad_opacity_logits"), bufs, like):
+            if buf.shape != t.shape or buf.dtype != _F32 or not buf.is_contiguous() or buf.device != t.device:
+                raise ValueError(f"{name} must be a contiguous float32 tensor of shape {tuple(t.shape)}")
+    gop = None if grad_opacities is None else grad_opacities.contiguous()
+    check(lib.hds_project_backward_raw(n, ptr(grad_means2D), ptr(grad_conics), ptr(gop) if gop is not None else None,
+                                       ptr(means), ptr(log_scales), ptr(quats), ptr(opacity_logits), ptr(pose),
+                                       float(fx), float(fy), float(cx), float(cy), int(width), int(height),
+                                       float(near_plane), float(low_pass), float(fov_scale), ptr(bufs[0]),
+                                       ptr(bufs[1]), ptr(bufs[2]), ptr(bufs[3]), accumulate, stream_of(dev)))
+    return bufs
+
+
 def ssim_forward(rendered, gt):
     """ssim.cu:306-338.  Returns (ssim_map, d_mu, d_aa, d_ab), each [H,W,3]."""
     if not (rendered.is_cuda and gt.is_cuda):

@@ -22,6 +22,10 @@ SIGNATURES = {
                             c_float, P, P, P, P, S],
     "hds_project_backward": [c_int, P, P, P, P, P, P, c_float, c_float, c_float, c_float, c_int, c_int, c_float,
                              c_float, c_float, P, P, P, S],
+    "hds_project_forward_raw": [c_int, P, P, P, P, P, c_float, c_float, c_float, c_float, c_int, c_int, c_float,
+                                c_float, c_float, P, P, P, P, P, S],
+    "hds_project_backward_raw": [c_int, P, P, P, P, P, P, P, P, c_float, c_float, c_float, c_float, c_int, c_int,
+                                 c_float, c_float, c_float, P, P, P, P, c_int, S],
     "hds_eval_sh_forward": [c_int, c_int, P, P, P, P, P, S],
     "hds_eval_sh_backward_adam": [c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, c_float, c_float, c_float, c_float,
                                   c_float, c_float, c_float, P, S],

@@ -1,4 +1,5 @@
-"""Projection autograd node: mirrors gaussian_splatting/rasterizer/projection.py of the reference."""
+"""Projection autograd nodes: mirrors gaussian_splatting/rasterizer/projection.py of the reference, plus a
+form that takes the model's raw parameters and applies their activations in the kernel."""
 from __future__ import annotations
 
 import torch
@@ -55,3 +56,57 @@ class ProjectGaussians(torch.autograd.Function):
 
 
 project_gaussians = ProjectGaussians.apply
+
+
+class ProjectGaussiansRaw(torch.autograd.Function):
+    """ProjectGaussians of the model's raw parameters, with the activations of the reference's
+    utils/gaussian.py:73-98 (exp of the log-scales, normalised quaternions, sigmoid of the opacity
+    logits) inside the projection kernels instead of torch glue.
+
+    Returns means2D, depths, radii and conics as ProjectGaussians does, plus the activated opacities
+    (shaped like the logits) for the blend; their gradient flows back to the logits.  Under
+    hds_b200.rasterizer.accumulate_leaf_grads() (active during this forward), when the four raw
+    parameters are leaves that hold float32 .grad buffers of their shapes, the backward adds the four
+    gradients into those buffers and hands autograd none for them."""
+
+    @staticmethod
+    def forward(ctx, means, log_scales, quats, opacity_logits, world_to_camera, fx, fy, cx, cy, width, height):
+        from . import rasterizer
+
+        leaves = (means, log_scales, quats, opacity_logits)
+        ctx.leaves = leaves if (rasterizer.ACCUMULATE_INTO_LEAF_GRAD and all(t.is_leaf for t in leaves)) else None
+        means, log_scales, quats = means.contiguous(), log_scales.contiguous(), quats.contiguous()
+        opacity_logits = opacity_logits.contiguous()
+        outputs = rasterizer._get_rasterizer().project_gaussians_raw(
+            means, log_scales, quats, opacity_logits, world_to_camera, fx, fy, cx, cy, width, height, NEAR_PLANE,
+            LOW_PASS, JACOBIAN_FOV_SCALE)
+        ctx.save_for_backward(means, log_scales, quats, opacity_logits, world_to_camera)
+        ctx.camera = (fx, fy, cx, cy, width, height)
+        ctx.mark_non_differentiable(outputs[1], outputs[2])
+        return outputs
+
+    @staticmethod
+    def backward(ctx, grad_means2D, grad_depths, grad_radii, grad_conics, grad_opacities):
+        from .rasterizer import _get_rasterizer
+        from .sh import _grad_buffer
+
+        means, log_scales, quats, logits, world_to_camera = ctx.saved_tensors
+        if grad_means2D is None:
+            grad_means2D = torch.zeros(means.shape[0], 2, device=means.device)
+        if grad_conics is None:
+            grad_conics = torch.zeros(means.shape[0], 3, device=means.device)
+        args = (grad_means2D.contiguous(), grad_conics.contiguous(), grad_opacities, means, log_scales, quats, logits,
+                world_to_camera, *ctx.camera, NEAR_PLANE, LOW_PASS, JACOBIAN_FOV_SCALE)
+        none = (None,) * 7
+        if ctx.leaves is not None and all(ctx.needs_input_grad[:4]):
+            bufs = [_grad_buffer(leaf, like) for leaf, like in zip(ctx.leaves, (means, log_scales, quats, logits))]
+            if all(b is not None for b in bufs):
+                with torch.cuda.nvtx.range("project_backward"):
+                    _get_rasterizer().project_gaussians_raw_backward(*args, into=bufs)
+                return (None, None, None, None) + none
+        with torch.cuda.nvtx.range("project_backward"):
+            grads = _get_rasterizer().project_gaussians_raw_backward(*args)
+        return (*grads, *none)
+
+
+project_gaussians_raw = ProjectGaussiansRaw.apply

@@ -70,6 +70,26 @@ int hds_project_backward(int n, const float* grad_means2D, const float* grad_con
                          float fov_scale, float* grad_means, float* grad_scales, float* grad_quats,
                          hds_stream_t stream);
 
+/* Projection of the model's raw parameters: log_scales [n,3], unnormalised quats [n,4] and opacity
+ * logits [n] are activated in the kernel (scale = exp, quat = q / max(|q|, 1e-12), opacity =
+ * sigmoid: the reference's utils/gaussian.py:73-98, which runs them as torch glue before
+ * project_gaussians).  Also writes the activated opacities [n] that the blend takes. */
+int hds_project_forward_raw(int n, const float* means, const float* log_scales, const float* quats,
+                            const float* opacity_logits, const float* world_to_camera, float fx, float fy, float cx,
+                            float cy, int width, int height, float near_plane, float low_pass, float fov_scale,
+                            float* means2D, float* depths, float* radii, float* conics, float* opacities,
+                            hds_stream_t stream);
+
+/* Backward of hds_project_forward_raw: gradients of the raw parameters, through the activations.
+ * grad_opacities (dL/d activated opacity, from the blend) may be NULL.  accumulate != 0 adds the four
+ * gradients to what their buffers hold; 0 writes them. */
+int hds_project_backward_raw(int n, const float* grad_means2D, const float* grad_conics, const float* grad_opacities,
+                             const float* means, const float* log_scales, const float* quats,
+                             const float* opacity_logits, const float* world_to_camera, float fx, float fy, float cx,
+                             float cy, int width, int height, float near_plane, float low_pass, float fov_scale,
+                             float* grad_means, float* grad_log_scales, float* grad_quats,
+                             float* grad_opacity_logits, int accumulate, hds_stream_t stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Spherical harmonics.  Replaces eval_sh (sh.cu:157-168; glue utils/sh.py:26-59).
  * sh_dc [n,1,3], sh_rest [n,15,3], dirs [n,3] unit vectors, radii [n]; rgb [n,3].

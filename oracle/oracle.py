@@ -58,6 +58,8 @@ def lib():
                                              c_int, c_int, c_float, c_float, c_float, F32P, F32P, F32P, F32P]
         L.oracle_project_backward.argtypes = [c_int, F32P, F32P, F32P, F32P, F32P, F32P, c_float, c_float, c_float,
                                               c_float, c_int, c_int, c_float, c_float, c_float, F32P, F32P, F32P]
+        L.oracle_activate.argtypes = [c_int, F32P, F32P, F32P, F32P, F32P, F32P]
+        L.oracle_activate_backward.argtypes = [c_int, F32P, F32P, F32P, F32P, F32P, vp, F32P, F32P, F32P]
         L.oracle_eval_sh_forward.argtypes = [c_int, c_int, F32P, F32P, F32P, F32P, F32P]
         L.oracle_eval_sh_backward.argtypes = [c_int, c_int, F32P, F32P, F32P, F32P, F32P, F32P, F32P, F32P]
         L.oracle_adam.argtypes = [c_int, F32P, F32P, F32P, F32P, c_float, c_float, c_float, c_float, c_float,
@@ -140,6 +142,26 @@ def eval_sh_backward(grad_rgb, sh_dc, sh_rest, dirs, degree, radii):
     lib().oracle_eval_sh_backward(n, degree, f32(grad_rgb), f32(sh_dc), f32(sh_rest), f32(dirs), f32(radii),
                                   gdc, grest, gd)
     return gdc, grest, gd
+
+
+def activate(log_scales, quats, logits):
+    """The model's activations (utils/gaussian.py:73-98): (scales [N,3], unit quats [N,4], opacities)."""
+    ls, q, lg = f32(log_scales), f32(quats), f32(logits)
+    n = q.shape[0]
+    scales, unit, opac = np.zeros((n, 3), np.float32), np.zeros((n, 4), np.float32), np.zeros(lg.shape, np.float32)
+    lib().oracle_activate(n, ls, q, lg, scales, unit, opac)
+    return scales, unit, opac
+
+
+def activate_backward(log_scales, quats, logits, grad_scales, grad_unit_quats, grad_opacities=None):
+    """Chain rule of activate: (dL/dlog_scales, dL/dquats, dL/dlogits)."""
+    ls, q, lg = f32(log_scales), f32(quats), f32(logits)
+    n = q.shape[0]
+    gls, gq, glg = np.zeros((n, 3), np.float32), np.zeros((n, 4), np.float32), np.zeros(lg.shape, np.float32)
+    gop = None if grad_opacities is None else f32(grad_opacities)
+    lib().oracle_activate_backward(n, ls, q, lg, f32(grad_scales), f32(grad_unit_quats),
+                                   None if gop is None else gop.ctypes.data, gls, gq, glg)
+    return gls, gq, glg
 
 
 def view_dirs(means, camera_center):

@@ -266,6 +266,103 @@ def test_projection_bit_exact(ext, which):
         assert np.array_equal(host(g), wv), f"{nm} differs"
 
 
+def _raw_params(which, zero_quat=True):
+    """Raw model parameters whose activations give a test scene: log-scales, quaternions scaled by
+    random factors in [0.5, 2) (with zero_quat, one of them zero: the clamp of normalize), opacity
+    logits."""
+    from hds_b200 import scenes
+
+    s = scenes.config0(0, channels=0) if which == "config0" else scenes.config1(1, n=50_000, channels=0)
+    rng = np.random.default_rng(3)
+    log_scales = np.log(s.scales.numpy()).astype(np.float32)
+    quats = (s.quats.numpy() * rng.uniform(0.5, 2.0, (s.n, 1))).astype(np.float32)
+    if zero_quat:
+        quats[7] = 0.0
+    op = np.clip(s.opacities.numpy(), 1e-6, 1 - 1e-6)
+    logits = np.log(op / (1 - op)).astype(np.float32)
+    return s.means.numpy(), log_scales, quats, logits, s.cameras[0]
+
+
+@pytest.mark.parametrize("which", ["config0", "config1"])
+def test_projection_raw_bit_exact(ext, which):
+    """The projection of raw parameters (exp, normalize and sigmoid in the kernel) equals the oracle's
+    activations followed by its projection, forward and backward, bit for bit; the accumulating
+    backward adds exactly those gradients."""
+    means, ls, q, lg, cam = _raw_params(which)
+    args = (cam.fx, cam.fy, cam.cx, cam.cy, cam.width, cam.height)
+    consts = (oracle.NEAR_PLANE, oracle.LOW_PASS, oracle.FOV_SCALE)
+    sc, unit, op = oracle.activate(ls, q, lg)
+    pose = cam.world_to_camera.numpy()
+    want = oracle.project_forward(means, sc, unit, op, pose, *args)
+    t_means, t_ls, t_q, t_lg, t_pose = cuda(means, ls, q, lg, pose)
+    got = ext.project_gaussians_raw(t_means, t_ls, t_q, t_lg, t_pose, *args, *consts)
+    for nm, g, wv in zip(("means2D", "depths", "radii", "conics", "opacities"), got, (*want, op)):
+        assert np.array_equal(host(g), wv), f"{nm} differs"
+    rng = np.random.default_rng(5)
+    n = means.shape[0]
+    gm2 = rng.standard_normal((n, 2)).astype(np.float32)
+    gcon = rng.standard_normal((n, 3)).astype(np.float32)
+    gop = rng.standard_normal(lg.shape).astype(np.float32)
+    g_means, g_sc, g_unit = oracle.project_backward(gm2, gcon, means, sc, unit, pose, *args)
+    g_ls, g_q, g_lg = oracle.activate_backward(ls, q, lg, g_sc, g_unit, gop)
+    t_gm2, t_gcon, t_gop = cuda(gm2, gcon, gop)
+    got = ext.project_gaussians_raw_backward(t_gm2, t_gcon, t_gop, t_means, t_ls, t_q, t_lg, t_pose, *args, *consts)
+    for nm, g, wv in zip(("means", "log_scales", "quats", "logits"), got, (g_means, g_ls, g_q, g_lg)):
+        assert np.array_equal(host(g), wv), f"grad {nm} differs"
+    bases = [rng.standard_normal(a.shape).astype(np.float32) for a in (means, ls, q, lg)]
+    bufs = cuda(*bases)
+    ext.project_gaussians_raw_backward(t_gm2, t_gcon, t_gop, t_means, t_ls, t_q, t_lg, t_pose, *args, *consts,
+                                       into=bufs)
+    for nm, buf, base, wv in zip(("means", "log_scales", "quats", "logits"), bufs, bases,
+                                 (g_means, g_ls, g_q, g_lg)):
+        assert np.array_equal(host(buf), base + wv), f"accumulated grad {nm} differs"
+    got = ext.project_gaussians_raw_backward(t_gm2, t_gcon, None, t_means, t_ls, t_q, t_lg, t_pose, *args, *consts)
+    assert np.array_equal(host(got[3]), np.zeros_like(lg)), "no opacity gradient must give zero logit gradients"
+
+
+@pytest.mark.parametrize("accumulate", [False, True])
+def test_projection_raw_matches_torch_activations(ext, accumulate):
+    """project_gaussians_raw against the reference's composition (torch exp, normalize and sigmoid,
+    then the projection node) through autograd: same outputs within float rounding of the
+    activations, and gradients within the gradient tolerance."""
+    import torch.nn.functional as F
+
+    from hds_b200.projection import project_gaussians, project_gaussians_raw
+    from hds_b200.rasterizer import accumulate_leaf_grads
+
+    # No zero quaternion here: at the clamp both sides divide by 1e-12, and that row would set the
+    # gradient tolerance's scale.
+    means, ls, q, lg, cam = _raw_params("config1", zero_quat=False)
+    args = (cam.fx, cam.fy, cam.cx, cam.cy, cam.width, cam.height)
+    pose = cam.world_to_camera.cuda()
+    rng = np.random.default_rng(9)
+    n = means.shape[0]
+    gm2, gcon, gop = (torch.from_numpy(rng.standard_normal(shape).astype(np.float32)).cuda()
+                      for shape in ((n, 2), (n, 3), lg.shape))
+
+    def leaves():
+        return [torch.from_numpy(a).cuda().requires_grad_(True) for a in (means, ls, q, lg)]
+
+    r = leaves()
+    r_out = project_gaussians(r[0], torch.exp(r[1]), F.normalize(r[2], dim=-1), torch.sigmoid(r[3]), pose, *args)
+    r_op = torch.sigmoid(r[3])
+    torch.autograd.backward([r_out[0], r_out[3], r_op], [gm2, gcon, gop])
+
+    o = leaves()
+    if accumulate:
+        for t in o:
+            t.grad = torch.zeros_like(t)
+    with accumulate_leaf_grads() if accumulate else torch.enable_grad():
+        o_out = project_gaussians_raw(*o, pose, *args)
+    torch.autograd.backward([o_out[0], o_out[3], o_out[4]], [gm2, gcon, gop])
+    np.testing.assert_allclose(host(o_out[4]), host(r_op), rtol=1e-6, atol=1e-7)
+    vis = (host(o_out[2]) > 0) & (host(r_out[2]) > 0)
+    assert vis.mean() > 0.5 and np.mean((host(o_out[2]) > 0) != (host(r_out[2]) > 0)) < 1e-3
+    np.testing.assert_allclose(host(o_out[0])[vis], host(r_out[0])[vis], rtol=1e-5, atol=1e-3)
+    for nm, a, b in zip(("means", "log_scales", "quats", "logits"), o, r):
+        assert_grads_close(host(a.grad), host(b.grad), nm)
+
+
 @pytest.mark.parametrize("degree", [0, 1, 2, 3])
 def test_sh_bit_exact(ext, golden, degree):
     g = golden("sh.npz")
