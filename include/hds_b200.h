@@ -138,14 +138,16 @@ int hds_eval_sh_backward_view(int n, int degree, const float* grad_rgb, const fl
  * Binning + RGB blend.  Together these three calls replace rasterize (forward.cu:239-435).
  *
  * 1. hds_rasterize_prepare (forward.cu:284-326): culls, packs conic4 [n,4] = (a, b, c, 0) and
- *    color_opacity [n,4] = (r, g, b, opacity), counts the tiles each gaussian touches, prefix-sums
- *    the counts and writes the total number of (tile, gaussian) pairs to *num_duplicates (host).
+ *    color_opacity [n,4] = (r, g, b, opacity), counts the tiles each gaussian touches, sums the
+ *    counts and writes the total number of (tile, gaussian) pairs to *num_duplicates (host).
  *    It synchronises `stream`.  scratch: hds_rasterize_prepare_scratch_bytes(n) bytes, which must
  *    stay untouched until hds_rasterize_sort has been queued.
- * 2. hds_rasterize_sort (forward.cu:340-404): emits keys tile << 32 | depth bits, radix-sorts them
- *    stably on 32 + ceil(log2 tiles) bits, and writes values_sorted [num_duplicates] (gaussian ids)
- *    and tile_ranges [tiles,2] ([start, end), empty tiles 0, 0).  keys_sorted may be NULL; when
- *    given it receives the sorted keys (bit-exactness checks).
+ * 2. hds_rasterize_sort (forward.cu:340-404): writes values_sorted [num_duplicates] (gaussian ids)
+ *    in the order of the reference's stable sort of the keys tile << 32 | depth bits -- every
+ *    tile's list front to back, equal depths in gaussian order -- and tile_ranges [tiles,2]
+ *    ([start, end), empty tiles 0, 0).  It reaches that order by a stable depth sort of the
+ *    gaussians and a stable tile-id sort of the pairs emitted in depth order.  keys_sorted may be
+ *    NULL; when given it receives the sorted 64-bit keys (bit-exactness checks).
  * 3. hds_render_forward (forward.cu:406-434): front-to-back FP32 blend.  image4 [H,W,4] (the
  *    reference's padded layout; channel 3 written 0), final_T [H,W], n_contrib [H,W] (1-based
  *    index of the last blended list entry).
