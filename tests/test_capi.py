@@ -61,3 +61,29 @@ def test_bad_arguments_are_rejected_on_the_host():
     assert rc == 4 and b"scratch" in native.lib.hds_last_error()
     with pytest.raises(RuntimeError, match="scratch"):
         native.check(rc)
+
+
+def test_new_entry_points_reject_bad_arguments_on_the_host():
+    """The view-direction SH, the SH accumulate and the raw-parameter projection validate their
+    arguments before touching the device (no GPU needed)."""
+    from hds_b200 import native
+
+    lib = native.lib
+    assert lib.hds_eval_sh_forward_view(10, 3, *([None] * 6), None) == 1
+    assert b"camera_center" in lib.hds_last_error()
+    assert lib.hds_eval_sh_backward_view(10, 3, *([None] * 9), 0, None) == 1
+    assert b"camera_center" in lib.hds_last_error()
+    assert lib.hds_eval_sh_forward_view(10, 5, *([None] * 6), None) == 1
+    assert b"degree" in lib.hds_last_error()
+    assert lib.hds_eval_sh_backward_accumulate(-1, 3, *([None] * 8), None) == 1
+    assert b"n must be" in lib.hds_last_error()
+    # quats 4 bytes off 16-byte alignment
+    assert lib.hds_project_forward_raw(10, None, None, 4, None, None, 1.0, 1.0, 0.0, 0.0, 16, 16, 0.2, 0.3, 1.3,
+                                       None, None, None, None, None, None) == 1
+    assert b"16-byte" in lib.hds_last_error()
+    assert lib.hds_project_backward_raw(10, *([None] * 8), 1.0, 1.0, 0.0, 0.0, 0, 16, 0.2, 0.3, 1.3,
+                                        *([None] * 4), 0, None) == 1
+    assert b"bad sizes" in lib.hds_last_error()
+    # Zero gaussians is a valid empty call.
+    assert lib.hds_project_forward_raw(0, None, None, None, None, None, 1.0, 1.0, 0.0, 0.0, 16, 16, 0.2, 0.3, 1.3,
+                                       None, None, None, None, None, None) == 0
