@@ -11,7 +11,11 @@ that its training loop runs) -- and backpropagates into every raw gaussian param
 over its views; with N > 1 ranks the per-gaussian gradients (59 + C floats each) are then
 all-reduced over NCCL.  Scaling is weak: every rank renders its own views.  value = views / s over all ranks.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--channels C] [--views V]
+On one GPU the line also carries the config-2 channel sweep (C = 32 ... 512, forward and backward
+timed separately in the reference harness's scope, median of 50 after 10 warm-ups) and the CPU
+oracle's rate on the host cores (cpu_baseline).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--channels C] [--views V] [--no-sweep]
     python bench.py --impl reference ...   # the CPU oracle on a bounded sample of the same workload
 """
 from __future__ import annotations
@@ -45,7 +49,8 @@ def parse_args():
     ap.add_argument("--gaussians", type=int, default=1_180_000)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--sweep", action="store_true", help="also time fwd/bwd per C in the reference harness scope")
+    ap.add_argument("--no-sweep", action="store_true",
+                    help="skip the channel sweep (fwd and bwd per C in the reference harness scope; 1 GPU only)")
     return ap.parse_args()
 
 
@@ -229,11 +234,9 @@ def zero_grads(wl):
 
 
 def tile_stats(wl, device):
-    """Visited list length per tile (min(list length, max contributor index)) for one view, for the
-    algorithmic byte / flop counts of the roofline."""
+    """Counts of one view of the step, for the algorithmic byte / flop models of the rooflines."""
     import torch
 
-    from hds_b200 import gaussian_rasterizer as ext
     from hds_b200.projection import project_gaussians_raw
 
     L = wl["leaves"]
@@ -242,9 +245,21 @@ def tile_stats(wl, device):
         means2D, depths, radii, conics, opacities = project_gaussians_raw(
             L["means"], L["log_scales"], L["quats"], L["opacity_logits"], wl["pose_dev"][0], cam.fx, cam.fy, cam.cx,
             cam.cy, cam.width, cam.height)
-        colors = torch.zeros_like(L["means"])
+    return projected_stats(means2D, depths, radii, conics, opacities, cam, device)
+
+
+def projected_stats(means2D, depths, radii, conics, opacities, cam, device):
+    """Pixels P, duplicated (tile, gaussian) pairs D, visited pairs V (per tile, min(list length, the
+    tile's largest contributor count)) and visible gaussians of one projected view."""
+    import torch
+
+    from hds_b200 import gaussian_rasterizer as ext
+
+    with torch.no_grad():
+        colors = torch.zeros_like(conics)
+        bg = torch.zeros(3, device=device)
         _, _, n_contrib, values, ranges, _, _ = ext.rasterize(means2D, depths, radii, conics, colors, opacities,
-                                                             wl["bg"], cam.width, cam.height)
+                                                             bg, cam.width, cam.height)
         h, w = cam.height, cam.width
         tx, ty = (w + 15) // 16, (h + 15) // 16
         pad = torch.zeros(ty * 16, tx * 16, dtype=torch.int32, device=device)
@@ -256,60 +271,97 @@ def tile_stats(wl, device):
             "visible": int((radii > 0).sum())}
 
 
-# DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one-pass ncu captures of
-# this bench's own workload: (call, channels, gaussians) -> (bytes, summary under profiles/).
-MEASURED_TRAFFIC = {
-    ("hds_render_backward_fused", 512, 1_180_000):  # the four-block cluster kernel (the default at C = 512)
-        (2.88e9 + 0.832e9, "profiles/feature_backward_traffic_config2_1180k_c512.md"),
-    ("hds_render_features_backward_accumulate", 512, 1_180_000):  # the one-block kernel
-        (2.59e9 + 0.595e9, "profiles/feature_backward_traffic_config2_1180k_c512.md"),
+# DRAM traffic per launch of the dominant call (dram__bytes_read.sum + dram__bytes_write.sum), from
+# one-pass ncu captures of two small cases of this bench's workload (one view, the bench's C, N
+# gaussians), fitted as a + b N and evaluated at the bench's N: the per-pixel terms (dL/dout, the
+# image) do not grow with N, the per-gaussian ones do.  (call, channels) -> (a bytes, b bytes per
+# gaussian, summary under profiles/).
+TRAFFIC_FIT = {}
+
+# The algorithmic model of each stage of one view (the hot-path table's measurement row): bytes that
+# must cross HBM, or tensor flops for the feature blend.  P pixels, V visited (tile, gaussian) pairs
+# (min(list length, the tile's last contributor)), D duplicated (tile, gaussian) pairs, n gaussians,
+# vis visible gaussians, C channels.
+STAGES = {
+    "preprocess": ("hds_project_forward_raw", "hds_eval_sh_forward_view"),
+    "binning": ("hds_rasterize_prepare", "hds_rasterize_sort"),
+    "feature_forward": ("hds_render_features_forward",),
+    "backward": ("hds_render_backward_fused", "hds_render_features_backward", "hds_render_features_backward_accumulate",
+                 "hds_render_backward"),
+    "preprocess_backward": ("hds_project_backward_raw", "hds_eval_sh_backward_view"),
+    "ssim_forward": ("hds_ssim_forward",),
+    "ssim_backward": ("hds_ssim_backward",),
 }
 
 
-def roofline(name, ms_per_launch, stats, args, peaks, n):
-    """Algorithmic bytes (or flops) per launch of the dominant call over its measured duration."""
-    C = args.channels
-    P = stats["pixels"]
-    V = stats["visited"]
-    if name == "hds_render_features_forward":
-        flops = 2.0 * C * 256 * V  # weights x features per visited (tile, gaussian), 256 px per tile
-        tf32_peak = peaks["bf16_tflops"] / 2.0
-        ach = flops / (ms_per_launch * 1e-3) / 1e12
-        return {"bound": "tensor", "achieved": ach, "peak": tf32_peak, "unit": "TFLOP/s", "frac": ach / tf32_peak,
-                "traffic": None, "kernel": name,
-                "peak_note": f"TF32 dense = half the {peaks['source']} cuBLAS bf16 rate"}
-    if name in ("hds_render_features_backward", "hds_render_features_backward_accumulate",
-                "hds_render_backward_fused"):
-        nbytes = P * (4 * C + 12) + V * (4 * C + 32) + n * (4 * C + 36) * 2
-        if name == "hds_render_backward_fused":  # plus the RGB terms: dL/dimage, colours and their gradient
-            nbytes += P * 12 + n * 24
-    elif name == "hds_render_backward":
-        nbytes = P * (12 + 8) + V * 44 + n * 36 * 2
-    else:
-        nbytes = None
-    if nbytes is None:
-        return {"bound": "hbm", "achieved": None, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": None,
-                "traffic": None, "kernel": name}
-    ach = nbytes / (ms_per_launch * 1e-3) / 1e9
-    out = {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": ach / peaks["hbm_gbs"],
-           "traffic": None, "kernel": name, "algorithmic_bytes": nbytes}
-    measured = MEASURED_TRAFFIC.get((name, C, args.gaussians))
-    if measured is not None:
-        out["traffic"], out["traffic_source"] = measured
+def stage_model(stage, st, C, n, rgb_terms=True):
+    """(bound, algorithmic bytes or flops, formula) of one view's stage."""
+    P, V, D, vis = st["pixels"], st["visited"], st["pairs"], st["visible"]
+    if stage == "preprocess":
+        return "hbm", 84 * n + 192 * vis, "84 B/gaussian + 192 B of SH per visible gaussian"
+    if stage == "binning":
+        return "hbm", 48 * n + 44 * D, "48 B/gaussian + 44 B per duplicated pair"
+    if stage == "feature_forward":
+        return "tensor", 2.0 * C * 256 * V, "2 C 256 V flops (weights x features per visited tile-gaussian pair)"
+    if stage == "backward":
+        b = P * (4 * C + 12) + V * (4 * C + 32) + n * (4 * C + 36) * 2
+        if rgb_terms:
+            b += P * 12 + n * 24
+        return "hbm", b, "P(4C+12) + V(4C+32) + 2n(4C+36) (+ 12P + 24n for the RGB terms)"
+    if stage == "preprocess_backward":
+        return "hbm", 172 * n + 624 * vis, ("projection backward 156 B/gaussian (accumulating), SH backward 16 "
+                                            "B/gaussian + 624 B per visible gaussian (SH read, gradient added)")
+    if stage in ("ssim_forward", "ssim_backward"):
+        return "hbm", 72 * P, "72 B per pixel (3 channels x 4 B x 6 maps)"
+    raise KeyError(stage)
+
+
+def rooflines(call_ms, counts, launches_per_view, st, C, n, peaks):
+    """Per stage of one view: device time (CUDA events on the launch stream, summed over the stage's
+    calls, per view), algorithmic bytes or flops, and the fraction of the measured peak."""
+    out = {}
+    for stage, calls in STAGES.items():
+        ms = sum(call_ms.get(c, 0.0) / max(1, counts.get(c, 0)) * launches_per_view.get(c, 0) for c in calls)
+        if ms <= 0:
+            continue
+        bound, amount, formula = stage_model(stage, st, C, n)
+        if bound == "tensor":
+            peak = peaks["bf16_tflops"] / 2.0
+            ach = amount / (ms * 1e-3) / 1e12
+            out[stage] = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
+                          "ms": ms, "flops": amount, "model": formula,
+                          "peak_note": f"TF32 dense = half the {peaks['source']} cuBLAS bf16 burst rate"}
+        else:
+            ach = amount / (ms * 1e-3) / 1e9
+            out[stage] = {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                          "frac": ach / peaks["hbm_gbs"], "ms": ms, "bytes": amount, "model": formula,
+                          "peak_note": f"{peaks['source']} HBM copy rate"}
     return out
 
 
-CPU_WINDOW = 64  # side of the image windows the CPU oracle renders as its bounded sample
+CPU_WINDOW = 64  # side of the image windows the CPU oracle blends as its bounded sample
+CPU_WINDOWS = 16  # fixed windows of view 0, spread over the image (the same every round and in both legs)
 CPU_MAX_WORKERS = 64  # worker processes at most (each holds a copy of the scene geometry)
-_cpu_state = None  # per worker process: the scene geometry, camera and feature table
+_cpu_state = None  # per worker process: scene slice, full-view projection, window subsets, feature table
 
 
-def _cpu_worker_init(geometry, camera, channels):
-    """Worker set-up, untimed: the oracle library, the scene geometry (means, scales, quats,
-    opacities), the camera (pose, fx, fy, cx, cy) and a seeded [4096, C] feature table.  The
-    oracle's cost does not depend on feature values, and a window is rendered with only the
-    gaussians it sees (rows of the table as their features), so no [N, C] array is built per worker.
-    Workers import numpy and the oracle only."""
+def _cpu_windows(width, height):
+    """CPU_WINDOWS window origins on the view's grid of whole 64 x 64 windows, stratified: every k-th
+    window in row-major order, so that dense and sparse parts of the view are both sampled.  Origins
+    are multiples of 64, so a window's tiles are tiles of the full image."""
+    cols, rows = width // CPU_WINDOW, height // CPU_WINDOW
+    total = cols * rows
+    picks = [(i * total) // CPU_WINDOWS + (total // CPU_WINDOWS) // 2 for i in range(CPU_WINDOWS)]
+    return [((k % cols) * CPU_WINDOW, (k // cols) * CPU_WINDOW) for k in picks]
+
+
+def _cpu_worker_init(raw, sh, camera, channels, workers, rank):
+    """Worker set-up, untimed: the oracle library, the raw parameters of every gaussian (means,
+    log-scales, quaternions, opacity logits) and the SH of this worker's slice, the camera, one
+    full-view projection (the windows blend from it), each window's candidate gaussians, and a
+    seeded [4096, C] feature table (the oracle's cost does not depend on feature values, so rows of
+    the table stand in for each gaussian's features; no [N, C] array per worker).  Workers import
+    numpy and the oracle only."""
     global _cpu_state
     import numpy as np
 
@@ -317,39 +369,96 @@ def _cpu_worker_init(geometry, camera, channels):
     import oracle
 
     oracle.lib()
+    means, log_scales, quats, logits = raw
+    pose, fx, fy, cx, cy, width, height = camera
+    n = means.shape[0]
+    lo, hi = (n * rank) // workers, (n * (rank + 1)) // workers
+    scales, unit, opac = oracle.activate(log_scales, quats, logits)
+    m2, dep, rad, con = oracle.project_forward(means, scales, unit, opac, pose, fx, fy, cx, cy, width, height)
+    # Candidates of a window: visible gaussians whose 3.4-sigma box (beyond the opacity-aware box,
+    # whose factor is at most sqrt(2 ln 255) < 3.34 sigma) meets the window; the window's own
+    # binning then applies the exact test.
+    reach = rad * np.float32(3.4 / 3.0) + np.float32(1.0)
+    subsets = {}
+    for wx, wy in _cpu_windows(width, height):
+        keep = (rad > 0) & (m2[:, 0] + reach >= wx) & (m2[:, 0] - reach <= wx + CPU_WINDOW) \
+            & (m2[:, 1] + reach >= wy) & (m2[:, 1] - reach <= wy + CPU_WINDOW)
+        subsets[(wx, wy)] = np.nonzero(keep)[0]
     table = np.random.default_rng(0).random((4096, channels), dtype=np.float32)
-    _cpu_state = {"oracle": oracle, "geometry": geometry, "camera": camera, "table": table, "channels": channels}
+    gt = np.random.default_rng(1).random((CPU_WINDOW, CPU_WINDOW, 3), dtype=np.float32)
+    _cpu_state = {"oracle": oracle, "slice": (lo, hi), "raw": raw, "sh": sh, "camera": camera,
+                  "proj": (m2, dep, rad, con, opac), "subsets": subsets, "table": table, "gt": gt,
+                  "channels": channels}
 
 
-def _cpu_window(wx, wy):
-    """Forward and backward of the CPU_WINDOW-square window at pixel (wx, wy) of view 0 through the
-    oracle: projection of every gaussian, binning, RGB + C-channel blend, backward.  Returns seconds."""
+def _cpu_slice(_):
+    """Per-gaussian work of one view for this worker's slice, forward and backward: activations,
+    projection, view directions and SH colour, the slice's binning against the full view, then the
+    SH, view-direction, projection and activation backward passes.  Returns seconds."""
     import numpy as np
 
     st = _cpu_state
-    oracle, (means, scales, quats, opac) = st["oracle"], st["geometry"]
-    pose, fx, fy, cx, cy = st["camera"]
+    oracle = st["oracle"]
+    lo, hi = st["slice"]
+    means, log_scales, quats, logits = (a[lo:hi] for a in st["raw"])
+    sh_dc, sh_rest = st["sh"]
+    pose, fx, fy, cx, cy, width, height = st["camera"]
+    center = -(pose[:3, :3].T @ pose[:3, 3])
+    t0 = time.perf_counter()
+    scales, unit, opac = oracle.activate(log_scales, quats, logits)
+    m2, dep, rad, con = oracle.project_forward(means, scales, unit, opac, pose, fx, fy, cx, cy, width, height)
+    dirs, s = oracle.view_dirs(means, center)
+    oracle.eval_sh(sh_dc, sh_rest, dirs, 3, rad)
+    oracle.bin_gaussians(m2, dep, rad, con, opac, width, height)
+    k = hi - lo
+    g2, gc = np.full((k, 2), 1e-3, np.float32), np.full((k, 3), 1e-3, np.float32)
+    _, _, gdirs = oracle.eval_sh_backward(np.full((k, 3), 1e-3, np.float32), sh_dc, sh_rest, dirs, 3, rad)
+    oracle.view_dirs_backward(gdirs, dirs, s)
+    _, gs, gq = oracle.project_backward(g2, gc, means, scales, unit, pose, fx, fy, cx, cy, width, height)
+    oracle.activate_backward(log_scales, quats, logits, gs, gq, np.full(opac.shape, 1e-3, np.float32))
+    return time.perf_counter() - t0
+
+
+def _cpu_window(wx, wy):
+    """Per-pixel work of one CPU_WINDOW-square window of view 0, forward and backward: binning of
+    the window's candidates, the RGB + C-channel blend, SSIM forward and backward of the window,
+    and the blend's backward.  Returns seconds."""
+    import numpy as np
+
+    st = _cpu_state
+    oracle = st["oracle"]
+    m2, dep, rad, con, opac = st["proj"]
+    keep = st["subsets"][(wx, wy)]
     crop = CPU_WINDOW
     t0 = time.perf_counter()
-    m2, dep, rad, con = oracle.project_forward(means, scales, quats, opac, pose, fx, fy, cx - wx, cy - wy, crop, crop)
-    keep = np.nonzero(rad > 0)[0]
-    m2, dep, rad, con, op = m2[keep], dep[keep], rad[keep], con[keep], opac[keep]
+    m2w = m2[keep] - np.array([wx, wy], np.float32)
+    dep_w, rad_w, con_w, op_w = dep[keep], rad[keep], con[keep], opac[keep]
     feats = st["table"][keep % len(st["table"])]
     colors = np.full((len(keep), 3), 0.5, np.float32)
-    r = oracle.rasterize(m2, dep, rad, con, colors, op, crop, crop, background=np.zeros(3), features=feats)
-    g_img = np.full((crop, crop, 3), 1e-3, np.float32)
+    r = oracle.rasterize(m2w, dep_w, rad_w, con_w, colors, op_w, crop, crop, background=np.zeros(3), features=feats)
+    ssim = oracle.ssim_forward(r["image"], st["gt"])
+    g_img = oracle.ssim_backward(np.float32(-0.2 / (crop * crop * 3)), r["image"], st["gt"], *ssim[1:])
     g_feat = np.full((crop, crop, st["channels"]), 1e-3, np.float32)
-    oracle.render_backward(r["ranges"], r["values"], m2, con, colors, op, crop, crop, r["final_T"], r["n_contrib"],
-                           grad_image=g_img, background=np.zeros(3), features=feats, grad_features=g_feat)
+    oracle.render_backward(r["ranges"], r["values"], m2w, con_w, colors, op_w, crop, crop, r["final_T"],
+                           r["n_contrib"], grad_image=g_img, background=np.zeros(3), features=feats,
+                           grad_features=g_feat)
     return time.perf_counter() - t0
 
 
 def cpu_sample(args, rounds: int, warmup: int):
-    """The CPU oracle on every usable host core: one worker process per core (started with spawn, so
-    that a parent that has touched CUDA is safe), each rendering one window per round at its own
-    place in the view.  Untimed warm-up rounds, then timed rounds; scaled to views/s."""
+    """The CPU oracle on every usable host core, one worker process per core (started with spawn, so
+    that a parent that has touched CUDA is safe).  A round restates one view of the bench's step on
+    the CPU, split in two timed phases:
+      A. per-gaussian work: every worker runs its 1/workers slice of all gaussians (activations,
+         projection, SH, binning, and their backward passes) -- a whole view's worth;
+      B. per-pixel work: the CPU_WINDOWS fixed 64 x 64 windows of the view (a fraction f of its
+         pixels) are blended forward and backward with SSIM, one task per window.
+    A view then costs T_A + T_B / f seconds of wall time on these cores.  Untimed warm-up rounds,
+    then timed rounds, all on the same windows."""
     import concurrent.futures
     import multiprocessing
+
+    import torch
 
     from hds_b200 import scenes
 
@@ -358,59 +467,194 @@ def cpu_sample(args, rounds: int, warmup: int):
 
     oracle.lib()  # built here once, before the workers load it
     s = scenes.config1(0, n=args.gaussians, channels=0)
-    geometry = tuple(t.numpy() for t in (s.means, s.scales, s.quats, s.opacities))
+    op = s.opacities.clamp(1e-6, 1 - 1e-6)
+    raw = tuple(t.numpy() for t in (s.means, torch.log(s.scales), s.quats, torch.log(op / (1 - op))))
     cam = scenes.orbit(64)[0]
-    camera = (cam.world_to_camera.numpy(), cam.fx, cam.fy, cam.cx, cam.cy)
-    cols, rows = cam.width // CPU_WINDOW, cam.height // CPU_WINDOW
+    camera = (cam.world_to_camera.numpy(), cam.fx, cam.fy, cam.cx, cam.cy, cam.width, cam.height)
     cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
     workers = min(cores, CPU_MAX_WORKERS)
-
-    def windows(r):
-        # Spread over the view's grid of windows: consecutive indices 37 windows apart.
-        out = []
-        for k in range(workers):
-            idx = ((r * workers + k) * 37) % (cols * rows)
-            out.append(((idx % cols) * CPU_WINDOW, (idx // cols) * CPU_WINDOW))
-        return out
-
+    windows = _cpu_windows(cam.width, cam.height)
+    f = len(windows) * CPU_WINDOW * CPU_WINDOW / (cam.width * cam.height)
     ctx = multiprocessing.get_context("spawn")
-    with concurrent.futures.ProcessPoolExecutor(max_workers=workers, mp_context=ctx, initializer=_cpu_worker_init,
-                                                initargs=(geometry, camera, args.channels)) as pool:
-        for r in range(warmup):
-            list(pool.map(_cpu_window, *zip(*windows(r))))
-        t0 = time.perf_counter()
-        busy = 0.0
-        for r in range(rounds):
-            busy += sum(pool.map(_cpu_window, *zip(*windows(warmup + r))))
-        secs = time.perf_counter() - t0
-    frac = rounds * workers * CPU_WINDOW * CPU_WINDOW / (cam.width * cam.height)
-    return {"value": frac / secs, "unit": "views/s", "cores": workers, "kind": "port",
-            "sample": f"{rounds} rounds x {workers} processes, each a {CPU_WINDOW}x{CPU_WINDOW} window of one "
-                      f"{cam.width}x{cam.height} view ({frac:.4f} views in all, windows spread over the view), "
-                      f"all {s.n} gaussians projected per window, C={args.channels}, fwd+bwd, oracle/hds_oracle.c, "
-                      f"{secs:.1f} s wall, {busy:.1f} s of CPU work"}, secs / max(rounds, 1)
+    pools = []
+    try:
+        # One pool per slice so that worker k always owns slice k; the window tasks go to all of them.
+        for rank in range(workers):
+            lo, hi = (s.n * rank) // workers, (s.n * (rank + 1)) // workers
+            sh = (s.sh_dc[lo:hi].numpy(), s.sh_rest[lo:hi].numpy())
+            pools.append(concurrent.futures.ProcessPoolExecutor(
+                max_workers=1, mp_context=ctx, initializer=_cpu_worker_init,
+                initargs=(raw, sh, camera, args.channels, workers, rank)))
+
+        def run_round():
+            t0 = time.perf_counter()
+            busy_a = sum(fut.result() for fut in [p.submit(_cpu_slice, 0) for p in pools])
+            t_a = time.perf_counter() - t0
+            t0 = time.perf_counter()
+            futs = [pools[i % workers].submit(_cpu_window, wx, wy) for i, (wx, wy) in enumerate(windows)]
+            busy_b = sum(fut.result() for fut in futs)
+            return t_a, time.perf_counter() - t0, busy_a + busy_b
+
+        for _ in range(warmup):
+            run_round()
+        t_a = t_b = busy = 0.0
+        for _ in range(rounds):
+            a, b, c = run_round()
+            t_a, t_b, busy = t_a + a, t_b + b, busy + c
+    finally:
+        for p in pools:
+            p.shutdown()
+    secs_per_view = (t_a + t_b / f) / max(rounds, 1)
+    return {"value": 1.0 / secs_per_view, "unit": "views/s", "cores": workers, "kind": "port",
+            "sample": f"{rounds} timed rounds after {warmup} untimed, {workers} processes; a round = one view's "
+                      f"per-gaussian work on all {s.n} gaussians (activations, projection, SH, binning, backward; "
+                      f"{t_a / max(rounds, 1):.3f} s wall) + the blend fwd+bwd with SSIM of {len(windows)} fixed "
+                      f"{CPU_WINDOW}x{CPU_WINDOW} windows = {f:.4f} of the {cam.width}x{cam.height} view "
+                      f"({t_b / max(rounds, 1):.3f} s wall, scaled by 1/{f:.4f}); C={args.channels}, "
+                      f"oracle/hds_oracle.c, {busy:.1f} s of CPU work in all"}, secs_per_view
 
 
 def cpu_baseline(args):
-    """The cpu_baseline object of the GPU arm's line: three timed rounds of cpu_sample."""
-    return cpu_sample(args, rounds=3, warmup=1)[0]
+    """The cpu_baseline object of the GPU arm's line: cpu_sample with the run's own rounds, as the
+    reference arm uses."""
+    return cpu_sample(args, rounds=max(args.steps, 1), warmup=max(args.warmup, 0))[0]
 
 
 def run_reference(args, rank, world):
     """The reference arm: the CPU oracle (the reference's path restated in C; its own CPU code is Python
-    that cannot travel) on all host cores, W untimed and K timed rounds of cpu_sample."""
+    that cannot travel) on all host cores, W untimed and K timed rounds of cpu_sample.  Under torchrun
+    only rank 0 runs; it reports one view per round at the GPU arm's config."""
     if rank != 0:
         return
-    base, secs_per_round = cpu_sample(args, rounds=max(args.steps, 1), warmup=max(args.warmup, 0))
+    base, secs_per_view = cpu_sample(args, rounds=max(args.steps, 1), warmup=max(args.warmup, 0))
     line = {"metric": METRIC, "value": base["value"], "unit": "views/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1000.0 * secs_per_round, "ms_per_view": 1000.0 / base["value"],
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "impl": "reference",
-            "config": {"workload": "config2 scene, orbit views, bounded CPU sample", "channels": args.channels,
-                       "gaussians": args.gaussians},
+            "warmup": args.warmup, "ms_per_step": 1000.0 * secs_per_view * args.views,
+            "ms_per_view": 1000.0 * secs_per_view,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": DATA, "impl": "reference", "config": bench_config(args, args.gpus),
             "cpu_baseline": base,
             "e2e": {"value": base["value"], "unit": "views/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+SWEEP_CHANNELS = (32, 64, 128, 256, 512)
+DATA = "synthetic (seeded config-1 distribution; the Truck scene is not available)"
+
+
+def bench_config(args, world):
+    """The config object both arms print (the GPU arm and --impl reference)."""
+    return {"workload": "config2 scene (1.18M gaussians), config3 orbit views, 979x546, full fwd+bwd step",
+            "gaussians": args.gaussians, "channels": args.channels, "views_per_gpu_per_step": args.views,
+            "sh_degree": 3, "parallelism": f"dp{world}",
+            "l2": f"inputs larger than L2 (features {args.gaussians * args.channels * 4 / 1e9:.2f} GB)"}
+
+
+def harness_time_ms(fn, before=None, iters=50, warmup=10):
+    """Median device time of fn over `iters` runs after `warmup`, each bracketed by CUDA events, with a
+    pause of 1.5x the last run between runs (bench/harness.py:133-154 of the reference)."""
+    import torch
+
+    for _ in range(warmup):
+        if before:
+            before()
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        if before:
+            before()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        e.synchronize()
+        times.append(s.elapsed_time(e))
+        time.sleep(max(0.002, 1.5 * times[-1] / 1000))
+    return statistics.median(times)
+
+
+def harness_sweep(args, device, timer, peaks):
+    """The config-2 channel sweep in the reference benchmark's scope (bench/harness.py:59-66, 133-177):
+    projection (quaternions normalised by torch, as the harness does) and rasterize with features,
+    colours as a leaf, forward and backward timed separately, each the median of 50 runs after 10
+    warm-ups.  1.18M gaussians of the config-1 distribution, its 979x546 view, features N(0, 1),
+    uniform random gradients of both images.  Per channel count it also reports the feature blend's
+    and the backward's device time per call (CUDA events around each entry point) against their
+    rooflines."""
+    import torch
+    import torch.nn.functional as F
+
+    from hds_b200 import scenes
+    from hds_b200.projection import project_gaussians
+    from hds_b200.rasterizer import rasterize
+
+    s = scenes.config1(0, n=args.gaussians, channels=0)
+    cam = s.cameras[0].to(device)
+    g = torch.Generator().manual_seed(0)
+    base = {"means": s.means, "scales": s.scales, "quats": s.quats, "opacities": s.opacities[:, 0].contiguous(),
+            "colors": torch.rand(s.n, 3, generator=g)}
+    base = {k: v.to(device) for k, v in base.items()}
+    grad_image = torch.rand(cam.height, cam.width, 3, generator=g).to(device)
+    stats = None
+    rows = {}
+    for C in SWEEP_CHANNELS:
+        leaves = {k: v.clone().requires_grad_(True) for k, v in base.items()}
+        leaves["features"] = torch.randn(s.n, C, generator=g).to(device).requires_grad_(True)
+        grad_feat = torch.rand(cam.height, cam.width, C, generator=g).to(device)
+        state = {}
+
+        def forward():
+            m2, d, r, c = project_gaussians(leaves["means"], leaves["scales"], F.normalize(leaves["quats"], dim=-1),
+                                            leaves["opacities"][:, None], cam.world_to_camera, cam.fx, cam.fy, cam.cx,
+                                            cam.cy, cam.width, cam.height)
+            state["out"] = rasterize(m2, d, r, c, leaves["colors"], leaves["opacities"][:, None], cam.width,
+                                     cam.height, features=leaves["features"])
+
+        def backward():
+            torch.autograd.backward(state["out"], [grad_image, grad_feat])
+
+        def reset():
+            for leaf in leaves.values():
+                leaf.grad = None
+            forward()
+
+        timer.events.clear()
+        timer.active = True
+        fwd = harness_time_ms(forward)
+        timer.active = False
+        f_calls, f_counts = timer.totals_ms(), timer.counts()
+        timer.events.clear()
+        timer.active = True
+        bwd = harness_time_ms(backward, before=reset)
+        timer.active = False
+        b_calls, b_counts = timer.totals_ms(), timer.counts()
+        timer.events.clear()
+        if stats is None:
+            with torch.no_grad():
+                m2, d, r, c = project_gaussians(base["means"], base["scales"], F.normalize(base["quats"], dim=-1),
+                                                base["opacities"][:, None], cam.world_to_camera, cam.fx, cam.fy,
+                                                cam.cx, cam.cy, cam.width, cam.height)
+            stats = projected_stats(m2, d, r, c, base["opacities"][:, None], cam, device)
+        # The backward timing's calls include the untimed forwards of reset(); keep its backward calls.
+        calls = {k: v for k, v in f_calls.items()}
+        counts = {k: v for k, v in f_counts.items()}
+        for k in STAGES["backward"] + STAGES["preprocess_backward"]:
+            if k in b_calls:
+                calls[k], counts[k] = b_calls[k], b_counts[k]
+        per_view = {k: 1 for k in calls}
+        roof = rooflines(calls, counts, per_view, stats, C, s.n, peaks)
+        rows[str(C)] = {"fwd_ms": fwd, "bwd_ms": bwd, "fwd_bwd_ms": fwd + bwd,
+                        "feature_forward": {k: roof["feature_forward"][k] for k in ("ms", "achieved", "unit", "frac")}
+                        if "feature_forward" in roof else None,
+                        "backward": {k: roof["backward"][k] for k in ("ms", "achieved", "unit", "frac")}
+                        if "backward" in roof else None}
+        del leaves, grad_feat, state
+        torch.cuda.empty_cache()
+    return {"scope": "projection + rasterize with features, colours as a leaf (bench/harness.py:59-66); median of "
+                     "50 after 10 warm-ups, fwd and bwd separately (harness.py:133-177)",
+            "scene": f"config2: {s.n} gaussians, one {cam.width}x{cam.height} view, features N(0,1)",
+            "tile_stats": stats, "channels": rows}
 
 
 def main():
@@ -491,26 +735,33 @@ def main():
 
     peaks = load_peaks()
     stats = tile_stats(wl, device)
-    kernel_calls = {k: v for k, v in calls.items()}
-    dominant = max(kernel_calls, key=kernel_calls.get)
-    per_launch = kernel_calls[dominant] / max(1, counts[dominant])
-    roof = roofline(dominant, per_launch, stats, args, peaks, n)
+    per_view = {k: 1 for k in calls}
+    stages = rooflines(calls, counts, per_view, stats, args.channels, n, peaks)
+    dominant = max(stages, key=lambda k: stages[k]["ms"])
+    roof = dict(stages[dominant])
+    roof["kernel"] = dominant + " (" + ", ".join(c for c in STAGES[dominant] if c in calls) + ")"
+    roof["traffic"] = None
+    for call in STAGES[dominant]:
+        fit = TRAFFIC_FIT.get((call, args.channels))
+        if fit is not None and call in calls:
+            roof["traffic"] = fit[0] + fit[1] * n
+            roof["traffic_source"] = f"a + b N fitted to two small one-pass captures, {fit[2]}"
     line = {
         "metric": METRIC, "value": value, "unit": "views/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "ms_per_view": ms / (args.steps * args.views),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (feature blend tf32)",
-        "data": "synthetic (seeded config-1 distribution; the Truck scene is not available)",
-        "config": {"workload": "config2 scene (1.18M gaussians), config3 orbit views, 979x546, full fwd+bwd step",
-                   "gaussians": n, "channels": args.channels, "views_per_gpu_per_step": args.views,
-                   "sh_degree": 3, "parallelism": f"dp{world}", "l2": "inputs larger than L2 (features "
-                   f"{n * args.channels * 4 / 1e9:.2f} GB)"},
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 (feature contractions in split bf16: hi*hi + hi*lo + lo*hi, fp32 accumulate)",
+        "data": DATA, "config": bench_config(args, world),
         "roofline": roof,
+        "rooflines": stages,
         "call_ms_per_step": {k: v / args.steps for k, v in sorted(calls.items(), key=lambda kv: -kv[1])},
         "gpu_launches": launches,
         "tile_stats": stats,
         "clocks": clock_info,
         "e2e": e2e,
     }
+    if world == 1 and not args.no_sweep:
+        line["sweep"] = harness_sweep(args, device, timer, peaks)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args)
     print(json.dumps(line), flush=True)

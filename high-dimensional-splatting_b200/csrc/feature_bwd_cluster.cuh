@@ -572,7 +572,7 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
                 const int k = 4 * j + i;
                 const float4 cq = ch.conic[k];
                 const float2 m = ch.mean[k];
-                const PairAlpha pa = pair_alpha_fast(cx, cy, m.x, m.y, cq.x, cq.y, cq.z, cq.w);
+                const PairAlpha pa = pair_alpha(cx, cy, m.x, m.y, cq.x, cq.y, cq.z, cq.w);
                 const float alpha = fminf(MAX_ALPHA, pa.raw);
                 const bool ok = ((hits >> k) & 1u) && inside && ch.pos[k] < last && alpha >= MIN_ALPHA;
                 a[i] = ok ? alpha : 0.0f;

@@ -17,21 +17,9 @@ constexpr int KC = 32;         // list entries per chunk (the N of both MMAs)
 constexpr int PIX = 128;       // pixels per half tile (the TMEM lanes of the dot)
 constexpr int LIST_SLOTS = 6;  // list ring: the list warp runs up to three chunks past the operand stages
 
-// (a, b) -> bf16x2 hi and lo with a in the low half: a = hi.x + lo.x + O(2^-17 a).
-__device__ __forceinline__ void split_bf16(float a, float b, uint32_t& hi, uint32_t& lo) {
-    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-    float2 hf = __bfloat1622float2(h);
-    __nv_bfloat162 l = __floats2bfloat162_rn(__fsub_rn(a, hf.x), __fsub_rn(b, hf.y));
-    hi = *reinterpret_cast<uint32_t*>(&h);
-    lo = *reinterpret_cast<uint32_t*>(&l);
-}
-
-__device__ __forceinline__ void st_shared_v2(uint32_t addr, uint32_t a, uint32_t b) {
-    asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
-}
-__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
-}
+using tc::split_bf16;
+using tc::st_shared_v2;
+using tc::st_shared_v4;
 
 // Pixel p (p < 128, the TMEM lane order) of the 16 x 8 half tile: quadrant p/32 is an 8 x 4 block.
 __device__ __forceinline__ int2 half_tile_pixel(int p) {

@@ -85,8 +85,6 @@ __device__ __forceinline__ bool tile_rect(float u, float v, float a, float b, fl
     return true;
 }
 
-// The per-pair opacity term of every blend: mahalanobis distance of the pixel centre under the
-// conic, G = exp(-m/2), raw alpha = opacity * G (forward.cu:197-208).  Same order as the oracle.
 // Reads and clears the feature backward kernel's device status (render_features_bwd.cu); the
 // copies are queued on `stream`.
 int read_and_clear_backward_status(int* status, cudaStream_t stream);
@@ -97,6 +95,10 @@ __device__ __forceinline__ int nth_set_bit(unsigned mask, int n) {
     return __ffs(mask) - 1;
 }
 
+// The per-pair opacity term of every blend: mahalanobis distance of the pixel centre under the
+// conic, G = exp(-m/2), raw alpha = opacity * G (forward.cu:197-208).  Same order as the oracle.
+// The backward walks use it too, so every pair's alpha -- and which side of the MIN_ALPHA cutoff it
+// falls on -- is bit-identical in the forward, the backward and the oracle.
 struct PairAlpha {
     float dx, dy, G, raw;
 };
@@ -110,22 +112,6 @@ __device__ __forceinline__ PairAlpha pair_alpha(float px, float py, float mx, fl
     float t2 = fmaf(c, r.dy, __fmul_rn(b, r.dx));
     float maha = fmaf(r.dy, t2, __fmul_rn(r.dx, t1));
     r.G = expf_det(__fmul_rn(-0.5f, maha));
-    r.raw = __fmul_rn(opacity, r.G);
-    return r;
-}
-
-// pair_alpha with the hardware exponential (__expf, ~2 ulp) instead of expf_det, for the backward
-// walks: they compare within tolerance, and only a pair exactly on the MIN_ALPHA cutoff can change
-// side.  The forward walks, whose outputs are bit-exact against the CPU oracle, keep pair_alpha.
-__device__ __forceinline__ PairAlpha pair_alpha_fast(float px, float py, float mx, float my, float a, float b,
-                                                     float c, float opacity) {
-    PairAlpha r;
-    r.dx = __fsub_rn(px, mx);
-    r.dy = __fsub_rn(py, my);
-    float t1 = fmaf(b, r.dy, __fmul_rn(a, r.dx));
-    float t2 = fmaf(c, r.dy, __fmul_rn(b, r.dx));
-    float maha = fmaf(r.dy, t2, __fmul_rn(r.dx, t1));
-    r.G = __expf(__fmul_rn(-0.5f, maha));
     r.raw = __fmul_rn(opacity, r.G);
     return r;
 }

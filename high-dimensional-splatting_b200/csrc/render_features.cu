@@ -1,21 +1,28 @@
-// render_features.cu -- C-channel feature blend on tcgen05 TF32 tensor cores.
+// render_features.cu -- C-channel feature blend on tcgen05 tensor cores (split-bf16 contraction).
 //
 // Restates features.cu:116-346 of the reference (render_features + its host wrapper): every pixel
 // blends its tile's sorted list front to back with the same alpha / transmittance walk as the RGB
 // pass, and the feature image is out[p, c] = sum_j w[p, j] f[j, c] with w = alpha * T.
 //
+// Precision.  The contraction runs on kind::f16 tensor cores with every weight and feature split
+// into bf16 halves, x = hi + lo + O(2^-17 x), and each product formed as hi*hi + hi*lo + lo*hi (three
+// MMAs into one fp32 TMEM accumulator; the dropped lo*lo term is O(2^-16) of the product).  Against
+// the FP32 blend the error is ~1e-5 of sum |w f|, inside the 1e-3 absolute feature bound for
+// features of any magnitude (one TF32 rounding of each factor, 2^-11, is not: 1.6e-3 on N(0, 1)
+// features).  The bf16 pair occupies the bytes one TF32 operand would, and a kind::f16 MMA of
+// K = 16 reads what a kind::tf32 MMA of K = 8 reads, so the three products cost 1.5x the operand
+// reads of one TF32 contraction.
+//
 // Blackwell design.  A block owns half a 16x16 tile: 128 pixels, one per TMEM lane.  It runs two
 // warp groups that hand chunks of 32 gaussians to each other through a two-stage ring:
 //   * producer warps 4-7: warp 4 fills a stage with the next list entries whose opacity-aware box
 //     touches the half tile (keeping each one's list position for the contributor count); all four
-//     then gather the entries' feature rows with 4-byte cp.async into the K-major core-matrix
-//     layout of the B operand (8 channel rows x 16 bytes = 4 gaussians), and round them to TF32
-//     (cvt.rna; the tensor core would otherwise truncate);
+//     then gather the entries' feature rows with 16-byte loads, split them and store them as the
+//     MN-major B operand (channel blocks of 8 x 32 entries, 16 bytes per entry);
 //   * pixel warps 0-3: one thread per pixel walks the stage's entries with the oracle's exact FP32
-//     arithmetic (a warp skips entries whose box misses its 8 x 4 pixels) and writes the
-//     TF32-rounded weights as the K-major A operand; then thread 0 issues 4 x C/256
-//     tcgen05.mma (M = 128, N <= 256, K = 8) into the TMEM accumulators and commits them to the
-//     stage's mbarrier.
+//     arithmetic (a warp skips entries whose box misses its 8 x 4 pixels) and writes its split
+//     weights as the K-major A operand; then thread 0 issues 2 x 3 tcgen05.mma (M = 128, N = C,
+//     K = 16) into the TMEM accumulators and commits them to the stage's mbarrier.
 // The producers run a stage ahead, so gathering, walking and the tensor cores overlap.  The
 // accumulators stay in TMEM until the epilogue (tcgen05.ld).  The same walk writes the RGB image,
 // final transmittance and contributor count, bit-identical to the RGB kernel.
@@ -36,30 +43,61 @@ constexpr uint32_t WAIT_LIMIT = 1u << 22;
 constexpr int STAGES = 2;
 constexpr int PIXEL_BAR = 1, PRODUCER_BAR = 2;  // named barriers of the two warp groups
 
+// Operand layouts shared by both forward kernels (bf16, no swizzle; KC = 32 entries per chunk):
+//   A (weights, M = 128 pixels x K = 32 entries), K-major: element (p, k) at
+//     (k / 8) * A_LBO + (p / 8) * 128 + (p % 8) * 16 + (k % 8) * 2, A_LBO = 2048;
+//   B (features, K = 32 entries x N = C channels), MN-major: element (k, n) at
+//     (n / 8) * B_SBO + (k / 8) * 128 + (k % 8) * 16 + (n % 8) * 2, B_SBO = 512,
+// one copy each for the hi and the lo halves.  A K = 16 step starts 2 * A_LBO into A and 256 bytes
+// into B.
+constexpr int KC_ENTRIES = 32;
+constexpr int A_LBO_BF16 = 2048;
+constexpr int A_COPY_BYTES = 128 * KC_ENTRIES * 2;  // one bf16 copy of A: 8 KB
+constexpr int B_SBO_BF16 = KC_ENTRIES * 16;          // 512: between 8-channel blocks of B
+
+// A gather item (k, cb) = channels 8 cb .. 8 cb + 7 of entry k, for item index i of 32 * C / 8:
+// within a warp, lanes take 8 entries x 4 channel blocks, so that the 32 16-byte stores of a warp hit
+// every bank once per wavefront and each entry's 4 lanes read 128 contiguous bytes of its row.
+__device__ __forceinline__ int gather_entry(int i) { return (i & 7) | (((i >> 5) & 3) << 3); }
+__device__ __forceinline__ int gather_block(int i) { return ((i >> 3) & 3) | ((i >> 7) << 2); }
+
+// Splits eight channels and stores them as one 16-byte row of B's hi and lo copies.
+__device__ __forceinline__ void store_split8(uint32_t hi_addr, uint32_t lo_addr, float4 a, float4 b) {
+    uint32_t h0, h1, h2, h3, l0, l1, l2, l3;
+    tc::split_bf16(a.x, a.y, h0, l0);
+    tc::split_bf16(a.z, a.w, h1, l1);
+    tc::split_bf16(b.x, b.y, h2, l2);
+    tc::split_bf16(b.z, b.w, h3, l3);
+    tc::st_shared_v4(hi_addr, h0, h1, h2, h3);
+    tc::st_shared_v4(lo_addr, l0, l1, l2, l3);
+}
+
+// The three MMAs of one K = 16 step of the split-bf16 product: hi*hi + hi*lo + lo*hi.
+__device__ __forceinline__ void mma_split3(uint32_t d, uint64_t a_hi, uint64_t a_lo, uint64_t b_hi, uint64_t b_lo,
+                                          uint32_t idesc, uint32_t accumulate) {
+    tc::mma_bf16(d, a_hi, b_hi, idesc, accumulate);
+    tc::mma_bf16(d, a_hi, b_lo, idesc, 1u);
+    tc::mma_bf16(d, a_lo, b_hi, idesc, 1u);
+}
+
 template <int C>
 struct FwdCfg {
     static constexpr int PIX = 128;
     static constexpr int THREADS = 256;
-    static constexpr int KC = 32;
+    static constexpr int KC = KC_ENTRIES;
     static constexpr int N_MMA = C < 256 ? C : 256;
     static constexpr int N_BLOCKS = C / N_MMA;
     static_assert(N_BLOCKS >= 1 && N_BLOCKS * N_MMA == C, "the MMAs must cover every channel");
     static constexpr int TMEM_COLS = C;
-    static constexpr int A_BYTES = PIX * KC * 4;
-    static constexpr int B_BYTES = KC * C * 4;
-    static constexpr int A_LBO = (PIX / 8) * 128;  // between K-quads: all 16 row groups of 8 rows x 16 B
-    static constexpr int B_LBO = (C / 8) * 128;    // between K-quads: all C/8 groups of 8 channel rows x 16 B
+    static constexpr int A_BYTES = 2 * A_COPY_BYTES;      // hi + lo
+    static constexpr int B_COPY = (C / 8) * B_SBO_BF16;   // one bf16 copy of B
+    static constexpr int B_BYTES = 2 * B_COPY;            // hi + lo
     static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + 1024;
-    // Both operands K-major: tf32 in MN-major layout is only readable with the 128B/32B-atom swizzle.
-    static constexpr uint32_t IDESC = tc::idesc_tf32(128, N_MMA, false, false);
+    static constexpr uint32_t IDESC = tc::idesc_bf16(128, N_MMA, false, true);
+    static constexpr int GATHER_ITEMS = KC * (C / 8);     // (entry, 8-channel block) pairs of a chunk
+    static_assert(GATHER_ITEMS % 128 == 0, "the producer sweeps must tile the chunk");
     static_assert(C == 32 || C == 64 || C == 128 || C == 256 || C == 512, "unsupported channel count");
 };
-
-__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 
 // One stage's list entries (written by producer warp 4, read by everyone).
@@ -209,31 +247,29 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
             const int valid = ch.count;
             if (valid == 0) break;
 
-            // B operand (K-major, no swizzle): element (k, n) at (k/4)*B_LBO + (n/8)*128 + (n%8)*16 + (k%4)*4,
-            // one 16-byte slot = four consecutive gaussians of one channel.  Item i = (quad kq, channel
-            // n = i % C): a warp fills 512 contiguous bytes, and each 4-byte gather of a warp reads 128
-            // contiguous bytes of one feature row.  Unused rows are zeroed.
-            const uint32_t b_stage = b_base + s * Cfg::B_BYTES;
-            for (int i = ptid; i < 8 * C; i += 128) {
-                const int n = i % C, kq = i / C;
-                const uint32_t dst = b_stage + kq * Cfg::B_LBO + (n >> 3) * 128 + (n & 7) * 16;
+            // B operand: each producer thread loads its items' 8-channel pieces (two 16-byte loads
+            // each, all issued before the first store), splits them into bf16 hi + lo and stores one
+            // 16-byte row of each copy.  Entries past the chunk's count are zero.
+            {
+                constexpr int PER = Cfg::GATHER_ITEMS / 128;
+                const uint32_t b_hi = b_base + s * Cfg::B_BYTES, b_lo = b_hi + Cfg::B_COPY;
+                float4 v[PER][2];
 #pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const int k = kq * 4 + e;
-                    if (k < valid)
-                        cp_async4(dst + 4 * e, features + (size_t)ch.id[k] * C + n);
-                    else
-                        asm volatile("st.shared.f32 [%0], %1;" ::"r"(dst + 4 * e), "f"(0.0f) : "memory");
+                for (int u = 0; u < PER; u++) {
+                    const int i = u * 128 + ptid, k = gather_entry(i), cb = gather_block(i);
+                    v[u][0] = v[u][1] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    if (k < valid) {
+                        const float4* row = reinterpret_cast<const float4*>(features + (size_t)ch.id[k] * C) + 2 * cb;
+                        v[u][0] = __ldg(row);
+                        v[u][1] = __ldg(row + 1);
+                    }
                 }
-            }
-            cp_async_commit();
-            cp_async_wait_all();
-            for (int i = ptid; i < 8 * C; i += 128) {
-                const int n = i % C, kq = i / C;
-                float4* p = reinterpret_cast<float4*>(smem + STAGES * Cfg::A_BYTES + s * Cfg::B_BYTES +
-                                                      kq * Cfg::B_LBO + (n >> 3) * 128 + (n & 7) * 16);
-                const float4 v = *p;
-                *p = make_float4(tc::to_tf32(v.x), tc::to_tf32(v.y), tc::to_tf32(v.z), tc::to_tf32(v.w));
+#pragma unroll
+                for (int u = 0; u < PER; u++) {
+                    const int i = u * 128 + ptid, k = gather_entry(i), cb = gather_block(i);
+                    const uint32_t off = cb * B_SBO_BF16 + k * 16;
+                    store_split8(b_hi + off, b_lo + off, v[u][0], v[u][1]);
+                }
             }
             tc::fence_proxy_async();
             tc::mbar_arrive(&s_b_full[s]);
@@ -266,18 +302,18 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
             const int valid = ch.count;
             if (valid == 0) break;
 
-            // A operand (K-major, no swizzle): row m = tid, K-quad qd at qd*A_LBO + (m/8)*128 + (m%8)*16.
-            float* a_row = reinterpret_cast<float*>(smem + s * Cfg::A_BYTES + (tid >> 3) * 128 + (tid & 7) * 16);
+            // A operand: row p = tid; group g of 8 entries at g * A_LBO + (p / 8) * 128 + (p % 8) * 16 in
+            // each of the hi and lo copies.
+            const uint32_t a_row = a_base + s * Cfg::A_BYTES + (tid >> 3) * 128 + (tid & 7) * 16;
             const bool warp_done = __all_sync(FULL_MASK, done);
             const unsigned hits_w = ch.hits[warp];  // entries whose box touches this warp's pixels
 #pragma unroll 1
-            for (int qd = 0; qd < Cfg::KC / 4; qd++) {
-                float w4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            for (int g8 = 0; g8 < Cfg::KC / 8; g8++) {
+                float w8[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
                 if (!warp_done) {
 #pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const int k = qd * 4 + e;
-                        float w = 0.0f;
+                    for (int e = 0; e < 8; e++) {
+                        const int k = g8 * 8 + e;
                         if (((hits_w >> k) & 1u) && !done) {
                             const float2 m = ch.mean[k];
                             const float4 q = ch.conic[k];
@@ -289,7 +325,7 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
                                 if (test < MIN_T) {
                                     done = true;
                                 } else {
-                                    w = alpha * T;
+                                    const float w = alpha * T;
                                     if (rgb) {
                                         ar = fmaf(w, col.x, ar);
                                         ag = fmaf(w, col.y, ag);
@@ -297,13 +333,17 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
                                     }
                                     T = test;
                                     last = ch.pos[k] + 1;
+                                    w8[e] = w;
                                 }
                             }
                         }
-                        w4[e] = tc::to_tf32(w);
                     }
                 }
-                *reinterpret_cast<float4*>(a_row + qd * (Cfg::A_LBO / 4)) = make_float4(w4[0], w4[1], w4[2], w4[3]);
+                uint32_t h[4], l[4];
+#pragma unroll
+                for (int j = 0; j < 4; j++) tc::split_bf16(w8[2 * j], w8[2 * j + 1], h[j], l[j]);
+                tc::st_shared_v4(a_row + g8 * A_LBO_BF16, h[0], h[1], h[2], h[3]);
+                tc::st_shared_v4(a_row + A_COPY_BYTES + g8 * A_LBO_BF16, l[0], l[1], l[2], l[3]);
             }
             tc::fence_proxy_async();
             // Every pixel thread has written its A row; tell the producers when all pixels are done.
@@ -313,16 +353,19 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
                     s_fail = 1;
                 } else {
                     tc::fence_after_sync();
-                    const uint32_t a_stage = a_base + s * Cfg::A_BYTES;
-                    const uint32_t b_stage = b_base + s * Cfg::B_BYTES;
+                    const uint32_t a_hi = a_base + s * Cfg::A_BYTES, a_lo = a_hi + A_COPY_BYTES;
+                    const uint32_t b_hi = b_base + s * Cfg::B_BYTES, b_lo = b_hi + Cfg::B_COPY;
 #pragma unroll
-                    for (int ks = 0; ks < Cfg::KC / 8; ks++) {
+                    for (int ks = 0; ks < Cfg::KC / 16; ks++) {
 #pragma unroll
                         for (int nb = 0; nb < Cfg::N_BLOCKS; nb++) {
-                            uint64_t ad = tc::smem_desc(a_stage + ks * 2 * Cfg::A_LBO, Cfg::A_LBO, 128);
-                            uint64_t bd = tc::smem_desc(b_stage + ks * 2 * Cfg::B_LBO + nb * (Cfg::N_MMA / 8) * 128,
-                                                        Cfg::B_LBO, 128);
-                            tc::mma_tf32(tmem + nb * Cfg::N_MMA, ad, bd, Cfg::IDESC, (c > 0 || ks > 0) ? 1u : 0u);
+                            const uint32_t a_off = ks * 2 * A_LBO_BF16;
+                            const uint32_t b_off = ks * 256 + nb * (Cfg::N_MMA / 8) * B_SBO_BF16;
+                            mma_split3(tmem + nb * Cfg::N_MMA, tc::smem_desc(a_hi + a_off, A_LBO_BF16, 128),
+                                       tc::smem_desc(a_lo + a_off, A_LBO_BF16, 128),
+                                       tc::smem_desc(b_hi + b_off, 128, B_SBO_BF16),
+                                       tc::smem_desc(b_lo + b_off, 128, B_SBO_BF16), Cfg::IDESC,
+                                       (c > 0 || ks > 0) ? 1u : 0u);
                         }
                     }
                     tc::commit(&s_mma_done[s]);
@@ -410,14 +453,15 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
 //     8 x 2 block); thread t < 16 and t + 16 share a pixel and each computes the alphas of half of
 //     every group of eight entries, swaps them (shfl.xor 16), and both run the walk over all eight
 //     with the oracle's exact FP32 operations in list order -- RGB, final T and the contributor count
-//     stay bit-identical -- each writing its four TF32 weights of the K-major A operand;
+//     stay bit-identical -- each writing its four split weights (8 bytes of each of A's hi and lo
+//     copies) of the K-major A operand;
 //   * list warp 8 cuts the tile's list (front to back) into chunks of 32 entries whose box meets the
 //     half tile, software-pipelined over three 32-position batches, into a ring of list slots;
-//   * gather warps 9-12 copy each chunk's feature rows with 16-byte loads, round them to TF32, and
-//     store them as the MN-major B operand in the 128-byte swizzle on 32-byte atoms (in row k of an
-//     atom the four 32-byte chunks are permuted by XOR with k mod 4) -- no transposition;
-//   * MMA warp 13 (one lane) issues 4 x C/256 tcgen05.mma per chunk (M = 128, N = 256, K = 8) into
-//     the TMEM accumulators, releases the list slot, and after the last chunk tells the pixel warps.
+//   * gather warps 9-12 copy each chunk's feature rows with 16-byte loads (16 in flight per thread),
+//     split them into bf16 hi + lo and store them as the MN-major B operand -- no transposition;
+//   * MMA warp 13 (one lane) issues 2 x 3 x C/256 tcgen05.mma per chunk (M = 128, N = 256, K = 16)
+//     into the TMEM accumulators, releases the list slot, and after the last chunk tells the pixel
+//     warps.
 // ----------------------------------------------------------------------------------------------
 namespace ws {
 
@@ -443,17 +487,18 @@ struct Cfg {
     static constexpr int N_MMA = 256;
     static constexpr int N_BLOCKS = C / N_MMA;
     static_assert(N_BLOCKS >= 1 && N_BLOCKS * N_MMA == C, "the MMAs must cover every channel");
-    static constexpr int A_BYTES = 128 * KC * 4;  // K-major: (k/4)*A_LBO + (p/8)*128 + (p%8)*16 + (k%4)*4
-    static constexpr int A_LBO = 2048;
-    static constexpr int B_SBO = (C / 32) * 512;  // between atoms of 4 entries; atoms of 32 channels are 512 B apart
-    static constexpr int B_BYTES = (KC / 4) * B_SBO;
+    static_assert(KC == KC_ENTRIES, "the operand layouts assume 32 entries per chunk");
+    static constexpr int A_BYTES = 2 * A_COPY_BYTES;      // hi + lo (layout above)
+    static constexpr int B_COPY = (C / 8) * B_SBO_BF16;   // one bf16 copy of B (layout above)
+    static constexpr int B_BYTES = 2 * B_COPY;
     static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + 1024;
-    static constexpr uint32_t IDESC = tc::idesc_tf32(128, N_MMA, false, true);
+    static constexpr uint32_t IDESC = tc::idesc_bf16(128, N_MMA, false, true);
     static_assert(C == 256 || C == 512, "the warp-specialised forward is for 256 or 512 channels");
-    // The gather's 8 x GATHER_THREADS item sweeps tile the chunk exactly (and the loop bound guards
-    // any other count as well).
-    static constexpr int GATHER_UNROLL = 16;  // float4 loads in flight per gather thread
-    static_assert((KC * (C / 4)) % (GATHER_UNROLL * GATHER_THREADS) == 0, "gather sweep must tile the chunk");
+    // Gather items (entry, 8-channel block): each is two float4 loads; GATHER_UNROLL items per thread
+    // per sweep keep 2 x GATHER_UNROLL loads in flight, and the sweeps tile the chunk exactly.
+    static constexpr int GATHER_ITEMS = KC * (C / 8);
+    static constexpr int GATHER_UNROLL = 8;
+    static_assert(GATHER_ITEMS % (GATHER_UNROLL * GATHER_THREADS) == 0, "gather sweep must tile the chunk");
 };
 
 // One list slot: chunk entries in list order.
@@ -647,26 +692,27 @@ __global__ void __launch_bounds__(THREADS, 1) feature_forward_ws_kernel(
             // (Only those: the chunk that finished the last pixel is still blended.)
             const bool stopped = tc::group_sync_count<GATHER_BAR>(gtid == 0 && c >= *(volatile int*)&s_zero_from,
                                                                   GATHER_THREADS) != 0;
-            // Item (k, j): entry k's channels 4j .. 4j + 3; a warp reads 512 contiguous bytes of a row.
-            const uint32_t b_stage = b_base + s * K::B_BYTES;
+            // Item i = (entry k, 8-channel block cb) (gather_entry / gather_block); entries past the
+            // chunk's count are stored as zeros.
+            const uint32_t b_hi = b_base + s * K::B_BYTES, b_lo = b_hi + K::B_COPY;
 #pragma unroll 1
-            for (int i0 = 0; i0 < (stopped ? 0 : KC * (C / 4)); i0 += K::GATHER_UNROLL * GATHER_THREADS) {
-                float4 v[K::GATHER_UNROLL];
+            for (int i0 = 0; i0 < (stopped ? 0 : K::GATHER_ITEMS); i0 += K::GATHER_UNROLL * GATHER_THREADS) {
+                float4 v[K::GATHER_UNROLL][2];
 #pragma unroll
                 for (int u = 0; u < K::GATHER_UNROLL; u++) {
-                    const int i = i0 + u * GATHER_THREADS + gtid, k = i / (C / 4), j = i % (C / 4);
-                    v[u] = k < cnt && k < KC
-                               ? __ldg(reinterpret_cast<const float4*>(features + (size_t)ch.id[k] * C) + j)
-                               : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    const int i = i0 + u * GATHER_THREADS + gtid, k = gather_entry(i), cb = gather_block(i);
+                    v[u][0] = v[u][1] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    if (k < cnt) {
+                        const float4* row = reinterpret_cast<const float4*>(features + (size_t)ch.id[k] * C) + 2 * cb;
+                        v[u][0] = __ldg(row);
+                        v[u][1] = __ldg(row + 1);
+                    }
                 }
 #pragma unroll
                 for (int u = 0; u < K::GATHER_UNROLL; u++) {
-                    const int i = i0 + u * GATHER_THREADS + gtid, k = i / (C / 4), j = i % (C / 4);
-                    if (k >= KC) continue;  // past the chunk: no slot of this stage
-                    const uint32_t off = (k >> 2) * K::B_SBO + (j >> 3) * 512 + (k & 3) * 128 +
-                                         ((((j & 7) >> 1) ^ (k & 3)) << 5) + (j & 1) * 16;
-                    st_shared_v4f(b_stage + off, make_float4(tc::to_tf32(v[u].x), tc::to_tf32(v[u].y),
-                                                             tc::to_tf32(v[u].z), tc::to_tf32(v[u].w)));
+                    const int i = i0 + u * GATHER_THREADS + gtid, k = gather_entry(i), cb = gather_block(i);
+                    const uint32_t off = cb * B_SBO_BF16 + k * 16;
+                    store_split8(b_hi + off, b_lo + off, v[u][0], v[u][1]);
                 }
             }
             tc::fence_proxy_async();
@@ -690,19 +736,20 @@ __global__ void __launch_bounds__(THREADS, 1) feature_forward_ws_kernel(
                     break;
                 }
                 tc::fence_after_sync();
-                const uint32_t a_stage = a_base + s * K::A_BYTES, b_stage = b_base + s * K::B_BYTES;
+                const uint32_t a_hi = a_base + s * K::A_BYTES, a_lo = a_hi + A_COPY_BYTES;
+                const uint32_t b_hi = b_base + s * K::B_BYTES, b_lo = b_hi + K::B_COPY;
                 const bool skip = *(volatile int*)&s_skip[s];
 #pragma unroll
-                for (int ks = 0; ks < (skip ? 0 : KC / 8); ks++) {
+                for (int ks = 0; ks < (skip ? 0 : KC / 16); ks++) {
 #pragma unroll
                     for (int nb = 0; nb < K::N_BLOCKS; nb++) {
-                        const uint64_t ad = tc::smem_desc(a_stage + ks * 2 * K::A_LBO, K::A_LBO, 128);
-                        // MN-major, 128-byte swizzle on 32-byte atoms (layout type 1): LBO between
-                        // 32-channel atoms, SBO between 4-entry atoms.
-                        const uint64_t bd = tc::smem_desc(b_stage + ks * 2 * K::B_SBO + nb * (K::N_MMA / 32) * 512, 512,
-                                                          K::B_SBO) |
-                                            (1ull << 61);
-                        tc::mma_tf32(tmem + nb * K::N_MMA, ad, bd, K::IDESC, (issued || ks > 0) ? 1u : 0u);
+                        const uint32_t a_off = ks * 2 * A_LBO_BF16;
+                        const uint32_t b_off = ks * 256 + nb * (K::N_MMA / 8) * B_SBO_BF16;
+                        mma_split3(tmem + nb * K::N_MMA, tc::smem_desc(a_hi + a_off, A_LBO_BF16, 128),
+                                   tc::smem_desc(a_lo + a_off, A_LBO_BF16, 128),
+                                   tc::smem_desc(b_hi + b_off, 128, B_SBO_BF16),
+                                   tc::smem_desc(b_lo + b_off, 128, B_SBO_BF16), K::IDESC,
+                                   (issued || ks > 0) ? 1u : 0u);
                     }
                 }
                 issued = issued || !skip;
@@ -746,9 +793,9 @@ __global__ void __launch_bounds__(THREADS, 1) feature_forward_ws_kernel(
             if (tc::group_sync_count<PIX_BAR>(bad, PIXEL_THREADS) != 0) break;
             const int cnt = ch.count;
             if (cnt == 0) break;
-            // A row of pixel p: K-quad q at q*A_LBO + (p/8)*128 + (p%8)*16; this thread owns quad 2g + part
-            // of group g.
-            const uint32_t a_row = a_base + s * K::A_BYTES + (p >> 3) * 128 + (p & 7) * 16;
+            // A row of pixel p: entry group g of 8 at g * A_LBO + (p / 8) * 128 + (p % 8) * 16 in each of the
+            // hi and lo copies; this thread owns entries 4 part .. 4 part + 3 of each group (8 bytes).
+            const uint32_t a_row = a_base + s * K::A_BYTES + (p >> 3) * 128 + (p & 7) * 16 + part * 8;
             const unsigned hits_w = ch.hits[warp];  // entries whose box touches this warp's pixels
 #pragma unroll 1
             for (int k0 = 0; k0 < (all_done ? 0 : KC); k0 += 8) {
@@ -797,9 +844,11 @@ __global__ void __launch_bounds__(THREADS, 1) feature_forward_ws_kernel(
                         }
                     }
                 }
-                st_shared_v4f(a_row + ((k0 >> 2) + part) * K::A_LBO,
-                              make_float4(tc::to_tf32(w_own[0]), tc::to_tf32(w_own[1]), tc::to_tf32(w_own[2]),
-                                          tc::to_tf32(w_own[3])));
+                uint32_t h0, h1, l0, l1;
+                tc::split_bf16(w_own[0], w_own[1], h0, l0);
+                tc::split_bf16(w_own[2], w_own[3], h1, l1);
+                tc::st_shared_v2(a_row + (k0 >> 3) * A_LBO_BF16, h0, h1);
+                tc::st_shared_v2(a_row + A_COPY_BYTES + (k0 >> 3) * A_LBO_BF16, l0, l1);
             }
             tc::fence_proxy_async();
             // Every pixel thread has written its A quads (none when all were done before the chunk:

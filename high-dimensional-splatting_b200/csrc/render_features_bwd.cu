@@ -506,7 +506,7 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
                     for (int i = 0; i < 4; i++) {
                         const float4 q = ch.conic[kb + i];
                         const float2 m = ch.mean[kb + i];
-                        const PairAlpha pa = pair_alpha_fast(cx, cy, m.x, m.y, q.x, q.y, q.z, q.w);
+                        const PairAlpha pa = pair_alpha(cx, cy, m.x, m.y, q.x, q.y, q.z, q.w);
                         const float alpha = fminf(MAX_ALPHA, pa.raw);
                         const bool ok = hit[i] && inside && ch.pos[kb + i] < last && alpha >= MIN_ALPHA;
                         a_own[i] = ok ? alpha : 0.0f;

@@ -199,7 +199,7 @@ __global__ void __launch_bounds__(TILE_PIXELS) rgb_backward_kernel(
                 float2 m = s_mean[k];
                 float4 q = s_conic[k];
                 float4 col = s_color[k];
-                PairAlpha pa = pair_alpha_fast(cx, cy, m.x, m.y, q.x, q.y, q.z, col.w);
+                PairAlpha pa = pair_alpha(cx, cy, m.x, m.y, q.x, q.y, q.z, col.w);
                 float alpha = fminf(MAX_ALPHA, pa.raw);
                 contributes = alpha >= MIN_ALPHA;
                 if (contributes) {

@@ -1,8 +1,9 @@
 """ctypes binding of libhds_b200.so (include/hds_b200.h).
 
-The library is the only compute path: if it is missing or fails to load, importing this module
-raises instead of falling back to anything else.  Build it with
-``python high-dimensional-splatting_b200/build.py``.
+The library is the only compute path.  It is mapped on the first call of any entry point (so that
+importing the package, e.g. for its scene generators, loads no native code); if it is missing or
+fails to load, that first call raises ImportError instead of falling back to anything else.  Build
+it with ``python high-dimensional-splatting_b200/build.py``.
 """
 from __future__ import annotations
 
@@ -74,7 +75,25 @@ def _load() -> ctypes.CDLL:
     return lib
 
 
-lib = _load()
+class _LazyLib:
+    """Stand-in for the ctypes library that loads it on first attribute access.  Attributes set on
+    it (a wrapper installed by a profiler, say) take precedence over the library's own symbols."""
+
+    def __init__(self):
+        self._cdll = None
+
+    def loaded(self) -> bool:
+        return self._cdll is not None
+
+    def __getattr__(self, name):
+        if name.startswith("__"):
+            raise AttributeError(name)
+        if self._cdll is None:
+            self._cdll = _load()
+        return getattr(self._cdll, name)
+
+
+lib = _LazyLib()
 
 
 def check(rc: int) -> None:

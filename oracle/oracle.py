@@ -53,6 +53,8 @@ def lib():
         L.oracle_logf.argtypes = [c_float]
         L.oracle_tf32_rna.restype = c_float
         L.oracle_tf32_rna.argtypes = [c_float]
+        L.oracle_bf16_rne.restype = c_float
+        L.oracle_bf16_rne.argtypes = [c_float]
         L.oracle_ssim_window.argtypes = [F32P]
         L.oracle_project_forward.argtypes = [c_int, F32P, F32P, F32P, F32P, F32P, c_float, c_float, c_float, c_float,
                                              c_int, c_int, c_float, c_float, c_float, F32P, F32P, F32P, F32P]
@@ -89,6 +91,15 @@ def expf(x: float) -> float:
 
 def logf(x: float) -> float:
     return lib().oracle_logf(float(x))
+
+
+def bf16(x: np.ndarray) -> np.ndarray:
+    """__float2bfloat16_rn applied elementwise (returned as float32)."""
+    u = f32(x).view(np.uint32).copy()
+    finite = (u & 0x7F800000) != 0x7F800000
+    v = u[finite]
+    u[finite] = (v + np.uint32(0x7FFF) + ((v >> np.uint32(16)) & np.uint32(1))) & np.uint32(0xFFFF0000)
+    return u.view(np.float32)
 
 
 def tf32(x: np.ndarray) -> np.ndarray:
@@ -214,9 +225,12 @@ def bin_gaussians(means2D, depths, radii, conics, opacities, width, height):
 
 
 def render_forward(ranges, values, means2D, conics, colors, opacities, width, height, background=None,
-                   features=None, tf32_round=False):
+                   features=None, tf32_round=False, split_bf16=False):
     """forward.cu:141-237 (RGB) and features.cu:116-282 (features) over the binned lists.
 
+    Feature products are exact by default; tf32_round rounds weights and features like
+    cvt.rna.tf32 (the reference's tensor-core blend), split_bf16 forms them as hi*hi + hi*lo + lo*hi
+    of bf16 halves (this library's tensor-core blend).  Sums are in double either way.
     Returns (image [H,W,3] or None, final_T [H,W], n_contrib [H,W] i32, feature_image or None)."""
     p = height * width
     image = np.zeros((height, width, 3), np.float32) if colors is not None else None
@@ -230,7 +244,8 @@ def render_forward(ranges, values, means2D, conics, colors, opacities, width, he
     lib().oracle_render_forward(width, height, np.ascontiguousarray(ranges, np.int32).reshape(-1),
                                 np.ascontiguousarray(values, np.int32).reshape(-1), f32(means2D), f32(conics),
                                 _ptr(colors_a), f32(opacities).reshape(-1), _ptr(bg), ch, _ptr(feats),
-                                int(tf32_round), _ptr(image), _ptr(final_T), _ptr(n_contrib), _ptr(feat))
+                                2 if split_bf16 else int(bool(tf32_round)), _ptr(image), _ptr(final_T),
+                                _ptr(n_contrib), _ptr(feat))
     del p
     return image, final_T, n_contrib, feat
 

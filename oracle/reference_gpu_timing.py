@@ -9,9 +9,10 @@ projection.py:25-93).  This library also runs through its own autograd path, whi
 features in one walk.  Before timing, the outputs must agree within the parity tolerances (as the
 harness gates, harness.py:201-210).
 
-    python tests/reference_gpu_timing.py [--channels 32 64 128 256 512] [--gaussians 1180000]
+    python oracle/reference_gpu_timing.py [--channels 32 64 128 256 512] [--gaussians 1180000]
 
-Prints one JSON object per channel count.
+Prints one JSON object per channel count.  Like everything under oracle/, this is test
+infrastructure: it runs the reference's own build as the GPU bar this library is compared with.
 """
 from __future__ import annotations
 

@@ -34,3 +34,30 @@ def golden():
         return dict(np.load(GOLDEN / name, allow_pickle=False))
 
     return load
+
+
+@pytest.fixture(autouse=True)
+def _name_comparisons(request):
+    """Labels the comparisons a test records with the test's id."""
+    import helpers
+
+    helpers.set_current_test(request.node.nodeid.split("::")[-1])
+    yield
+
+
+def pytest_terminal_summary(terminalreporter):
+    """The worst error of every gradient and absolute comparison of the session, per test."""
+    try:
+        import helpers
+    except ImportError:  # pragma: no cover
+        return
+    if helpers.GRAD_REPORT:
+        terminalreporter.write_sep("-", "gradients: worst |got - want| / max|want| (bound 1e-4)")
+        worst = max(r[1] for r in helpers.GRAD_REPORT)
+        for label, err, size in helpers.GRAD_REPORT:
+            terminalreporter.write_line(f"{err:.3e}  {label} ({size} entries)")
+        terminalreporter.write_line(f"worst over {len(helpers.GRAD_REPORT)} gradient comparisons: {worst:.3e}")
+    if helpers.ABS_REPORT:
+        terminalreporter.write_sep("-", "absolute comparisons: worst |got - want| (bound)")
+        for label, err, atol in helpers.ABS_REPORT:
+            terminalreporter.write_line(f"{err:.3e}  (bound {atol:g})  {label}")
