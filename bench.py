@@ -156,7 +156,7 @@ class CallTimer:
 def make_workload(args, device, rank, world):
     import torch
 
-    from hds_b200 import parallel, scenes
+    from hds_b200 import optim, parallel, scenes
 
     scene = scenes.config1(0, n=args.gaussians, channels=args.channels)
     cams = scenes.orbit(64)
@@ -176,7 +176,11 @@ def make_workload(args, device, rank, world):
            "features": scene.features}
     leaves = {k: v.to(device).contiguous().requires_grad_(True) for k, v in raw.items()}
     bucket = parallel.GradBucket(list(leaves.values()))
-    return {"bucket": bucket, "scene": scene, "cams": cams, "views": views, "gt_host": gt_host, "pose_host": pose_host,
+    # The step ends with the training loop's optimizer step (main.py:194): one fused Adam kernel over
+    # every parameter, at the reference's learning rates (the means' scaled by a scene extent of 5).
+    lrs = [optim.REFERENCE_LRS[k] * (5.0 if k == "means" else 1.0) for k in leaves]
+    opt = optim.FlatAdam(list(leaves.values()), lrs, eps=1e-15, bucket=bucket)
+    return {"bucket": bucket, "optimizer": opt, "scene": scene, "cams": cams, "views": views, "gt_host": gt_host, "pose_host": pose_host,
             "gt_dev": [g.to(device) for g in gt_host], "pose_dev": [p.to(device) for p in pose_host],
             "feat_grad": feat_grad, "leaves": leaves, "bg": torch.zeros(3, device=device)}
 
@@ -223,6 +227,7 @@ def run_step(wl, dist, e2e: bool):
         losses.append(render_view(wl, i, pose, gt))
     if dist is not None:
         wl["bucket"].all_reduce()  # one NCCL all-reduce of every per-gaussian gradient
+    wl["optimizer"].step()
     loss = torch.stack(losses).sum()
     if e2e:
         return loss.item()  # device -> host read of the step's result
@@ -291,6 +296,7 @@ STAGES = {
     "preprocess_backward": ("hds_project_backward_raw", "hds_eval_sh_backward_view"),
     "ssim_forward": ("hds_ssim_forward",),
     "ssim_backward": ("hds_ssim_backward",),
+    "optimizer": ("hds_adam_step",),  # once per step, not per view
 }
 
 
@@ -313,12 +319,15 @@ def stage_model(stage, st, C, n, rgb_terms=True):
                                             "B/gaussian + 624 B per visible gaussian (SH read, gradient added)")
     if stage in ("ssim_forward", "ssim_backward"):
         return "hbm", 72 * P, "72 B per pixel (3 channels x 4 B x 6 maps)"
+    if stage == "optimizer":
+        return "hbm", 28 * (59 + C) * n, "28 B per parameter (param, 2 moments, grad in; param, 2 moments out)"
     raise KeyError(stage)
 
 
 def rooflines(call_ms, counts, launches_per_view, st, C, n, peaks):
-    """Per stage of one view: device time (CUDA events on the launch stream, summed over the stage's
-    calls, per view), algorithmic bytes or flops, and the fraction of the measured peak."""
+    """Per stage of one view (the optimizer: of one step): device time (CUDA events on the launch
+    stream, per launch of each of the stage's calls, summed), algorithmic bytes or flops, and the
+    fraction of the measured peak."""
     out = {}
     for stage, calls in STAGES.items():
         ms = sum(call_ms.get(c, 0.0) / max(1, counts.get(c, 0)) * launches_per_view.get(c, 0) for c in calls)
@@ -342,6 +351,7 @@ def rooflines(call_ms, counts, launches_per_view, st, C, n, peaks):
 CPU_WINDOW = 64  # side of the image windows the CPU oracle blends as its bounded sample
 CPU_WINDOWS = 16  # fixed windows of view 0, spread over the image (the same every round and in both legs)
 CPU_MAX_WORKERS = 64  # worker processes at most (each holds a copy of the scene geometry)
+CPU_ADAM_SAMPLE = 1 << 22  # elements of the per-worker Adam sample
 _cpu_state = None  # per worker process: scene slice, full-view projection, window subsets, feature table
 
 
@@ -386,7 +396,8 @@ def _cpu_worker_init(raw, sh, camera, channels, workers, rank):
         subsets[(wx, wy)] = np.nonzero(keep)[0]
     table = np.random.default_rng(0).random((4096, channels), dtype=np.float32)
     gt = np.random.default_rng(1).random((CPU_WINDOW, CPU_WINDOW, 3), dtype=np.float32)
-    _cpu_state = {"oracle": oracle, "slice": (lo, hi), "raw": raw, "sh": sh, "camera": camera,
+    adam = [np.random.default_rng(2).standard_normal(CPU_ADAM_SAMPLE).astype(np.float32) for _ in range(4)]
+    _cpu_state = {"oracle": oracle, "slice": (lo, hi), "raw": raw, "sh": sh, "camera": camera, "adam": adam,
                   "proj": (m2, dep, rad, con, opac), "subsets": subsets, "table": table, "gt": gt,
                   "channels": channels}
 
@@ -417,6 +428,18 @@ def _cpu_slice(_):
     _, gs, gq = oracle.project_backward(g2, gc, means, scales, unit, pose, fx, fy, cx, cy, width, height)
     oracle.activate_backward(log_scales, quats, logits, gs, gq, np.full(opac.shape, 1e-3, np.float32))
     return time.perf_counter() - t0
+
+
+def _cpu_adam(_):
+    """The optimizer step's share of this worker's slice: one oracle Adam step over a fixed
+    CPU_ADAM_SAMPLE-element buffer, scaled to the slice's (59 + C) parameters per gaussian.  Returns
+    seconds."""
+    st = _cpu_state
+    p, m, v, g = st["adam"]
+    lo, hi = st["slice"]
+    t0 = time.perf_counter()
+    st["oracle"].adam(p, m, v, g, 1, 1e-3, 0.9, 0.999, 1e-15)
+    return (time.perf_counter() - t0) * (hi - lo) * (59 + st["channels"]) / CPU_ADAM_SAMPLE
 
 
 def _cpu_window(wx, wy):
@@ -453,8 +476,10 @@ def cpu_sample(args, rounds: int, warmup: int):
          projection, SH, binning, and their backward passes) -- a whole view's worth;
       B. per-pixel work: the CPU_WINDOWS fixed 64 x 64 windows of the view (a fraction f of its
          pixels) are blended forward and backward with SSIM, one task per window.
-    A view then costs T_A + T_B / f seconds of wall time on these cores.  Untimed warm-up rounds,
-    then timed rounds, all on the same windows."""
+    plus the optimizer step (one Adam pass over all parameters per step of args.views views, timed
+    on a fixed sample per worker and scaled to its slice).  A view then costs
+    T_A + T_adam / views + T_B / f seconds of wall time on these cores.  Untimed warm-up rounds, then
+    timed rounds, all on the same windows."""
     import concurrent.futures
     import multiprocessing
 
@@ -490,25 +515,33 @@ def cpu_sample(args, rounds: int, warmup: int):
             t0 = time.perf_counter()
             busy_a = sum(fut.result() for fut in [p.submit(_cpu_slice, 0) for p in pools])
             t_a = time.perf_counter() - t0
+            # The slowest worker's scaled Adam time stands for the parallel optimizer step.
+            adam = [fut.result() for fut in [p.submit(_cpu_adam, 0) for p in pools]]
             t0 = time.perf_counter()
             futs = [pools[i % workers].submit(_cpu_window, wx, wy) for i, (wx, wy) in enumerate(windows)]
             busy_b = sum(fut.result() for fut in futs)
-            return t_a, time.perf_counter() - t0, busy_a + busy_b
+            return t_a, max(adam), time.perf_counter() - t0, busy_a + sum(adam) + busy_b
 
+        # Start every worker (its set-up runs in the initializer) before anything is timed.
+        for fut in [p.submit(time.perf_counter) for p in pools]:
+            fut.result()
         for _ in range(warmup):
             run_round()
-        t_a = t_b = busy = 0.0
+        t_a = t_o = t_b = busy = 0.0
         for _ in range(rounds):
-            a, b, c = run_round()
-            t_a, t_b, busy = t_a + a, t_b + b, busy + c
+            a, o, b, c = run_round()
+            t_a, t_o, t_b, busy = t_a + a, t_o + o, t_b + b, busy + c
     finally:
         for p in pools:
             p.shutdown()
-    secs_per_view = (t_a + t_b / f) / max(rounds, 1)
+    # The optimizer steps once per step of args.views views.
+    secs_per_view = (t_a + t_o / args.views + t_b / f) / max(rounds, 1)
     return {"value": 1.0 / secs_per_view, "unit": "views/s", "cores": workers, "kind": "port",
             "sample": f"{rounds} timed rounds after {warmup} untimed, {workers} processes; a round = one view's "
                       f"per-gaussian work on all {s.n} gaussians (activations, projection, SH, binning, backward; "
-                      f"{t_a / max(rounds, 1):.3f} s wall) + the blend fwd+bwd with SSIM of {len(windows)} fixed "
+                      f"{t_a / max(rounds, 1):.3f} s wall) + one Adam step over all (59 + C) parameters per gaussian "
+                      f"per {args.views} views ({t_o / max(rounds, 1):.3f} s wall per step, from a "
+                      f"{CPU_ADAM_SAMPLE}-element sample per worker) + the blend fwd+bwd with SSIM of {len(windows)} fixed "
                       f"{CPU_WINDOW}x{CPU_WINDOW} windows = {f:.4f} of the {cam.width}x{cam.height} view "
                       f"({t_b / max(rounds, 1):.3f} s wall, scaled by 1/{f:.4f}); C={args.channels}, "
                       f"oracle/hds_oracle.c, {busy:.1f} s of CPU work in all"}, secs_per_view

@@ -47,6 +47,8 @@ SIGNATURES = {
     "hds_render_backward_fused": [c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, c_int, S],
     "hds_ssim_forward": [c_int, c_int, P, P, P, P, P, P, S],
     "hds_ssim_backward": [c_int, c_int, P, P, P, P, P, P, P, S],
+    "hds_adam_step": [c_int64, P, P, P, P, c_int, ctypes.POINTER(c_int64), ctypes.POINTER(c_float), c_float, c_float,
+                      c_float, c_float, c_float, c_float, S],
     "hds_device_status": [ctypes.POINTER(c_int), S],
     "hds_rasterize_bin_noalloc": [c_int, P, P, P, P, P, P, c_int, c_int, P, P, P, c_int64, P,
                                   ctypes.POINTER(c_int64), S],

@@ -1,0 +1,97 @@
+"""The optimizer step of the reference's training loop (gaussian_splatting/main.py:194,
+torch.optim.Adam(fused=True, eps=1e-15) over one parameter group per tensor) as one kernel.
+
+FlatAdam moves the storage of every parameter tensor into one flat fp32 buffer (the tensors stay
+the same leaf objects, now views of it), keeps both Adam moments as flat buffers of the same
+length, and reads the gradients from the flat GradBucket the backward passes accumulate into.  A
+step is then a single memory-bound pass over all of them (hds_adam_step): 28 bytes per element.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from .native import check, lib, ptr, stream_of
+from .parallel import GradBucket
+
+# One learning rate per group, as the reference's GaussianModel.get_optimizer_params
+# (utils/gaussian.py:123-139) and TrainingParams (config.py) set them; the means' rate is scaled by the
+# scene extent.  The reference trains no feature table; it steps here at the SH DC rate.
+REFERENCE_LRS = {"means": 0.00016, "log_scales": 0.005, "quats": 0.001, "opacity_logits": 0.025,
+                 "sh_dc": 0.0025, "sh_rest": 0.0025 / 20, "features": 0.0025}
+MAX_SEGMENTS = 16
+
+
+def adam_step(params: torch.Tensor, exp_avg: torch.Tensor, exp_avg_sq: torch.Tensor, grads: torch.Tensor,
+              segment_ends, segment_lrs, step: int, betas=(0.9, 0.999), eps: float = 1e-15) -> None:
+    """One Adam step over flat [n] fp32 CUDA buffers (updated in place); segment s of the buffers,
+    [segment_ends[s-1], segment_ends[s]), steps with learning rate segment_lrs[s]."""
+    for t, name in ((params, "params"), (exp_avg, "exp_avg"), (exp_avg_sq, "exp_avg_sq"), (grads, "grads")):
+        if not (t.is_cuda and t.dtype == torch.float32 and t.is_contiguous() and t.dim() == 1):
+            raise RuntimeError(f"{name} must be a contiguous 1-D float32 CUDA tensor")
+        if t.numel() != params.numel():
+            raise RuntimeError(f"{name} has {t.numel()} elements, params {params.numel()}")
+    k = len(segment_ends)
+    if k != len(segment_lrs):
+        raise RuntimeError("one learning rate per segment")
+    ends = (ctypes.c_int64 * k)(*[int(e) for e in segment_ends])
+    lrs = (ctypes.c_float * k)(*[float(x) for x in segment_lrs])
+    b1, b2 = betas
+    check(lib.hds_adam_step(params.numel(), ptr(params), ptr(exp_avg), ptr(exp_avg_sq), ptr(grads), k, ends, lrs,
+                            float(step), float(b1), float(b2), float(np.float32(1.0 - b1)),
+                            float(np.float32(1.0 - b2)), float(eps), stream_of(params.device)))
+
+
+class FlatAdam:
+    """Adam over a list of leaf parameters, with one learning rate per parameter (group).
+
+    On construction every parameter's data moves into one flat buffer (`self.flat`, in list order)
+    and, unless a bucket over the same parameters is given, a GradBucket is made for their gradients.
+    step() runs one kernel over all parameters; lrs can change between steps (set_lr)."""
+
+    def __init__(self, params: list[torch.Tensor], lrs: list[float], betas=(0.9, 0.999), eps: float = 1e-15,
+                 bucket: GradBucket | None = None):
+        if not params or len(params) != len(lrs):
+            raise ValueError("one learning rate per parameter")
+        if len(params) > MAX_SEGMENTS:
+            raise ValueError(f"at most {MAX_SEGMENTS} parameters")
+        dev = params[0].device
+        for p in params:
+            if not (p.is_leaf and p.dtype == torch.float32 and p.device == dev):
+                raise ValueError("parameters must be float32 leaves on one device")
+        self.params = params
+        self.lrs = [float(x) for x in lrs]
+        self.betas = betas
+        self.eps = eps
+        with torch.no_grad():
+            self.flat = torch.cat([p.detach().reshape(-1) for p in params]).contiguous()
+        ends, off = [], 0
+        for p in params:
+            n = p.numel()
+            p.data = self.flat[off:off + n].view_as(p)
+            off += n
+            ends.append(off)
+        self.segment_ends = ends
+        self.exp_avg = torch.zeros_like(self.flat)
+        self.exp_avg_sq = torch.zeros_like(self.flat)
+        if bucket is None:
+            bucket = GradBucket(params)
+        elif bucket.flat.numel() != self.flat.numel() or any(a is not b for a, b in zip(bucket.params, params)):
+            raise ValueError("the bucket must cover the same parameters in the same order")
+        self.bucket = bucket
+        self.step_count = 0
+
+    def set_lr(self, index: int, lr: float) -> None:
+        self.lrs[index] = float(lr)
+
+    def zero_grad(self) -> None:
+        self.bucket.zero()
+
+    @torch.no_grad()
+    def step(self) -> None:
+        self.bucket.ready()
+        self.step_count += 1
+        adam_step(self.flat, self.exp_avg, self.exp_avg_sq, self.bucket.flat, self.segment_ends, self.lrs,
+                  self.step_count, self.betas, self.eps)

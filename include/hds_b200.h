@@ -241,6 +241,23 @@ int hds_ssim_backward(int height, int width, const float* grad_mean, const float
                       const float* d_mu, const float* d_aa, const float* d_ab, float* grad_rendered,
                       hds_stream_t stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * Optimizer step.  Replaces optimizer.step() of the reference's training loop (main.py:194:
+ * torch.optim.Adam(fused=True, eps=1e-15), one parameter group per tensor, built by
+ * utils/gaussian.py:123-139) with ONE kernel over flat buffers: params, exp_avg, exp_avg_sq and grads
+ * each hold every parameter tensor back to back ([n] fp32).  Segment s covers
+ * [segment_ends[s-1], segment_ends[s]) and steps with learning rate segment_lrs[s] (both host arrays,
+ * at most HDS_ADAM_MAX_SEGMENTS; the last end must be n).  step counts from 1.  The element update is
+ * the reference's Adam form (sh.cu:90-102): m += (1 - b1) (g - m); v = b2 v + (1 - b2) g g;
+ * p -= lr / (1 - b1^step) * m / (sqrt(v) / sqrt(1 - b2^step) + eps), with one_minus_beta1/2 given by
+ * the caller.  params, exp_avg and exp_avg_sq are updated in place.  16-byte aligned buffers move as
+ * float4s; others element by element.
+ * ------------------------------------------------------------------------------------------- */
+#define HDS_ADAM_MAX_SEGMENTS 16
+int hds_adam_step(int64_t n, float* params, float* exp_avg, float* exp_avg_sq, const float* grads, int segments,
+                  const int64_t* segment_ends, const float* segment_lrs, float step, float beta1, float beta2,
+                  float one_minus_beta1, float one_minus_beta2, float eps, hds_stream_t stream);
+
 /* Reads and clears the device-side failure word that kernels with bounded waits set (0 = none).
  * Synchronises `stream`. */
 int hds_device_status(int* status, hds_stream_t stream);

@@ -87,3 +87,25 @@ def test_new_entry_points_reject_bad_arguments_on_the_host():
     # Zero gaussians is a valid empty call.
     assert lib.hds_project_forward_raw(0, None, None, None, None, None, 1.0, 1.0, 0.0, 0.0, 16, 16, 0.2, 0.3, 1.3,
                                        None, None, None, None, None, None) == 0
+
+
+def test_adam_step_rejects_bad_tables_on_the_host():
+    """hds_adam_step checks its segment table before any device work (no GPU needed); an empty
+    buffer with a valid table is a no-op."""
+    from hds_b200 import native
+
+    lib = native.lib
+    ends = (ctypes.c_int64 * 2)(5, 10)
+    lrs = (ctypes.c_float * 2)(0.1, 0.2)
+    args = (0.9, 0.999, 0.1, 0.001, 1e-15, None)
+    assert lib.hds_adam_step(10, None, None, None, None, 0, ends, lrs, 1.0, *args) == 1
+    assert b"segments" in lib.hds_last_error()
+    assert lib.hds_adam_step(10, None, None, None, None, 17, ends, lrs, 1.0, *args) == 1
+    assert lib.hds_adam_step(12, None, None, None, None, 2, ends, lrs, 1.0, *args) == 1
+    assert b"not at n" in lib.hds_last_error()
+    assert lib.hds_adam_step(10, None, None, None, None, 2, ends, lrs, 0.0, *args) == 1
+    assert b"count from 1" in lib.hds_last_error()
+    back = (ctypes.c_int64 * 2)(6, 5)
+    assert lib.hds_adam_step(5, None, None, None, None, 2, back, lrs, 1.0, *args) == 1
+    zero = (ctypes.c_int64 * 1)(0)
+    assert lib.hds_adam_step(0, None, None, None, None, 1, zero, lrs, 1.0, *args) == 0
