@@ -157,7 +157,7 @@ int exclusive_scan(const T* in, T* out, int64_t n, T* block_sums, T* total_out, 
 __global__ void __launch_bounds__(256) prepare_kernel(int n, const float2* __restrict__ means2D, const float* __restrict__ depths,
                                                       const float* __restrict__ radii, const float* __restrict__ conics,
                                                       const float* __restrict__ colors, const float* __restrict__ opacities,
-                                                      int tiles_x, int tiles_y, float4* __restrict__ conic4,
+                                                      int tiles_x, int row0, int tiles_y, float4* __restrict__ conic4,
                                                       float4* __restrict__ color_opacity, int4* __restrict__ rect,
                                                       int64_t* __restrict__ touched) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -170,7 +170,7 @@ __global__ void __launch_bounds__(256) prepare_kernel(int n, const float2* __res
     int count = 0;
     float2 m = means2D[i];
     // Written as radius > 0 so a NaN radius is culled too (forward.cu:31-36).
-    if (radii[i] > 0.0f && tile_rect(m.x, m.y, a, b, c, o, tiles_x, tiles_y, x0, y0, x1, y1))
+    if (radii[i] > 0.0f && tile_rect(m.x, m.y, a, b, c, o, tiles_x, row0, tiles_y, x0, y0, x1, y1))
         count = (x1 - x0 + 1) * (y1 - y0 + 1);
     rect[i] = make_int4(x0, y0, x1 - x0 + 1, (int)__float_as_uint(depths[i]));
     touched[i] = count;
@@ -412,11 +412,13 @@ extern "C" size_t hds_rasterize_prepare_scratch_bytes(int n) { return PrepareLay
 
 extern "C" int hds_rasterize_prepare(int n, const float* means2D, const float* depths, const float* radii,
                                      const float* conics, const float* colors, const float* opacities, int width,
-                                     int height, float* conic4, float* color_opacity, void* scratch,
+                                     int height, int origin_y, float* conic4, float* color_opacity, void* scratch,
                                      size_t scratch_bytes, int64_t* num_duplicates, hds_stream_t stream) {
     clear_error();
     HDS_REQUIRE(n >= 0 && width > 0 && height > 0 && num_duplicates, HDS_ERR_INVALID,
                 "rasterize: bad arguments (n=%d, %dx%d)", n, width, height);
+    HDS_REQUIRE(origin_y >= 0 && origin_y % TILE == 0, HDS_ERR_INVALID,
+                "rasterize: origin_y %d must be a non-negative multiple of 16", origin_y);
     PrepareLayout L(n);
     HDS_REQUIRE(scratch && scratch_bytes >= L.bytes, HDS_ERR_SCRATCH, "rasterize: prepare scratch needs %zu bytes",
                 L.bytes);
@@ -432,7 +434,8 @@ extern "C" int hds_rasterize_prepare(int n, const float* means2D, const float* d
     auto* total = reinterpret_cast<int64_t*>(s + L.total);
     int tx = tiles_for(width), ty = tiles_for(height);
     prepare_kernel<<<(n + 255) / 256, 256, 0, stream>>>(n, reinterpret_cast<const float2*>(means2D), depths, radii, conics,
-                                                        colors, opacities, tx, ty, reinterpret_cast<float4*>(conic4),
+                                                        colors, opacities, tx, origin_y / TILE, ty,
+                                                        reinterpret_cast<float4*>(conic4),
                                                         reinterpret_cast<float4*>(color_opacity), rect, touched);
     HDS_CHECK_LAUNCH("prepare_kernel");
     if (int rc = reduce_total<int64_t>(touched, n, block_sums, total, stream)) return rc;

@@ -69,7 +69,7 @@ extern "C" int hds_rasterize_bin_noalloc(int n, const float* means2D, const floa
     char* scratch = static_cast<char*>(base);
 
     // Step 1 (pack, count, scan, host read of the pair count) into the front of the array.
-    if (int rc = hds_rasterize_prepare(n, means2D, depths, radii, conics, colors, opacities, width, height, conic4,
+    if (int rc = hds_rasterize_prepare(n, means2D, depths, radii, conics, colors, opacities, width, height, 0, conic4,
                                        color_opacity, scratch, prep, num_duplicates, stream))
         return rc;
     const int64_t dups = *num_duplicates;

@@ -98,7 +98,7 @@ __device__ __forceinline__ float4 ld_shared_f4(uint32_t addr) {
 
 template <int CK, bool RGB>
 __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) feature_backward_cluster_kernel(
-    int C, int width, int height, int tiles_x, int helper_every, const int2* __restrict__ ranges,
+    int C, int width, int height, int tiles_x, int origin_y, int helper_every, const int2* __restrict__ ranges,
     const int32_t* __restrict__ values,
     const float2* __restrict__ means2D, const float4* __restrict__ conic4, const float4* __restrict__ color_opacity,
     const float* __restrict__ features, const float* __restrict__ final_T_in, const int32_t* __restrict__ n_contrib,
@@ -163,13 +163,13 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
         // ------------------------------------------------------------------ list warp 8
         // Every block of the cluster cuts the same chunks (same half tile, same inputs); the hit
         // mask is its own quadrant's (an 8 x 4 block).
-        list_producer<RGB>(lane, x0, y0, width, height, range, values, means2D, conic4, color_opacity, n_contrib,
+        list_producer<RGB>(lane, x0, y0, origin_y, width, height, range, values, means2D, conic4, color_opacity, n_contrib,
                            s_list, s_list_full, s_list_free, &s_fail, [&](BwdChunk& ch, int filled) {
                                const bool valid = lane < filled;
                                const float2 m = valid ? ch.mean[lane] : make_float2(0.0f, 0.0f);
                                const float2 e = valid ? ch.ext[lane] : make_float2(-1e30f, -1e30f);
                                const float bx0 = (float)(x0 + (rank & 1) * 8) + 0.5f;
-                               const float by0 = (float)(y0 + (rank >> 1) * 4) + 0.5f;
+                               const float by0 = (float)(y0 + origin_y + (rank >> 1) * 4) + 0.5f;
                                const unsigned mask = __ballot_sync(
                                    FULL_MASK, valid && box_hits(m, e, bx0, bx0 + 7.0f, by0, by0 + 3.0f));
                                if (lane == 0) ch.hits[0] = mask;
@@ -274,7 +274,7 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
                     const bool kv = k < ecnt;
                     const float2 m = kv ? ce.mean[k] : make_float2(0.0f, 0.0f);
                     const float bx = (float)(x0 + (rank & 1) * 8) + 0.5f;
-                    const float dy = __fsub_rn((float)(y0 + (rank >> 1) * 4 + g) + 0.5f, m.y);
+                    const float dy = __fsub_rn((float)(y0 + origin_y + (rank >> 1) * 4 + g) + 0.5f, m.y);
                     const uint32_t ub = ubuf(s) + g * 8 * 128 + (((k >> 2) ^ (g << 1)) << 4) + (k & 3) * 4;
                     float m0 = 0.0f, mx = 0.0f, mxx = 0.0f;
 #pragma unroll
@@ -473,7 +473,7 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
         const int2 lp = half_tile_pixel(p);
         const int px = x0 + lp.x, py = y0 + lp.y;
         const bool inside = px < width && py < height;
-        const float cx = (float)px + 0.5f, cy = (float)py + 0.5f;
+        const float cx = (float)px + 0.5f, cy = (float)(py + origin_y) + 0.5f;
         const size_t pix = (size_t)py * width + px;
         float T = inside ? final_T_in[pix] : 0.0f;
         const float fT = T;  // final transmittance: the background's weight
@@ -677,7 +677,7 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
 }
 
 template <int CK>
-int launch_backward_cluster(int D, int width, int height, const int32_t* tile_ranges, const int32_t* values,
+int launch_backward_cluster(int D, int width, int height, int origin_y, const int32_t* tile_ranges, const int32_t* values,
                             const float* means2D, const float* conic4, const float* color_opacity,
                             const float* features, const float* final_T, const int32_t* n_contrib,
                             const float* grad_output, float* grad_features, float* grad_means2D, float* grad_conics,
@@ -691,7 +691,7 @@ int launch_backward_cluster(int D, int width, int height, const int32_t* tile_ra
     const int halves = 2 * tx * ty;
     const int clusters = halves - (helper_every > 1 ? halves / helper_every : 0);
     kernel<<<clusters * CLUSTER, THREADS, K::SMEM, stream>>>(
-        D, width, height, tx, helper_every, reinterpret_cast<const int2*>(tile_ranges), values,
+        D, width, height, tx, origin_y, helper_every, reinterpret_cast<const int2*>(tile_ranges), values,
         reinterpret_cast<const float2*>(means2D), reinterpret_cast<const float4*>(conic4),
         reinterpret_cast<const float4*>(color_opacity), features, final_T, n_contrib, grad_output, grad_means2D,
         grad_conics, grad_features, grad_opacities, grad_image, background, grad_colors);

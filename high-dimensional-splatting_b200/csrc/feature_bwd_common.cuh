@@ -43,7 +43,7 @@ struct BwdChunk {
 // chunk.  mark_hits(ch, filled) runs on the whole warp once a chunk is filled and records the
 // per-group hit masks.  A slot is refilled only after s_list_free[slot] completes.
 template <bool RGB, class MarkHits>
-__device__ __forceinline__ void list_producer(int lane, int x0, int y0, int width, int height, int2 range,
+__device__ __forceinline__ void list_producer(int lane, int x0, int y0, int origin_y, int width, int height, int2 range,
                                               const int32_t* __restrict__ values,
                                               const float2* __restrict__ means2D,
                                               const float4* __restrict__ conic4,
@@ -65,7 +65,7 @@ __device__ __forceinline__ void list_producer(int lane, int x0, int y0, int widt
         if (px < width && py < height) m = max(m, n_contrib[(size_t)py * width + px]);
     }
     int top = min(range.y - range.x, __reduce_max_sync(FULL_MASK, m));
-    const float hx0 = (float)x0 + 0.5f, hx1 = hx0 + 15.0f, hy0 = (float)y0 + 0.5f, hy1 = hy0 + 7.0f;
+    const float hx0 = (float)x0 + 0.5f, hx1 = hx0 + 15.0f, hy0 = (float)(y0 + origin_y) + 0.5f, hy1 = hy0 + 7.0f;
     auto fetch_id = [&](int t) { return t - 1 - lane >= 0 ? values[range.x + t - 1 - lane] : -1; };
     // Batch A: ids only.  Batch B: ids and gathered geometry.  Batch C: geometry and hits.
     int top_a = top, id_a = fetch_id(top);

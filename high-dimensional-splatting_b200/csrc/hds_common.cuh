@@ -68,9 +68,12 @@ __device__ __forceinline__ float logf_det(float y) {
 
 // common.cuh:49-65 of the reference (alpha_extent + tile_rect): the opacity-aware ellipse box,
 // as an inclusive tile rectangle.  Clamped in float before the int conversion so NaN or huge
-// coordinates are rejected.  Identical to oracle_tile_rect.
+// coordinates are rejected.  Identical to oracle_tile_rect.  The grid is tile rows
+// [row0, row0 + tiles_y) of the full image (row0 = 0: the whole image); (u, v) are full-image pixel
+// coordinates and the returned rows count from row0, so a band of rows gets exactly the tiles the
+// full image's rectangle has there.
 __device__ __forceinline__ bool tile_rect(float u, float v, float a, float b, float c, float opacity, int tiles_x,
-                                          int tiles_y, int& x0, int& y0, int& x1, int& y1) {
+                                          int row0, int tiles_y, int& x0, int& y0, int& x1, int& y1) {
     if (!(opacity > MIN_ALPHA)) return false;
     float k = __fsqrt_rn(__fmul_rn(2.0f, logf_det(__fdiv_rn(opacity, MIN_ALPHA))));
     float det = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, b));
@@ -79,9 +82,9 @@ __device__ __forceinline__ bool tile_rect(float u, float v, float a, float b, fl
     float lx = floorf(__fdiv_rn(__fsub_rn(u, ex), 16.0f)), hx = floorf(__fdiv_rn(__fadd_rn(u, ex), 16.0f));
     float ly = floorf(__fdiv_rn(__fsub_rn(v, ey), 16.0f)), hy = floorf(__fdiv_rn(__fadd_rn(v, ey), 16.0f));
     float fx0 = fmaxf(lx, 0.0f), fx1 = fminf(hx, (float)(tiles_x - 1));
-    float fy0 = fmaxf(ly, 0.0f), fy1 = fminf(hy, (float)(tiles_y - 1));
+    float fy0 = fmaxf(ly, (float)row0), fy1 = fminf(hy, (float)(row0 + tiles_y - 1));
     if (!(fx1 >= fx0 && fy1 >= fy0)) return false;
-    x0 = (int)fx0; x1 = (int)fx1; y0 = (int)fy0; y1 = (int)fy1;
+    x0 = (int)fx0; x1 = (int)fx1; y0 = (int)fy0 - row0; y1 = (int)fy1 - row0;
     return true;
 }
 

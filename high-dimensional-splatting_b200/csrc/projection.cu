@@ -208,8 +208,8 @@ __global__ void __launch_bounds__(PBLOCK) project_forward_kernel(
         const float lambda = mid + sqrtf(fmaxf(mid * mid - g.det, 0.0f));
         int x0, y0, x1, y1;
         const bool visible = !g.behind && g.det > 0.0f &&
-                             tile_rect(u, v, ca, cb, cc, opacity, tiles_for(cam.width), tiles_for(cam.height), x0,
-                                       y0, x1, y1);
+                             tile_rect(u, v, ca, cb, cc, opacity, tiles_for(cam.width), 0, tiles_for(cam.height),
+                                       x0, y0, x1, y1);
         radii[i] = visible ? 3.0f * sqrtf(lambda) : 0.0f;
     }
     __syncthreads();

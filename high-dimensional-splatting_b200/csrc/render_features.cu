@@ -119,7 +119,8 @@ __device__ __forceinline__ void st_shared_v4f(uint32_t addr, float4 v) {
 
 template <int C>
 __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
-    int width, int height, int tiles_x, const int2* __restrict__ ranges, const int32_t* __restrict__ values,
+    int width, int height, int tiles_x, int origin_y, const int2* __restrict__ ranges,
+    const int32_t* __restrict__ values,
     const float2* __restrict__ means2D, const float4* __restrict__ conic4, const float4* __restrict__ color_opacity,
     const float* __restrict__ features, const float* __restrict__ background, float* __restrict__ feature_image,
     float* __restrict__ final_T, int32_t* __restrict__ n_contrib, float4* __restrict__ image4) {
@@ -162,7 +163,7 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
         // ------------------------------------------------------------------ producer warps 4-7
         const int ptid = tid - 128;
         // Pixel-centre rectangle of the half tile.
-        const float hx0 = (float)x0 + 0.5f, hx1 = hx0 + 15.0f, hy0 = (float)y0 + 0.5f, hy1 = hy0 + 7.0f;
+        const float hx0 = (float)x0 + 0.5f, hx1 = hx0 + 15.0f, hy0 = (float)(y0 + origin_y) + 0.5f, hy1 = hy0 + 7.0f;
         int cursor = 0;
         for (int c = 0;; c++) {
             const int s = c % STAGES;
@@ -233,7 +234,7 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
 #pragma unroll
                     for (int w = 0; w < 4; w++) {
                         const float bx0 = (float)(x0 + (w & 1) * 8) + 0.5f;
-                        const float by0 = (float)(y0 + (w >> 1) * 4) + 0.5f;
+                        const float by0 = (float)(y0 + origin_y + (w >> 1) * 4) + 0.5f;
                         const unsigned mask =
                             __ballot_sync(FULL_MASK, valid && box_hits(mm, ee, bx0, bx0 + 7.0f, by0, by0 + 3.0f));
                         if (lane == 0) ch.hits[w] = mask;
@@ -280,7 +281,7 @@ __global__ void __launch_bounds__(256, 1) feature_forward_kernel(
         const int px = x0 + (warp & 1) * 8 + (lane & 7);
         const int py = y0 + (warp >> 1) * 4 + (lane >> 3);
         const bool inside = px < width && py < height;
-        const float cx = (float)px + 0.5f, cy = (float)py + 0.5f;
+        const float cx = (float)px + 0.5f, cy = (float)(py + origin_y) + 0.5f;
         const bool rgb = image4 != nullptr;
 
         float T = 1.0f, ar = 0.0f, ag = 0.0f, ab = 0.0f;
@@ -519,7 +520,8 @@ __device__ __forceinline__ int2 half_tile_pixel(int p) {
 
 template <int C>
 __global__ void __launch_bounds__(THREADS, 1) feature_forward_ws_kernel(
-    int width, int height, int tiles_x, const int2* __restrict__ ranges, const int32_t* __restrict__ values,
+    int width, int height, int tiles_x, int origin_y, const int2* __restrict__ ranges,
+    const int32_t* __restrict__ values,
     const float2* __restrict__ means2D, const float4* __restrict__ conic4, const float4* __restrict__ color_opacity,
     const float* __restrict__ features, const float* __restrict__ background, float* __restrict__ feature_image,
     float* __restrict__ final_T, int32_t* __restrict__ n_contrib, float4* __restrict__ image4) {
@@ -571,7 +573,7 @@ __global__ void __launch_bounds__(THREADS, 1) feature_forward_ws_kernel(
 
     if (role == Role::List) {
         // ---------------------------------------------------------------- list warp
-        const float hx0 = (float)x0 + 0.5f, hx1 = hx0 + 15.0f, hy0 = (float)y0 + 0.5f, hy1 = hy0 + 7.0f;
+        const float hx0 = (float)x0 + 0.5f, hx1 = hx0 + 15.0f, hy0 = (float)(y0 + origin_y) + 0.5f, hy1 = hy0 + 7.0f;
         auto fetch_id = [&](int b) { return b + lane < count ? values[range.x + b + lane] : -1; };
         auto gather = [&](int g, float2& m, float4& q, float4& col) {
             if (g >= 0) {
@@ -660,7 +662,7 @@ __global__ void __launch_bounds__(THREADS, 1) feature_forward_ws_kernel(
 #pragma unroll
                 for (int w = 0; w < PIXEL_WARPS; w++) {
                     const float bx0 = (float)(x0 + ((w & 3) & 1) * 8) + 0.5f;
-                    const float by0 = (float)(y0 + ((w & 3) >> 1) * 4 + (w >> 2) * 2) + 0.5f;
+                    const float by0 = (float)(y0 + origin_y + ((w & 3) >> 1) * 4 + (w >> 2) * 2) + 0.5f;
                     const unsigned mask =
                         __ballot_sync(FULL_MASK, valid && box_hits(m, e, bx0, bx0 + 7.0f, by0, by0 + 1.0f));
                     if (lane == 0) ch.hits[w] = mask;
@@ -772,7 +774,7 @@ __global__ void __launch_bounds__(THREADS, 1) feature_forward_ws_kernel(
         const int2 lp = half_tile_pixel(p);
         const int px = x0 + lp.x, py = y0 + lp.y;
         const bool inside = px < width && py < height;
-        const float cx = (float)px + 0.5f, cy = (float)py + 0.5f;
+        const float cx = (float)px + 0.5f, cy = (float)(py + origin_y) + 0.5f;
         const bool rgb = image4 != nullptr;
         float T = 1.0f, ar = 0.0f, ag = 0.0f, ab = 0.0f;
         int last = 0;
@@ -930,7 +932,7 @@ __global__ void __launch_bounds__(THREADS, 1) feature_forward_ws_kernel(
 }
 
 template <int C>
-int launch_forward_ws(int width, int height, const int32_t* tile_ranges, const int32_t* values, const float* means2D,
+int launch_forward_ws(int width, int height, int origin_y, const int32_t* tile_ranges, const int32_t* values, const float* means2D,
                       const float* conic4, const float* color_opacity, const float* features,
                       const float* background, float* feature_image, float* final_T, int32_t* n_contrib,
                       float* image4, cudaStream_t stream) {
@@ -938,7 +940,8 @@ int launch_forward_ws(int width, int height, const int32_t* tile_ranges, const i
     HDS_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<C>::SMEM));
     int tx = tiles_for(width), ty = tiles_for(height);
     kernel<<<2 * tx * ty, THREADS, Cfg<C>::SMEM, stream>>>(
-        width, height, tx, reinterpret_cast<const int2*>(tile_ranges), values, reinterpret_cast<const float2*>(means2D),
+        width, height, tx, origin_y, reinterpret_cast<const int2*>(tile_ranges), values,
+        reinterpret_cast<const float2*>(means2D),
         reinterpret_cast<const float4*>(conic4), reinterpret_cast<const float4*>(color_opacity), features, background,
         feature_image, final_T, n_contrib, reinterpret_cast<float4*>(image4));
     HDS_CHECK_LAUNCH("feature_forward_ws_kernel");
@@ -948,7 +951,7 @@ int launch_forward_ws(int width, int height, const int32_t* tile_ranges, const i
 }  // namespace ws
 
 template <int C>
-int launch_forward(int width, int height, const int32_t* tile_ranges, const int32_t* values, const float* means2D,
+int launch_forward(int width, int height, int origin_y, const int32_t* tile_ranges, const int32_t* values, const float* means2D,
                    const float* conic4, const float* color_opacity, const float* features, const float* background,
                    float* feature_image, float* final_T, int32_t* n_contrib, float* image4, cudaStream_t stream) {
     using Cfg = FwdCfg<C>;
@@ -956,7 +959,8 @@ int launch_forward(int width, int height, const int32_t* tile_ranges, const int3
     HDS_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
     int tx = tiles_for(width), ty = tiles_for(height);
     kernel<<<2 * tx * ty, Cfg::THREADS, Cfg::SMEM, stream>>>(
-        width, height, tx, reinterpret_cast<const int2*>(tile_ranges), values, reinterpret_cast<const float2*>(means2D),
+        width, height, tx, origin_y, reinterpret_cast<const int2*>(tile_ranges), values,
+        reinterpret_cast<const float2*>(means2D),
         reinterpret_cast<const float4*>(conic4), reinterpret_cast<const float4*>(color_opacity), features, background,
         feature_image, final_T, n_contrib, reinterpret_cast<float4*>(image4));
     HDS_CHECK_LAUNCH("feature_forward_kernel");
@@ -968,13 +972,16 @@ int launch_forward(int width, int height, const int32_t* tile_ranges, const int3
 
 using namespace hds;
 
-extern "C" int hds_render_features_forward(int n, int channels, int width, int height, const int32_t* tile_ranges,
+extern "C" int hds_render_features_forward(int n, int channels, int width, int height, int origin_y,
+                                           const int32_t* tile_ranges,
                                            const int32_t* values_sorted, const float* means2D, const float* conic4,
                                            const float* color_opacity, const float* features, const float* background,
                                            float* feature_image, float* final_T, int32_t* n_contrib, float* image4,
                                            hds_stream_t stream) {
     clear_error();
     HDS_REQUIRE(n >= 0 && width > 0 && height > 0, HDS_ERR_INVALID, "rasterize_features: bad sizes");
+    HDS_REQUIRE(origin_y >= 0 && origin_y % TILE == 0, HDS_ERR_INVALID,
+                "rasterize_features: origin_y %d must be a non-negative multiple of 16", origin_y);
     HDS_REQUIRE((int64_t)channels * width * height <= INT32_MAX, HDS_ERR_TOO_LARGE,
                 "a %dx%d image of %d channels overflows the feature kernels' int indices", width, height, channels);
     HDS_REQUIRE(((uintptr_t)features & 15) == 0 && ((uintptr_t)feature_image & 15) == 0, HDS_ERR_INVALID,
@@ -982,11 +989,11 @@ extern "C" int hds_render_features_forward(int n, int channels, int width, int h
     HDS_REQUIRE(image4 == nullptr || (background != nullptr && ((uintptr_t)image4 & 15) == 0), HDS_ERR_INVALID,
                 "rasterize_features: the fused RGB output needs a background and 16-byte alignment");
     switch (channels) {
-        case 32: return launch_forward<32>(width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, background, feature_image, final_T, n_contrib, image4, stream);
-        case 64: return launch_forward<64>(width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, background, feature_image, final_T, n_contrib, image4, stream);
-        case 128: return launch_forward<128>(width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, background, feature_image, final_T, n_contrib, image4, stream);
-        case 256: return ws::launch_forward_ws<256>(width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, background, feature_image, final_T, n_contrib, image4, stream);
-        case 512: return ws::launch_forward_ws<512>(width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, background, feature_image, final_T, n_contrib, image4, stream);
+        case 32: return launch_forward<32>(width, height, origin_y, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, background, feature_image, final_T, n_contrib, image4, stream);
+        case 64: return launch_forward<64>(width, height, origin_y, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, background, feature_image, final_T, n_contrib, image4, stream);
+        case 128: return launch_forward<128>(width, height, origin_y, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, background, feature_image, final_T, n_contrib, image4, stream);
+        case 256: return ws::launch_forward_ws<256>(width, height, origin_y, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, background, feature_image, final_T, n_contrib, image4, stream);
+        case 512: return ws::launch_forward_ws<512>(width, height, origin_y, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, background, feature_image, final_T, n_contrib, image4, stream);
         default:
             set_error("features must have 32, 64, 128, 256 or 512 channels, got %d", channels);
             return HDS_ERR_UNSUPPORTED;

@@ -93,7 +93,8 @@ struct BwdCfg {
 
 template <int CK, bool RGB>
 __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
-    int C, int width, int height, int tiles_x, int slices, int helper_every, const int2* __restrict__ ranges,
+    int C, int width, int height, int tiles_x, int origin_y, int slices, int helper_every,
+    const int2* __restrict__ ranges,
     const int32_t* __restrict__ values, const float2* __restrict__ means2D, const float4* __restrict__ conic4,
     const float4* __restrict__ color_opacity, const float* __restrict__ features, const float* __restrict__ final_T_in,
     const int32_t* __restrict__ n_contrib, const float* __restrict__ grad_out, float* __restrict__ grad_means2D,
@@ -156,7 +157,7 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
     if (role == Role::List) {
         // ------------------------------------------------------------------ list warp 8
         // Hit masks: which entries touch each pixel warp's 8 x 2 block (the pixel warps skip the others).
-        list_producer<RGB>(lane, x0, y0, width, height, range, values, means2D, conic4, color_opacity, n_contrib,
+        list_producer<RGB>(lane, x0, y0, origin_y, width, height, range, values, means2D, conic4, color_opacity, n_contrib,
                            s_list, s_list_full, s_list_free, &s_fail, [&](BwdChunk& ch, int filled) {
                                const bool valid = lane < filled;
                                const float2 m = valid ? ch.mean[lane] : make_float2(0.0f, 0.0f);
@@ -164,7 +165,7 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
 #pragma unroll
                                for (int w = 0; w < 8; w++) {
                                    const float bx0 = (float)(x0 + (w & 1) * 8) + 0.5f;
-                                   const float by0 = (float)(y0 + ((w & 3) >> 1) * 4 + (w >> 2) * 2) + 0.5f;
+                                   const float by0 = (float)(y0 + origin_y + ((w & 3) >> 1) * 4 + (w >> 2) * 2) + 0.5f;
                                    const unsigned mask = __ballot_sync(
                                        FULL_MASK, valid && box_hits(m, e, bx0, bx0 + 7.0f, by0, by0 + 1.0f));
                                    if (lane == 0) ch.hits[w] = mask;
@@ -268,7 +269,7 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
                 if (lane < ecnt) {
                     const float2 m = ce.mean[lane];
                     const float4 q = ce.conic[lane];
-                    const float bx = (float)(x0 + (q4 & 1) * 8) + 0.5f, by = (float)(y0 + (q4 >> 1) * 4) + 0.5f;
+                    const float bx = (float)(x0 + (q4 & 1) * 8) + 0.5f, by = (float)(y0 + origin_y + (q4 >> 1) * 4) + 0.5f;
                     const uint8_t* ub = smem + (u_base(s) - g_hi) + (lane >> 2) * U_QUAD_STRIDE + (lane & 3) * 4 +
                                         q4 * 32 * 16;
                     float m0 = 0.0f, mx = 0.0f, my = 0.0f, mxx = 0.0f, mxy = 0.0f, myy = 0.0f;
@@ -444,7 +445,7 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
         const int2 lp = half_tile_pixel(p);
         const int px = x0 + lp.x, py = y0 + lp.y;
         const bool inside = px < width && py < height;
-        const float cx = (float)px + 0.5f, cy = (float)py + 0.5f;
+        const float cx = (float)px + 0.5f, cy = (float)(py + origin_y) + 0.5f;
         const size_t pix = (size_t)py * width + px;
         float T = inside ? final_T_in[pix] : 0.0f;
         const float fT = T;  // final transmittance: the background's weight
@@ -569,7 +570,7 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
 }
 
 template <int CK>
-int launch_backward(int D, int width, int height, const int32_t* tile_ranges, const int32_t* values,
+int launch_backward(int D, int width, int height, int origin_y, const int32_t* tile_ranges, const int32_t* values,
                     const float* means2D, const float* conic4, const float* color_opacity, const float* features,
                     const float* final_T, const int32_t* n_contrib, const float* grad_output, float* grad_features,
                     float* grad_means2D, float* grad_conics, float* grad_opacities, const float* grad_image,
@@ -582,7 +583,7 @@ int launch_backward(int D, int width, int height, const int32_t* tile_ranges, co
     const int groups = helper_every > 0 ? halves / helper_every : halves;
     if (groups == 0) return HDS_OK;
     kernel<<<groups * slices, THREADS, Cfg::SMEM, stream>>>(
-        D, width, height, tx, slices, helper_every, reinterpret_cast<const int2*>(tile_ranges), values,
+        D, width, height, tx, origin_y, slices, helper_every, reinterpret_cast<const int2*>(tile_ranges), values,
         reinterpret_cast<const float2*>(means2D), reinterpret_cast<const float4*>(conic4),
         reinterpret_cast<const float4*>(color_opacity), features, final_T, n_contrib, grad_output, grad_means2D,
         grad_conics, grad_features, grad_opacities, grad_image, background, grad_colors);
@@ -651,7 +652,8 @@ int launch_with_helper(cudaStream_t stream, ClusterLaunch&& clusters, HelperLaun
 
 // grad_image (with background and grad_colors) adds the RGB backward to the same walk; NULL leaves
 // it out (the reference's rasterize_features_backward).
-int features_backward(int n, int channels, int slice_width, int width, int height, const float* grad_output,
+int features_backward(int n, int channels, int slice_width, int width, int height, int origin_y,
+                      const float* grad_output,
                       const float* features, const float* means2D, const float* conic4, const float* color_opacity,
                       const int32_t* values_sorted, const int32_t* tile_ranges, const float* final_T,
                       const int32_t* n_contrib, float* grad_features, float* grad_means2D, float* grad_conics,
@@ -659,6 +661,8 @@ int features_backward(int n, int channels, int slice_width, int width, int heigh
                       const float* background, float* grad_colors, cudaStream_t stream) {
     clear_error();
     HDS_REQUIRE(n >= 0 && width > 0 && height > 0, HDS_ERR_INVALID, "rasterize_features_backward: bad sizes");
+    HDS_REQUIRE(origin_y >= 0 && origin_y % TILE == 0, HDS_ERR_INVALID,
+                "rasterize_features_backward: origin_y %d must be a non-negative multiple of 16", origin_y);
     HDS_REQUIRE((int64_t)channels * width * height <= INT32_MAX, HDS_ERR_TOO_LARGE,
                 "a %dx%d image of %d channels overflows the feature kernels' int indices", width, height, channels);
     // The (channels, slice) pairs the reference dispatches (features.cu:601-612).
@@ -687,20 +691,20 @@ int features_backward(int n, int channels, int slice_width, int width, int heigh
             return launch_with_helper(
                 stream,
                 [&](cudaStream_t st) {
-                    return clus::launch_backward_cluster<128>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, st, m);
+                    return clus::launch_backward_cluster<128>(D, width, height, origin_y, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, st, m);
                 },
                 [&](cudaStream_t st) {
-                    return launch_backward<128>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, st, m);
+                    return launch_backward<128>(D, width, height, origin_y, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, st, m);
                 });
         }
         if (D == 256)
-            return clus::launch_backward_cluster<64>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);
-        return clus::launch_backward_cluster<128>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);
+            return clus::launch_backward_cluster<64>(D, width, height, origin_y, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);
+        return clus::launch_backward_cluster<128>(D, width, height, origin_y, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);
     }
     switch (D) {
-        case 32: return launch_backward<32>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);
-        case 64: return launch_backward<64>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);
-        default: return launch_backward<128>(D, width, height, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);
+        case 32: return launch_backward<32>(D, width, height, origin_y, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);
+        case 64: return launch_backward<64>(D, width, height, origin_y, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);
+        default: return launch_backward<128>(D, width, height, origin_y, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);
     }
 }
 
@@ -718,31 +722,32 @@ int read_and_clear_backward_status(int* status, cudaStream_t stream) {
 using namespace hds;
 
 extern "C" int hds_render_features_backward(int n, int channels, int slice_width, int width, int height,
-                                            const float* grad_output, const float* features, const float* means2D,
+                                            int origin_y, const float* grad_output, const float* features, const float* means2D,
                                             const float* conic4, const float* color_opacity,
                                             const int32_t* values_sorted, const int32_t* tile_ranges,
                                             const float* final_T, const int32_t* n_contrib, float* grad_features,
                                             float* grad_means2D, float* grad_conics, float* grad_opacities,
                                             hds_stream_t stream) {
-    return features_backward(n, channels, slice_width, width, height, grad_output, features, means2D, conic4,
+    return features_backward(n, channels, slice_width, width, height, origin_y, grad_output, features, means2D, conic4,
                              color_opacity, values_sorted, tile_ranges, final_T, n_contrib, grad_features,
                              grad_means2D, grad_conics, grad_opacities, false, nullptr, nullptr, nullptr, stream);
 }
 
 extern "C" int hds_render_features_backward_accumulate(int n, int channels, int slice_width, int width, int height,
-                                                       const float* grad_output, const float* features,
+                                                       int origin_y, const float* grad_output, const float* features,
                                                        const float* means2D, const float* conic4,
                                                        const float* color_opacity, const int32_t* values_sorted,
                                                        const int32_t* tile_ranges, const float* final_T,
                                                        const int32_t* n_contrib, float* grad_features,
                                                        float* grad_means2D, float* grad_conics, float* grad_opacities,
                                                        hds_stream_t stream) {
-    return features_backward(n, channels, slice_width, width, height, grad_output, features, means2D, conic4,
+    return features_backward(n, channels, slice_width, width, height, origin_y, grad_output, features, means2D, conic4,
                              color_opacity, values_sorted, tile_ranges, final_T, n_contrib, grad_features,
                              grad_means2D, grad_conics, grad_opacities, true, nullptr, nullptr, nullptr, stream);
 }
 
-extern "C" int hds_render_backward_fused(int n, int channels, int width, int height, const float* grad_image,
+extern "C" int hds_render_backward_fused(int n, int channels, int width, int height, int origin_y,
+                                         const float* grad_image,
                                          const float* background, const float* grad_feature_image,
                                          const float* features, const float* means2D, const float* conic4,
                                          const float* color_opacity, const int32_t* values_sorted,
@@ -750,7 +755,8 @@ extern "C" int hds_render_backward_fused(int n, int channels, int width, int hei
                                          float* grad_colors, float* grad_features, float* grad_means2D,
                                          float* grad_conics, float* grad_opacities, int accumulate_features,
                                          hds_stream_t stream) {
-    return features_backward(n, channels, channels < 128 ? channels : 128, width, height, grad_feature_image, features,
+    return features_backward(n, channels, channels < 128 ? channels : 128, width, height, origin_y,
+                             grad_feature_image, features,
                              means2D, conic4, color_opacity, values_sorted, tile_ranges, final_T, n_contrib,
                              grad_features, grad_means2D, grad_conics, grad_opacities, accumulate_features != 0,
                              grad_image, background, grad_colors, stream);

@@ -19,7 +19,7 @@ __device__ __forceinline__ int2 tile_pixel(int tid) {
     return make_int2((warp & 1) * 8 + (lane & 7), (warp >> 1) * 4 + (lane >> 3));
 }
 
-__global__ void __launch_bounds__(TILE_PIXELS) rgb_forward_kernel(int width, int height, int tiles_x,
+__global__ void __launch_bounds__(TILE_PIXELS) rgb_forward_kernel(int width, int height, int tiles_x, int origin_y,
                                                                   const int2* __restrict__ ranges,
                                                                   const int32_t* __restrict__ values,
                                                                   const float2* __restrict__ means2D,
@@ -38,9 +38,9 @@ __global__ void __launch_bounds__(TILE_PIXELS) rgb_forward_kernel(int width, int
     const int2 lp = tile_pixel(tid);
     const int px = x0 + lp.x, py = y0 + lp.y;
     const bool inside = px < width && py < height;
-    const float cx = (float)px + 0.5f, cy = (float)py + 0.5f;
+    const float cx = (float)px + 0.5f, cy = (float)(py + origin_y) + 0.5f;
     const float wx0 = (float)(x0 + (warp & 1) * 8) + 0.5f, wx1 = wx0 + 7.0f;
-    const float wy0 = (float)(y0 + (warp >> 1) * 4) + 0.5f, wy1 = wy0 + 3.0f;
+    const float wy0 = (float)(y0 + origin_y + (warp >> 1) * 4) + 0.5f, wy1 = wy0 + 3.0f;
     const int2 range = ranges[tile];
     const int count = range.y - range.x;
 
@@ -133,7 +133,7 @@ __device__ __forceinline__ float warp_sum(float x) {
 }
 
 __global__ void __launch_bounds__(TILE_PIXELS) rgb_backward_kernel(
-    int width, int height, int tiles_x, const int2* __restrict__ ranges, const int32_t* __restrict__ values,
+    int width, int height, int tiles_x, int origin_y, const int2* __restrict__ ranges, const int32_t* __restrict__ values,
     const float2* __restrict__ means2D, const float4* __restrict__ conic4, const float4* __restrict__ color_opacity,
     const float* __restrict__ background, const float* __restrict__ final_T_in, const int32_t* __restrict__ n_contrib,
     const float* __restrict__ grad_image, float* __restrict__ grad_means2D, float* __restrict__ grad_conics,
@@ -150,9 +150,9 @@ __global__ void __launch_bounds__(TILE_PIXELS) rgb_backward_kernel(
     const int2 lp = tile_pixel(tid);
     const int px = x0 + lp.x, py = y0 + lp.y;
     const float wx0 = (float)(x0 + (warp & 1) * 8) + 0.5f, wx1 = wx0 + 7.0f;
-    const float wy0 = (float)(y0 + (warp >> 1) * 4) + 0.5f, wy1 = wy0 + 3.0f;
+    const float wy0 = (float)(y0 + origin_y + (warp >> 1) * 4) + 0.5f, wy1 = wy0 + 3.0f;
     const bool inside = px < width && py < height;
-    const float cx = (float)px + 0.5f, cy = (float)py + 0.5f;
+    const float cx = (float)px + 0.5f, cy = (float)(py + origin_y) + 0.5f;
     const int2 range = ranges[tile];
     const int p = py * width + px;
 
@@ -251,17 +251,20 @@ __global__ void __launch_bounds__(TILE_PIXELS) rgb_backward_kernel(
 
 using namespace hds;
 
-extern "C" int hds_render_forward(int width, int height, const int32_t* tile_ranges, const int32_t* values_sorted,
+extern "C" int hds_render_forward(int width, int height, int origin_y, const int32_t* tile_ranges,
+                                  const int32_t* values_sorted,
                                   const float* means2D, const float* conic4, const float* color_opacity,
                                   const float* background, float* image4, float* final_T, int32_t* n_contrib,
                                   hds_stream_t stream) {
     clear_error();
     HDS_REQUIRE(width > 0 && height > 0, HDS_ERR_INVALID, "render_forward: bad image size %dx%d", width, height);
+    HDS_REQUIRE(origin_y >= 0 && origin_y % TILE == 0, HDS_ERR_INVALID,
+                "render_forward: origin_y %d must be a non-negative multiple of 16", origin_y);
     HDS_REQUIRE(((uintptr_t)image4 & 15) == 0 && ((uintptr_t)conic4 & 15) == 0 && ((uintptr_t)color_opacity & 15) == 0,
                 HDS_ERR_INVALID, "render_forward: image4, conic4 and color_opacity must be 16-byte aligned");
     int tx = tiles_for(width), ty = tiles_for(height);
     rgb_forward_kernel<<<tx * ty, TILE_PIXELS, 0, stream>>>(
-        width, height, tx, reinterpret_cast<const int2*>(tile_ranges), values_sorted,
+        width, height, tx, origin_y, reinterpret_cast<const int2*>(tile_ranges), values_sorted,
         reinterpret_cast<const float2*>(means2D), reinterpret_cast<const float4*>(conic4),
         reinterpret_cast<const float4*>(color_opacity), background, reinterpret_cast<float4*>(image4), final_T,
         n_contrib);
@@ -269,13 +272,16 @@ extern "C" int hds_render_forward(int width, int height, const int32_t* tile_ran
     return HDS_OK;
 }
 
-extern "C" int hds_render_backward(int n, int width, int height, const float* grad_image, const float* means2D,
+extern "C" int hds_render_backward(int n, int width, int height, int origin_y, const float* grad_image,
+                                   const float* means2D,
                                    const float* conic4, const float* color_opacity, const int32_t* values_sorted,
                                    const int32_t* tile_ranges, const float* final_T, const int32_t* n_contrib,
                                    const float* background, float* grad_means2D, float* grad_conics, float* grad_colors,
                                    float* grad_opacities, hds_stream_t stream) {
     clear_error();
     HDS_REQUIRE(n >= 0 && width > 0 && height > 0, HDS_ERR_INVALID, "render_backward: bad sizes");
+    HDS_REQUIRE(origin_y >= 0 && origin_y % TILE == 0, HDS_ERR_INVALID,
+                "render_backward: origin_y %d must be a non-negative multiple of 16", origin_y);
     if (n == 0) return HDS_OK;
     HDS_CHECK_CUDA(cudaMemsetAsync(grad_means2D, 0, sizeof(float) * 2 * (size_t)n, stream));
     HDS_CHECK_CUDA(cudaMemsetAsync(grad_conics, 0, sizeof(float) * 3 * (size_t)n, stream));
@@ -283,7 +289,7 @@ extern "C" int hds_render_backward(int n, int width, int height, const float* gr
     HDS_CHECK_CUDA(cudaMemsetAsync(grad_opacities, 0, sizeof(float) * (size_t)n, stream));
     int tx = tiles_for(width), ty = tiles_for(height);
     rgb_backward_kernel<<<tx * ty, TILE_PIXELS, 0, stream>>>(
-        width, height, tx, reinterpret_cast<const int2*>(tile_ranges), values_sorted,
+        width, height, tx, origin_y, reinterpret_cast<const int2*>(tile_ranges), values_sorted,
         reinterpret_cast<const float2*>(means2D), reinterpret_cast<const float4*>(conic4),
         reinterpret_cast<const float4*>(color_opacity), background, final_T, n_contrib, grad_image, grad_means2D,
         grad_conics, grad_colors, grad_opacities);

@@ -7,6 +7,11 @@ on the current CUDA stream.  Additive entry points serve this package's own auto
 ``rasterize_with_features`` (one walk producing RGB and features), ``rasterize_backward_fused`` (one
 walk for both backward passes), ``eval_sh_backward`` (plain SH gradients, for data-parallel training
 that all-reduces them) and the ``*_into`` forms that add a gradient into a caller's buffer.
+
+Every binning, blend and backward call also takes ``origin_y`` (keyword, default 0): the full
+image's row at which the given image's row 0 lies, a multiple of 16.  With it an image of
+``image_height`` rows is the band [origin_y, origin_y + image_height) of a taller view -- means2D in
+full-image pixels -- and equals those rows of the full render bit for bit (the tile-row split).
 """
 from __future__ import annotations
 
@@ -32,7 +37,7 @@ def _tiles(width: int, height: int) -> int:
     return ((width + TILE - 1) // TILE) * ((height + TILE - 1) // TILE)
 
 
-def _bin(means2D, depths, radii, conics, colors, opacities, width, height, keep_keys=False):
+def _bin(means2D, depths, radii, conics, colors, opacities, width, height, keep_keys=False, origin_y=0):
     """forward.cu:262-404: pack, count, scan, (host read), emit, sort, ranges.
 
     Returns (conic [N,4], color_opacity [N,4], values_sorted, tile_ranges [T,2], keys_sorted or None)."""
@@ -44,7 +49,7 @@ def _bin(means2D, depths, radii, conics, colors, opacities, width, height, keep_
     prep = torch.empty(lib.hds_rasterize_prepare_scratch_bytes(n), dtype=torch.uint8, device=dev)
     total = ctypes.c_int64(0)
     check(lib.hds_rasterize_prepare(n, ptr(means2D), ptr(depths), ptr(radii), ptr(conics), ptr(colors), ptr(opacities),
-                                    width, height, ptr(conic), ptr(color_opacity), ptr(prep), prep.numel(),
+                                    width, height, int(origin_y), ptr(conic), ptr(color_opacity), ptr(prep), prep.numel(),
                                     ctypes.byref(total), stream))
     dups = total.value
     tiles = _tiles(width, height)
@@ -60,7 +65,8 @@ def _bin(means2D, depths, radii, conics, colors, opacities, width, height, keep_
     return conic, color_opacity, values, ranges, keys
 
 
-def rasterize(means2D, depths, radii, conics, colors, opacities, background, image_width: int, image_height: int):
+def rasterize(means2D, depths, radii, conics, colors, opacities, background, image_width: int, image_height: int, *,
+              origin_y: int = 0):
     """forward.cu:239-435.  Returns (image [H,W,3] view of [H,W,4], final_T [H,W], n_contrib [H,W],
     values_sorted [Dups], tile_ranges [T,2], conic [N,4], color_opacity [N,4])."""
     for t, name in ((means2D, "means2D"), (depths, "depths"), (radii, "radii"), (conics, "conics"),
@@ -68,7 +74,8 @@ def rasterize(means2D, depths, radii, conics, colors, opacities, background, ima
         _check(t, name)
     width, height = int(image_width), int(image_height)
     dev = means2D.device
-    conic, color_opacity, values, ranges, _ = _bin(means2D, depths, radii, conics, colors, opacities, width, height)
+    conic, color_opacity, values, ranges, _ = _bin(means2D, depths, radii, conics, colors, opacities, width, height,
+                                                   origin_y=origin_y)
     if values.numel() == 0:
         return (background.reshape(1, 1, 3).expand(height, width, 3).contiguous(),
                 torch.ones(height, width, dtype=_F32, device=dev), torch.zeros(height, width, dtype=_I32, device=dev),
@@ -76,13 +83,14 @@ def rasterize(means2D, depths, radii, conics, colors, opacities, background, ima
     out = torch.empty(height, width, 4, dtype=_F32, device=dev)
     final_T = torch.empty(height, width, dtype=_F32, device=dev)
     n_contrib = torch.empty(height, width, dtype=_I32, device=dev)
-    check(lib.hds_render_forward(width, height, ptr(ranges), ptr(values), ptr(means2D), ptr(conic), ptr(color_opacity),
+    check(lib.hds_render_forward(width, height, int(origin_y), ptr(ranges), ptr(values), ptr(means2D), ptr(conic),
+                                 ptr(color_opacity),
                                  ptr(background), ptr(out), ptr(final_T), ptr(n_contrib), stream_of(dev)))
     return out[..., :3], final_T, n_contrib, values, ranges, conic, color_opacity
 
 
 def rasterize_with_features(means2D, depths, radii, conics, colors, opacities, background, features,
-                            image_width: int, image_height: int):
+                            image_width: int, image_height: int, *, origin_y: int = 0):
     """rasterize + rasterize_features in one walk of the sorted lists (the RGB image is a by-product of
     the feature pass).  Returns (image, feature_image, final_T, n_contrib, values_sorted, tile_ranges,
     conic, color_opacity); final_T / n_contrib serve both images' backward passes."""
@@ -94,19 +102,21 @@ def rasterize_with_features(means2D, depths, radii, conics, colors, opacities, b
     width, height = int(image_width), int(image_height)
     dev = means2D.device
     n, d = features.shape
-    conic, color_opacity, values, ranges, _ = _bin(means2D, depths, radii, conics, colors, opacities, width, height)
+    conic, color_opacity, values, ranges, _ = _bin(means2D, depths, radii, conics, colors, opacities, width, height,
+                                                   origin_y=origin_y)
     out = torch.empty(height, width, 4, dtype=_F32, device=dev)
     feature_image = torch.empty(height, width, d, dtype=_F32, device=dev)
     final_T = torch.empty(height, width, dtype=_F32, device=dev)
     n_contrib = torch.empty(height, width, dtype=_I32, device=dev)
-    check(lib.hds_render_features_forward(n, d, width, height, ptr(ranges), ptr(values), ptr(means2D), ptr(conic),
+    check(lib.hds_render_features_forward(n, d, width, height, int(origin_y), ptr(ranges), ptr(values), ptr(means2D),
+                                          ptr(conic),
                                           ptr(color_opacity), ptr(features), ptr(background), ptr(feature_image),
                                           ptr(final_T), ptr(n_contrib), ptr(out), stream_of(dev)))
     return out[..., :3], feature_image, final_T, n_contrib, values, ranges, conic, color_opacity
 
 
 def rasterize_backward(grad_image, means2D, conic, color_opacity, values_sorted, tile_ranges, final_transmittance,
-                       n_contrib, background, image_width: int, image_height: int):
+                       n_contrib, background, image_width: int, image_height: int, *, origin_y: int = 0):
     """backward.cu:166-226.  Returns (dL/dmeans2D [N,2], dL/dconics [N,3], dL/dcolors [N,3], dL/dopacities [N,1])."""
     for t, name in ((grad_image, "grad_image"), (means2D, "means2D"), (conic, "conic"),
                     (color_opacity, "color_opacity"), (values_sorted, "values_sorted"), (tile_ranges, "tile_ranges"),
@@ -118,7 +128,8 @@ def rasterize_backward(grad_image, means2D, conic, color_opacity, values_sorted,
     gc = torch.empty(n, 3, dtype=_F32, device=dev)
     gcol = torch.empty(n, 3, dtype=_F32, device=dev)
     go = torch.empty(n, 1, dtype=_F32, device=dev)
-    check(lib.hds_render_backward(n, int(image_width), int(image_height), ptr(grad_image), ptr(means2D), ptr(conic),
+    check(lib.hds_render_backward(n, int(image_width), int(image_height), int(origin_y), ptr(grad_image), ptr(means2D),
+                                  ptr(conic),
                                   ptr(color_opacity), ptr(values_sorted), ptr(tile_ranges), ptr(final_transmittance),
                                   ptr(n_contrib), ptr(background), ptr(gm), ptr(gc), ptr(gcol), ptr(go),
                                   stream_of(dev)))
@@ -126,7 +137,7 @@ def rasterize_backward(grad_image, means2D, conic, color_opacity, values_sorted,
 
 
 def rasterize_features(features, means2D, conic, color_opacity, values_sorted, tile_ranges, image_width: int,
-                       image_height: int):
+                       image_height: int, *, origin_y: int = 0):
     """features.cu:299-346.  Returns (feature_image [H,W,D], final_T [H,W], n_contrib [H,W])."""
     if not (features.is_cuda and features.is_contiguous() and features.dtype == _F32):
         raise RuntimeError("features must be a contiguous float32 CUDA tensor")
@@ -136,14 +147,16 @@ def rasterize_features(features, means2D, conic, color_opacity, values_sorted, t
     out = torch.empty(height, width, d, dtype=_F32, device=dev)
     final_T = torch.empty(height, width, dtype=_F32, device=dev)
     n_contrib = torch.empty(height, width, dtype=_I32, device=dev)
-    check(lib.hds_render_features_forward(n, d, width, height, ptr(tile_ranges), ptr(values_sorted), ptr(means2D),
+    check(lib.hds_render_features_forward(n, d, width, height, int(origin_y), ptr(tile_ranges), ptr(values_sorted),
+                                          ptr(means2D),
                                           ptr(conic), ptr(color_opacity), ptr(features), None, ptr(out), ptr(final_T),
                                           ptr(n_contrib), None, stream_of(dev)))
     return out, final_T, n_contrib
 
 
 def rasterize_features_backward(grad_output, features, means2D, conic, color_opacity, values_sorted, tile_ranges,
-                                final_transmittance, n_contrib, image_width: int, image_height: int, slice_width: int):
+                                final_transmittance, n_contrib, image_width: int, image_height: int, slice_width: int, *,
+                                origin_y: int = 0):
     """features.cu:561-616.  Returns (dL/dfeatures [N,D], dL/dmeans2D [N,2], dL/dconics [N,3], dL/dopacities [N,1])."""
     if not (grad_output.is_cuda and grad_output.is_contiguous()):
         raise RuntimeError("grad_output must be a contiguous CUDA tensor")
@@ -153,7 +166,8 @@ def rasterize_features_backward(grad_output, features, means2D, conic, color_opa
     gm = torch.empty(n, 2, dtype=_F32, device=dev)
     gc = torch.empty(n, 3, dtype=_F32, device=dev)
     go = torch.empty(n, 1, dtype=_F32, device=dev)
-    check(lib.hds_render_features_backward(n, d, int(slice_width), int(image_width), int(image_height), ptr(grad_output),
+    check(lib.hds_render_features_backward(n, d, int(slice_width), int(image_width), int(image_height), int(origin_y),
+                                           ptr(grad_output),
                                            ptr(features), ptr(means2D), ptr(conic), ptr(color_opacity),
                                            ptr(values_sorted), ptr(tile_ranges), ptr(final_transmittance),
                                            ptr(n_contrib), ptr(gf), ptr(gm), ptr(gc), ptr(go), stream_of(dev)))
@@ -162,7 +176,7 @@ def rasterize_features_backward(grad_output, features, means2D, conic, color_opa
 
 def rasterize_features_backward_into(grad_features, grad_output, features, means2D, conic, color_opacity,
                                      values_sorted, tile_ranges, final_transmittance, n_contrib, image_width: int,
-                                     image_height: int, slice_width: int):
+                                     image_height: int, slice_width: int, *, origin_y: int = 0):
     """rasterize_features_backward that ADDS dL/dfeatures into grad_features ([N,D] fp32, contiguous)
     instead of returning a fresh tensor; no counterpart in the reference.  Returns (dL/dmeans2D,
     dL/dconics, dL/dopacities)."""
@@ -177,7 +191,8 @@ def rasterize_features_backward_into(grad_features, grad_output, features, means
     gc = torch.empty(n, 3, dtype=_F32, device=dev)
     go = torch.empty(n, 1, dtype=_F32, device=dev)
     check(lib.hds_render_features_backward_accumulate(
-        n, d, int(slice_width), int(image_width), int(image_height), ptr(grad_output), ptr(features), ptr(means2D),
+        n, d, int(slice_width), int(image_width), int(image_height), int(origin_y), ptr(grad_output), ptr(features),
+        ptr(means2D),
         ptr(conic), ptr(color_opacity), ptr(values_sorted), ptr(tile_ranges), ptr(final_transmittance),
         ptr(n_contrib), ptr(grad_features), ptr(gm), ptr(gc), ptr(go), stream_of(dev)))
     return gm, gc, go
@@ -185,7 +200,7 @@ def rasterize_features_backward_into(grad_features, grad_output, features, means
 
 def rasterize_backward_fused(grad_image, background, grad_feature_image, features, means2D, conic, color_opacity,
                              values_sorted, tile_ranges, final_transmittance, n_contrib, image_width: int,
-                             image_height: int, grad_features_into=None):
+                             image_height: int, grad_features_into=None, *, origin_y: int = 0):
     """The RGB and feature backward in one walk (no counterpart in the reference, which runs
     rasterize_backward and rasterize_features_backward).  grad_image may be None (no RGB terms).
     grad_features_into, if given, is an [N, D] fp32 buffer that dL/dfeatures is added to.
@@ -210,7 +225,7 @@ def rasterize_backward_fused(grad_image, background, grad_feature_image, feature
     go = torch.empty(n, 1, dtype=_F32, device=dev)
     gcol = torch.empty(n, 3, dtype=_F32, device=dev) if grad_image is not None else None
     check(lib.hds_render_backward_fused(
-        n, d, int(image_width), int(image_height), ptr(grad_image) if grad_image is not None else None,
+        n, d, int(image_width), int(image_height), int(origin_y), ptr(grad_image) if grad_image is not None else None,
         ptr(background) if grad_image is not None else None, ptr(grad_feature_image), ptr(features), ptr(means2D),
         ptr(conic), ptr(color_opacity), ptr(values_sorted), ptr(tile_ranges), ptr(final_transmittance),
         ptr(n_contrib), ptr(gcol) if gcol is not None else None, ptr(gf), ptr(gm), ptr(gc), ptr(go), accumulate,
@@ -396,10 +411,11 @@ def ssim_backward(grad_mean, rendered, gt, d_mu, d_aa, d_ab):
     return grad
 
 
-def bin_gaussians(means2D, depths, radii, conics, opacities, image_width: int, image_height: int):
+def bin_gaussians(means2D, depths, radii, conics, opacities, image_width: int, image_height: int, *,
+                  origin_y: int = 0):
     """The binning stage alone, with the sorted keys (for bit-exact checks against the oracle).
     Returns (keys_sorted int64 [Dups], values_sorted [Dups], tile_ranges [T,2])."""
     colors = torch.zeros(means2D.shape[0], 3, dtype=_F32, device=means2D.device)
     _, _, values, ranges, keys = _bin(means2D, depths, radii, conics, colors, opacities, int(image_width),
-                                      int(image_height), keep_keys=True)
+                                      int(image_height), keep_keys=True, origin_y=origin_y)
     return keys, values, ranges

@@ -12,7 +12,7 @@ from ctypes import c_float, c_int, c_int64, c_size_t, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libhds_b200.so"
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 P = c_void_p  # device pointer
 S = c_void_p  # cudaStream_t
@@ -35,16 +35,19 @@ SIGNATURES = {
     "hds_eval_sh_forward_view": [c_int, c_int, P, P, P, P, P, P, S],
     "hds_eval_sh_backward_view": [c_int, c_int, P, P, P, P, P, P, P, P, P, c_int, S],
     "hds_rasterize_prepare_scratch_bytes": [c_int],
-    "hds_rasterize_prepare": [c_int, P, P, P, P, P, P, c_int, c_int, P, P, P, c_size_t, ctypes.POINTER(c_int64), S],
+    "hds_rasterize_prepare": [c_int, P, P, P, P, P, P, c_int, c_int, c_int, P, P, P, c_size_t, ctypes.POINTER(c_int64),
+                              S],
     "hds_rasterize_sort_scratch_bytes": [c_int, c_int64, c_int, c_int],
     "hds_rasterize_sort": [c_int, c_int64, c_int, c_int, P, P, c_size_t, P, P, P, S],
-    "hds_render_forward": [c_int, c_int, P, P, P, P, P, P, P, P, P, S],
-    "hds_render_backward": [c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, P, P, S],
-    "hds_render_features_forward": [c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, S],
-    "hds_render_features_backward": [c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, P, P, S],
-    "hds_render_features_backward_accumulate": [c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, P,
-                                                P, S],
-    "hds_render_backward_fused": [c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, c_int, S],
+    "hds_render_forward": [c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, S],
+    "hds_render_backward": [c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, P, P, S],
+    "hds_render_features_forward": [c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, S],
+    "hds_render_features_backward": [c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, P, P,
+                                     S],
+    "hds_render_features_backward_accumulate": [c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P,
+                                                P, P, P, S],
+    "hds_render_backward_fused": [c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P,
+                                  c_int, S],
     "hds_ssim_forward": [c_int, c_int, P, P, P, P, P, P, S],
     "hds_ssim_backward": [c_int, c_int, P, P, P, P, P, P, P, S],
     "hds_adam_step": [c_int64, P, P, P, P, c_int, ctypes.POINTER(c_int64), ctypes.POINTER(c_float), c_float, c_float,

@@ -66,21 +66,23 @@ class RasterizeGaussians(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, means2D, depths, radii, conics, colors, opacities, background, features, image_width,
-                image_height):
+                image_height, origin_y=0):
         ext = _get_rasterizer()
         width, height = int(image_width), int(image_height)
         ctx.image_size = (width, height)
+        ctx.origin_y = o = int(origin_y)
         args = (means2D.contiguous(), depths.contiguous(), radii.contiguous(), conics.contiguous(),
                 colors.contiguous(), opacities.contiguous(), background.contiguous())
         if features is None:
-            image, final_T, n_contrib, values, ranges, conic, color_opacity = ext.rasterize(*args, width, height)
+            image, final_T, n_contrib, values, ranges, conic, color_opacity = ext.rasterize(*args, width, height,
+                                                                                            origin_y=o)
             ctx.save_for_backward(means2D, conic, color_opacity, values, ranges, final_T, n_contrib, background, None,
                                   None, None)
             return image
         ctx.features_leaf = features if (ACCUMULATE_INTO_LEAF_GRAD and features.is_leaf) else None
         features = features.contiguous()
         image, feature_image, final_T, n_contrib, values, ranges, conic, color_opacity = ext.rasterize_with_features(
-            *args, features, width, height)
+            *args, features, width, height, origin_y=o)
         ctx.save_for_backward(means2D, conic, color_opacity, values, ranges, final_T, n_contrib, background, features,
                               final_T, n_contrib)
         return image, feature_image
@@ -90,6 +92,7 @@ class RasterizeGaussians(torch.autograd.Function):
         (means2D, conic, color_opacity, values, ranges, final_T, n_contrib, background, features, feature_T,
          feature_contrib) = ctx.saved_tensors
         width, height = ctx.image_size
+        o = ctx.origin_y
         ext = _get_rasterizer()
         means2D = means2D.contiguous()
         # Frozen features still shape the geometry gradients (the reference's __init__.py:150-153).
@@ -107,7 +110,7 @@ class RasterizeGaussians(torch.autograd.Function):
                     grad_means2D, grad_conics, grad_colors, grad_opacities, grad_feats = ext.rasterize_backward_fused(
                         grad_image.contiguous() if grad_image is not None else None, background,
                         grad_features.contiguous(), features, means2D, conic, color_opacity, values, ranges,
-                        feature_T, feature_contrib, width, height, grad_features_into=target)
+                        feature_T, feature_contrib, width, height, grad_features_into=target, origin_y=o)
                 if grad_colors is None:
                     grad_colors = torch.zeros(means2D.shape[0], 3, device=means2D.device)
             else:
@@ -117,41 +120,43 @@ class RasterizeGaussians(torch.autograd.Function):
                 with torch.cuda.nvtx.range("rasterize_backward"):
                     grad_means2D, grad_conics, grad_colors, grad_opacities = ext.rasterize_backward(
                         grad_image.contiguous(), means2D, conic, color_opacity, values, ranges, final_T, n_contrib,
-                        background, width, height)
+                        background, width, height, origin_y=o)
                 slice_width = FEATURE_SLICE_WIDTH or min(features.shape[1], 128)
                 with torch.cuda.nvtx.range("rasterize_features_backward"):
                     if target is not None:
                         f_means2D, f_conics, f_opacities = ext.rasterize_features_backward_into(
                             target, grad_features.contiguous(), features, means2D, conic, color_opacity, values,
-                            ranges, feature_T, feature_contrib, width, height, slice_width)
+                            ranges, feature_T, feature_contrib, width, height, slice_width, origin_y=o)
                         grad_feats = None
                     else:
                         grad_feats, f_means2D, f_conics, f_opacities = ext.rasterize_features_backward(
                             grad_features.contiguous(), features, means2D, conic, color_opacity, values, ranges,
-                            feature_T, feature_contrib, width, height, slice_width)
+                            feature_T, feature_contrib, width, height, slice_width, origin_y=o)
                 grad_means2D += f_means2D
                 grad_conics += f_conics
                 grad_opacities += f_opacities
             if not ctx.needs_input_grad[7]:
                 grad_feats = None
-            return grad_means2D, None, None, grad_conics, grad_colors, grad_opacities, None, grad_feats, None, None
+            return (grad_means2D, None, None, grad_conics, grad_colors, grad_opacities, None, grad_feats, None, None,
+                    None)
         if grad_image is None:
             grad_image = torch.zeros(height, width, 3, device=means2D.device)
         with torch.cuda.nvtx.range("rasterize_backward"):
             grad_means2D, grad_conics, grad_colors, grad_opacities = ext.rasterize_backward(
                 grad_image.contiguous(), means2D, conic, color_opacity, values, ranges, final_T, n_contrib,
-                background, width, height)
-        return grad_means2D, None, None, grad_conics, grad_colors, grad_opacities, None, None, None, None
+                background, width, height, origin_y=o)
+        return grad_means2D, None, None, grad_conics, grad_colors, grad_opacities, None, None, None, None, None
 
 
 def rasterize(means2D: torch.Tensor, depths: torch.Tensor, radii: torch.Tensor, conics: torch.Tensor,
               colors: torch.Tensor, opacities: torch.Tensor, image_width: int, image_height: int,
-              background: torch.Tensor | None = None, features: torch.Tensor | None = None):
+              background: torch.Tensor | None = None, features: torch.Tensor | None = None, *, origin_y: int = 0):
     """Alpha-blends projected gaussians into an image, front to back, on 16x16 tiles
     (the reference's __init__.py:168-211).
 
     Returns the [H, W, 3] image, or (image, [H, W, D] feature image) when features ([N, D], D one of
-    32, 64, 128, 256 or 512) are given."""
+    32, 64, 128, 256 or 512) are given.  origin_y (a multiple of 16) renders the band of rows
+    [origin_y, origin_y + image_height) of a taller view whose means2D these are."""
     n = means2D.shape[0]
     assert means2D.shape == (n, 2)
     assert depths.shape == (n,) and radii.shape == (n,)
@@ -162,4 +167,4 @@ def rasterize(means2D: torch.Tensor, depths: torch.Tensor, radii: torch.Tensor, 
     assert background.shape == (3,)
     assert features is None or (features.ndim == 2 and features.shape[0] == n)
     return RasterizeGaussians.apply(means2D, depths, radii, conics, colors, opacities, background, features,
-                                    image_width, image_height)
+                                    image_width, image_height, origin_y)

@@ -50,7 +50,7 @@ int hds_abi_version(void);
 
 /* Number of kernels this library has launched in the process so far (all threads and devices). */
 unsigned long long hds_launch_count(void);
-#define HDS_ABI_VERSION 1
+#define HDS_ABI_VERSION 2
 
 /* ---------------------------------------------------------------------------------------------
  * Projection.  Replaces project_gaussians (projection.cu:210-231; autograd glue projection.py:25-96).
@@ -151,10 +151,18 @@ int hds_eval_sh_backward_view(int n, int degree, const float* grad_rgb, const fl
  * 3. hds_render_forward (forward.cu:406-434): front-to-back FP32 blend.  image4 [H,W,4] (the
  *    reference's padded layout; channel 3 written 0), final_T [H,W], n_contrib [H,W] (1-based
  *    index of the last blended list entry).
+ *
+ * Bands of rows (origin_y; no counterpart in the reference).  Every call of the binning, blend and
+ * backward entry points takes origin_y, the row of the full image at which this image's row 0 lies
+ * (a non-negative multiple of 16; 0 renders a whole image, the reference's call).  With
+ * origin_y = y0 and height = the band's rows, the call renders rows [y0, y0 + height) of the full
+ * view: means2D stay in full-image pixels, pixel centres and tile rectangles use full-image
+ * coordinates, and only the band's tile rows are binned, so the band's outputs equal those rows of
+ * the full render bit for bit.  The tile-row split of one view across GPUs is built on it.
  * ------------------------------------------------------------------------------------------- */
 size_t hds_rasterize_prepare_scratch_bytes(int n);
 int hds_rasterize_prepare(int n, const float* means2D, const float* depths, const float* radii, const float* conics,
-                          const float* colors, const float* opacities, int width, int height, float* conic4,
+                          const float* colors, const float* opacities, int width, int height, int origin_y, float* conic4,
                           float* color_opacity, void* scratch, size_t scratch_bytes, int64_t* num_duplicates,
                           hds_stream_t stream);
 
@@ -163,14 +171,14 @@ int hds_rasterize_sort(int n, int64_t num_duplicates, int width, int height, con
                        void* scratch, size_t scratch_bytes, int32_t* values_sorted, int32_t* tile_ranges,
                        uint64_t* keys_sorted, hds_stream_t stream);
 
-int hds_render_forward(int width, int height, const int32_t* tile_ranges, const int32_t* values_sorted,
+int hds_render_forward(int width, int height, int origin_y, const int32_t* tile_ranges, const int32_t* values_sorted,
                        const float* means2D, const float* conic4, const float* color_opacity,
                        const float* background, float* image4, float* final_T, int32_t* n_contrib,
                        hds_stream_t stream);
 
 /* Replaces rasterize_backward (backward.cu:166-226).  grad_image [H,W,3]; outputs dL/dmeans2D [n,2],
  * dL/dconics [n,3], dL/dcolors [n,3], dL/dopacities [n]. */
-int hds_render_backward(int n, int width, int height, const float* grad_image, const float* means2D,
+int hds_render_backward(int n, int width, int height, int origin_y, const float* grad_image, const float* means2D,
                         const float* conic4, const float* color_opacity, const int32_t* values_sorted,
                         const int32_t* tile_ranges, const float* final_T, const int32_t* n_contrib,
                         const float* background, float* grad_means2D, float* grad_conics, float* grad_colors,
@@ -179,12 +187,12 @@ int hds_render_backward(int n, int width, int height, const float* grad_image, c
 /* ---------------------------------------------------------------------------------------------
  * Feature blend.  Replaces rasterize_features (features.cu:299-346): features [n,C] with
  * C in {32, 64, 128, 256, 512} blended over a zero background into feature_image [H,W,C], plus its
- * own final_T and n_contrib.  The contraction runs on tcgen05 TF32 tensor cores (weights and
- * features rounded to nearest TF32).  When image4 is non-NULL the same walk also writes the RGB
+ * own final_T and n_contrib.  The contraction runs on tcgen05 tensor cores in split bf16 (each weight
+ * and feature as bf16 hi + lo, products hi*hi + hi*lo + lo*hi, fp32 accumulation).  When image4 is non-NULL the same walk also writes the RGB
  * image (colours from color_opacity, over `background`), which the reference computes in a second
  * pass; that is an addition, NULL reproduces the reference call.
  * ------------------------------------------------------------------------------------------- */
-int hds_render_features_forward(int n, int channels, int width, int height, const int32_t* tile_ranges,
+int hds_render_features_forward(int n, int channels, int width, int height, int origin_y, const int32_t* tile_ranges,
                                 const int32_t* values_sorted, const float* means2D, const float* conic4,
                                 const float* color_opacity, const float* features, const float* background,
                                 float* feature_image, float* final_T, int32_t* n_contrib, float* image4,
@@ -193,7 +201,7 @@ int hds_render_features_forward(int n, int channels, int width, int height, cons
 /* Replaces rasterize_features_backward (features.cu:561-616).  slice_width is the channel slice one
  * block owns, one of the reference's pairs (features.cu:601-612); any other pair is rejected.
  * Outputs dL/dfeatures [n,C], dL/dmeans2D [n,2], dL/dconics [n,3], dL/dopacities [n]. */
-int hds_render_features_backward(int n, int channels, int slice_width, int width, int height,
+int hds_render_features_backward(int n, int channels, int slice_width, int width, int height, int origin_y,
                                  const float* grad_output, const float* features, const float* means2D,
                                  const float* conic4, const float* color_opacity, const int32_t* values_sorted,
                                  const int32_t* tile_ranges, const float* final_T, const int32_t* n_contrib,
@@ -205,7 +213,7 @@ int hds_render_features_backward(int n, int channels, int slice_width, int width
  * a training loop that accumulates several views into one gradient buffer skip clearing a fresh
  * [n,C] buffer and adding it afterwards.  grad_features must be 16-byte aligned. */
 int hds_render_features_backward_accumulate(int n, int channels, int slice_width, int width, int height,
-                                            const float* grad_output, const float* features, const float* means2D,
+                                            int origin_y, const float* grad_output, const float* features, const float* means2D,
                                             const float* conic4, const float* color_opacity,
                                             const int32_t* values_sorted, const int32_t* tile_ranges,
                                             const float* final_T, const int32_t* n_contrib, float* grad_features,
@@ -222,7 +230,7 @@ int hds_render_features_backward_accumulate(int n, int channels, int slice_width
  *  - Outputs dL/dcolors [n,3], dL/dfeatures [n,C] (added to the buffer when accumulate_features is
  *    non-zero, otherwise overwritten), dL/dmeans2D [n,2], dL/dconics [n,3], dL/dopacities [n]: the
  *    sums of both passes. */
-int hds_render_backward_fused(int n, int channels, int width, int height, const float* grad_image,
+int hds_render_backward_fused(int n, int channels, int width, int height, int origin_y, const float* grad_image,
                               const float* background, const float* grad_feature_image, const float* features,
                               const float* means2D, const float* conic4, const float* color_opacity,
                               const int32_t* values_sorted, const int32_t* tile_ranges, const float* final_T,

@@ -67,11 +67,11 @@ def lib():
         L.oracle_adam.argtypes = [c_int, F32P, F32P, F32P, F32P, c_float, c_float, c_float, c_float, c_float,
                                   c_float, c_float]
         L.oracle_bin.restype = c_i64
-        L.oracle_bin.argtypes = [c_int, F32P, F32P, F32P, F32P, F32P, c_int, c_int, c_i64, vp, vp, vp, vp]
-        L.oracle_render_forward.argtypes = [c_int, c_int, I32P, I32P, F32P, F32P, vp, F32P, vp, c_int, vp, c_int,
-                                            vp, vp, vp, vp]
-        L.oracle_render_backward.argtypes = [c_int, c_int, I32P, I32P, F32P, F32P, vp, F32P, vp, F32P, I32P, vp,
-                                             c_int, vp, vp, F64P, F64P, F64P, F64P, vp]
+        L.oracle_bin.argtypes = [c_int, F32P, F32P, F32P, F32P, F32P, c_int, c_int, c_int, c_i64, vp, vp, vp, vp]
+        L.oracle_render_forward.argtypes = [c_int, c_int, c_int, I32P, I32P, F32P, F32P, vp, F32P, vp, c_int, vp,
+                                            c_int, vp, vp, vp, vp]
+        L.oracle_render_backward.argtypes = [c_int, c_int, c_int, I32P, I32P, F32P, F32P, vp, F32P, vp, F32P, I32P,
+                                             vp, c_int, vp, vp, F64P, F64P, F64P, F64P, vp]
         L.oracle_ssim_forward.argtypes = [c_int, c_int, F32P, F32P, F32P, F32P, F32P, F32P]
         L.oracle_ssim_backward.argtypes = [c_int, c_int, c_float, F32P, F32P, F32P, F32P, F32P, F32P]
     return _lib
@@ -208,24 +208,25 @@ def tile_grid(width: int, height: int) -> tuple[int, int]:
     return (width + TILE - 1) // TILE, (height + TILE - 1) // TILE
 
 
-def bin_gaussians(means2D, depths, radii, conics, opacities, width, height):
-    """forward.cu:13-139 plus the stable radix sort (forward.cu:363-394).
+def bin_gaussians(means2D, depths, radii, conics, opacities, width, height, origin_y=0):
+    """forward.cu:13-139 plus the stable radix sort (forward.cu:363-394).  origin_y (a multiple of 16):
+    bin the band of `height` rows starting at that row of a taller view (means2D in its pixels).
 
     Returns (tiles_touched [N] i32, keys_sorted [Dups] u64, values_sorted [Dups] i32, ranges [T,2] i32)."""
     args = [f32(means2D), f32(depths).reshape(-1), f32(radii).reshape(-1), f32(conics), f32(opacities).reshape(-1)]
     n = args[1].shape[0]
     tx, ty = tile_grid(width, height)
     touched = np.zeros(max(n, 1), np.int32)
-    total = lib().oracle_bin(n, *args, width, height, 0, None, None, None, _ptr(touched))
+    total = lib().oracle_bin(n, *args, width, height, int(origin_y), 0, None, None, None, _ptr(touched))
     keys = np.zeros(max(total, 1), np.uint64)
     vals = np.zeros(max(total, 1), np.int32)
     ranges = np.zeros((tx * ty, 2), np.int32)
-    lib().oracle_bin(n, *args, width, height, total, _ptr(keys), _ptr(vals), _ptr(ranges), None)
+    lib().oracle_bin(n, *args, width, height, int(origin_y), total, _ptr(keys), _ptr(vals), _ptr(ranges), None)
     return touched[:n], keys[:total], vals[:total], ranges
 
 
 def render_forward(ranges, values, means2D, conics, colors, opacities, width, height, background=None,
-                   features=None, tf32_round=False, split_bf16=False):
+                   features=None, tf32_round=False, split_bf16=False, origin_y=0):
     """forward.cu:141-237 (RGB) and features.cu:116-282 (features) over the binned lists.
 
     Feature products are exact by default; tf32_round rounds weights and features like
@@ -241,7 +242,7 @@ def render_forward(ranges, values, means2D, conics, colors, opacities, width, he
     colors_a = None if colors is None else f32(colors)
     bg = None if background is None else f32(background)
     feats = None if features is None else f32(features)
-    lib().oracle_render_forward(width, height, np.ascontiguousarray(ranges, np.int32).reshape(-1),
+    lib().oracle_render_forward(width, height, int(origin_y), np.ascontiguousarray(ranges, np.int32).reshape(-1),
                                 np.ascontiguousarray(values, np.int32).reshape(-1), f32(means2D), f32(conics),
                                 _ptr(colors_a), f32(opacities).reshape(-1), _ptr(bg), ch, _ptr(feats),
                                 2 if split_bf16 else int(bool(tf32_round)), _ptr(image), _ptr(final_T),
@@ -251,7 +252,7 @@ def render_forward(ranges, values, means2D, conics, colors, opacities, width, he
 
 
 def render_backward(ranges, values, means2D, conics, colors, opacities, width, height, final_T, n_contrib,
-                    grad_image=None, background=None, features=None, grad_features=None):
+                    grad_image=None, background=None, features=None, grad_features=None, origin_y=0):
     """backward.cu:7-164 and features.cu:350-542.  Returns float64 grads
     (means2D [N,2], conics [N,3], colors [N,3], opacities [N,1], features [N,C] or None)."""
     n = f32(means2D).shape[0]
@@ -264,7 +265,7 @@ def render_backward(ranges, values, means2D, conics, colors, opacities, width, h
             f32(grad_image) if grad_image is not None else None,
             f32(features) if features is not None else None,
             f32(grad_features) if grad_features is not None else None]
-    lib().oracle_render_backward(width, height, np.ascontiguousarray(ranges, np.int32).reshape(-1),
+    lib().oracle_render_backward(width, height, int(origin_y), np.ascontiguousarray(ranges, np.int32).reshape(-1),
                                  np.ascontiguousarray(values, np.int32).reshape(-1), f32(means2D), f32(conics),
                                  _ptr(keep[0]), f32(opacities).reshape(-1), _ptr(keep[1]), f32(final_T),
                                  np.ascontiguousarray(n_contrib, np.int32), _ptr(keep[2]), ch, _ptr(keep[3]),
@@ -291,10 +292,11 @@ def ssim_backward(grad_mean, rendered, gt, d_mu, d_aa, d_ab):
 
 
 def rasterize(means2D, depths, radii, conics, colors, opacities, width, height, background=None, features=None,
-              tf32_round=False):
-    """Binning + blend in one call: the oracle's counterpart of the reference's rasterize (+ features)."""
-    touched, keys, values, ranges = bin_gaussians(means2D, depths, radii, conics, opacities, width, height)
+              tf32_round=False, origin_y=0):
+    """Binning + blend in one call: the oracle's counterpart of the reference's rasterize (+ features).
+    origin_y: the band of `height` rows starting at that row of a taller view."""
+    touched, keys, values, ranges = bin_gaussians(means2D, depths, radii, conics, opacities, width, height, origin_y)
     image, final_T, n_contrib, feat = render_forward(ranges, values, means2D, conics, colors, opacities, width, height,
-                                                     background, features, tf32_round)
+                                                     background, features, tf32_round, origin_y=origin_y)
     return {"tiles_touched": touched, "keys": keys, "values": values, "ranges": ranges, "image": image,
             "final_T": final_T, "n_contrib": n_contrib, "features": feat}

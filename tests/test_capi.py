@@ -49,15 +49,15 @@ def test_abi_version_and_scratch_queries():
 def test_bad_arguments_are_rejected_on_the_host():
     from hds_b200 import native
 
-    rc = native.lib.hds_render_features_forward(10, 24, 16, 16, None, None, None, None, None, None, None, None, None,
+    rc = native.lib.hds_render_features_forward(10, 24, 16, 16, 0, None, None, None, None, None, None, None, None, None,
                                                 None, None, None)
     assert rc == 2 and b"32, 64, 128, 256 or 512" in native.lib.hds_last_error()
-    rc = native.lib.hds_render_features_backward(10, 256, 32, 16, 16, *([None] * 14))
+    rc = native.lib.hds_render_features_backward(10, 256, 32, 16, 16, 0, *([None] * 14))
     assert rc == 2 and b"no feature backward for 256 channels in slices of 32" in native.lib.hds_last_error()
     rc = native.lib.hds_eval_sh_forward(10, 4, None, None, None, None, None, None)
     assert rc == 1 and b"degree" in native.lib.hds_last_error()
     out = ctypes.c_int64(0)
-    rc = native.lib.hds_rasterize_prepare(10, *([None] * 6), 16, 16, None, None, None, 0, ctypes.byref(out), None)
+    rc = native.lib.hds_rasterize_prepare(10, *([None] * 6), 16, 16, 0, None, None, None, 0, ctypes.byref(out), None)
     assert rc == 4 and b"scratch" in native.lib.hds_last_error()
     with pytest.raises(RuntimeError, match="scratch"):
         native.check(rc)

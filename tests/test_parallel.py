@@ -44,23 +44,26 @@ def test_bucket_zero_async_on_cpu_is_zero():
     assert torch.count_nonzero(bucket.flat) == 0
 
 
-def band_render_np(inputs, width, y0, y1, background):
+def band_render_np(inputs, width, y0, y1, background, features=None):
+    """Rows [y0, y1) of the full render: the band is an image of its own whose row 0 lies at row y0
+    of the full view (origin_y), with the means in full-image pixels."""
     m2, dep, rad, con, col, opac = inputs
-    shifted = m2 - np.array([0.0, y0], np.float32)
-    return oracle.rasterize(shifted, dep, rad, con, col, opac, width, y1 - y0, background=background)
+    return oracle.rasterize(m2, dep, rad, con, col, opac, width, y1 - y0, background=background, features=features,
+                            origin_y=y0)
 
 
 def test_bands_stitch_into_the_full_render():
+    """Pixel centres and tile rectangles in full-image coordinates make every band's outputs equal
+    its rows of the full render bit for bit, features included."""
     width, height = 96, 80
     inputs = reference_scene(5, 3000, width, height)
+    feats = np.random.default_rng(2).standard_normal((3000, 8)).astype(np.float32)
     bg = np.array([0.3, 0.5, 0.7], np.float32)
-    full = oracle.rasterize(*inputs, width, height, background=bg)
-    parts = [band_render_np(inputs, width, y0, y1, bg) for y0, y1 in parallel.row_bands(height, 3)]
-    stitched = np.concatenate([p["image"] for p in parts], axis=0)
-    # Shifting the means re-rounds them (about 1 ulp of a few hundred pixels); a pixel whose pair sits
-    # exactly on a cutoff may flip, so a tiny fraction may differ by more.
-    assert_close_abs(stitched, full["image"], 1e-5, "stitched bands")
-    assert np.array_equal(np.concatenate([p["n_contrib"] for p in parts]) > 0, full["n_contrib"] > 0)
+    full = oracle.rasterize(*inputs, width, height, background=bg, features=feats)
+    for world in (2, 3, 5):
+        parts = [band_render_np(inputs, width, y0, y1, bg, feats) for y0, y1 in parallel.row_bands(height, world)]
+        for key in ("image", "final_T", "n_contrib", "features"):
+            assert np.array_equal(np.concatenate([p[key] for p in parts], axis=0), full[key]), key
 
 
 def free_port():
@@ -93,9 +96,8 @@ def _gloo_worker(rank, world, port, out):
         y0, y1 = parallel.row_bands(height, world)[rank]
         band = band_render_np(inputs, width, y0, y1, None)
         grad_image = np.random.default_rng(3).random((height, width, 3), dtype=np.float32)
-        shifted = m2 - np.array([0.0, y0], np.float32)
-        g = oracle.render_backward(band["ranges"], band["values"], shifted, con, col, opac, width, y1 - y0,
-                                   band["final_T"], band["n_contrib"], grad_image=grad_image[y0:y1])
+        g = oracle.render_backward(band["ranges"], band["values"], m2, con, col, opac, width, y1 - y0,
+                                   band["final_T"], band["n_contrib"], grad_image=grad_image[y0:y1], origin_y=y0)
         grads = [torch.from_numpy(np.ascontiguousarray(x)) for x in g[:4]]
         for t in grads:
             dist.all_reduce(t)
@@ -135,6 +137,6 @@ def test_two_gloo_ranks_bucket_and_band_split():
     for rank in range(world):
         r = results[rank]
         assert r["bucket"]
-        assert_close_abs(r["image"], full["image"], 1e-5, "stitched bands")
+        assert np.array_equal(r["image"], full["image"]), "stitched bands differ from the full render"
         for name, got, w in zip(("means2D", "conics", "colors", "opacities"), r["grads"], want[:4]):
             assert_grads_close(got, w, name)
