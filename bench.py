@@ -51,7 +51,13 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true",
                     help="skip the channel sweep (fwd and bwd per C in the reference harness scope; 1 GPU only)")
-    return ap.parse_args()
+    ap.add_argument("--split", choices=["views", "rows"], default="views",
+                    help="views: data parallel over views (config 2/3, default); rows: one config-4 view split by "
+                         "tile rows across the ranks (4M gaussians, 1920x1080, C=512 unless overridden)")
+    args = ap.parse_args()
+    if args.split == "rows" and "--gaussians" not in sys.argv:
+        args.gaussians = 4_000_000
+    return args
 
 
 def load_peaks():
@@ -690,6 +696,123 @@ def harness_sweep(args, device, timer, peaks):
             "tile_stats": stats, "channels": rows}
 
 
+def feature_block_init(device, channels, block=1 << 16, seed=1000):
+    """Feature rows [start, end) of a table drawn N(0, 1) in fixed blocks of rows, each from its own
+    seeded device generator: the table does not depend on how it is split over ranks."""
+    import torch
+
+    def init(start, end):
+        out = torch.empty(end - start, channels, device=device)
+        for b in range(start // block, (end + block - 1) // block):
+            g = torch.Generator(device=device).manual_seed(seed + b)
+            rows = torch.randn(block, channels, generator=g, device=device)
+            lo, hi = max(start, b * block), min(end, (b + 1) * block)
+            out[lo - start:hi - start] = rows[lo - b * block:hi - b * block]
+        return out
+
+    return init
+
+
+def run_band_split(args, device, rank, world, dist, timer):
+    """--split rows: BASELINE config 4, one view split by tile rows (hds_b200.band_split).  4M gaussians
+    (80% in 200 dense clusters), one 1920x1080 view, C-channel features; every step renders the view
+    once over all ranks (strong scaling) -- projection, SH, band binning and blend, 0.8 L1 + 0.2 (1 -
+    SSIM) with the SSIM halo exchange, a fixed feature-image gradient, the backward, the feature
+    gradients combined at their owners, the geometry/SH all-reduce and both Adam steps.  Bands are
+    balanced by (tile, gaussian) pairs per tile row of a first binning pass."""
+    import torch
+
+    from hds_b200 import band_split, gaussian_rasterizer, optim, scenes
+    from hds_b200.projection import project_gaussians_raw
+
+    s = scenes.config4(0, channels=0, n=args.gaussians)
+    cam = s.cameras[0].to(device)
+    H, W, C = cam.height, cam.width, args.channels
+    op = s.opacities.clamp(1e-6, 1 - 1e-6)
+    raw = {"means": s.means, "log_scales": torch.log(s.scales), "quats": s.quats,
+           "opacity_logits": torch.log(op / (1 - op)), "sh_dc": s.sh_dc, "sh_rest": s.sh_rest}
+    raw = {k: v.to(device).contiguous().requires_grad_(True) for k, v in raw.items()}
+    with torch.no_grad():
+        m2, dep, rad, con, opa = project_gaussians_raw(raw["means"], raw["log_scales"], raw["quats"],
+                                                       raw["opacity_logits"], cam.world_to_camera, cam.fx, cam.fy,
+                                                       cam.cx, cam.cy, W, H)
+        _, _, ranges = gaussian_rasterizer.bin_gaussians(m2, dep, rad, con, opa, W, H)
+        tx = (W + 15) // 16
+        per_row = (ranges[:, 1] - ranges[:, 0]).reshape(-1, tx).sum(dim=1).double()
+        weights = (per_row + 1.0).tolist()
+    features = band_split.FeatureShards(s.n, C, rank, world, device, init=feature_block_init(device, C))
+    lrs = [optim.REFERENCE_LRS[k] * (5.0 if k == "means" else 1.0) for k in raw] + [optim.REFERENCE_LRS["features"]]
+    trainer = band_split.BandSplitTrainer(raw, features, cam, lrs, rank, world, row_weights=weights)
+    y0, y1 = trainer.y0, trainer.y1
+    gen = torch.Generator().manual_seed(7)
+    gt_host = torch.randint(0, 256, (H, W, 3), dtype=torch.uint8, generator=gen).pin_memory()
+    gt_dev = gt_host.to(device).float() / 255.0
+    fgen = torch.Generator(device=device).manual_seed(11 + rank)
+    feature_grad = torch.rand(y1 - y0, W, C, generator=fgen, device=device) / (H * W)
+
+    for _ in range(args.warmup):
+        trainer.step(gt_dev, feature_grad)
+    torch.cuda.synchronize()
+
+    def timed(e2e: bool, record_calls: bool):
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        timer.active = record_calls
+        launches0 = native_launches()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            gt = (gt_host.to(device, non_blocking=True).float() / 255.0) if e2e else gt_dev
+            loss = trainer.step(gt, feature_grad)
+            if e2e:
+                loss.item()
+        end.record()
+        torch.cuda.synchronize()
+        timer.active = False
+        timed.launches = native_launches() - launches0
+        ms = start.elapsed_time(end)
+        if dist is not None:
+            t = torch.tensor([ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = t.item()
+        return ms
+
+    clocks = ClockSampler(int(str(device).split(":")[-1]) if ":" in str(device) else 0)
+    clocks.start()
+    ms = timed(e2e=False, record_calls=True)
+    launches = timed.launches
+    clock_info = clocks.stop()
+    calls, counts = timer.totals_ms(), timer.counts()
+    ms_e2e = timed(e2e=True, record_calls=False)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": args.steps / (ms / 1000.0), "unit": "views/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "ms_per_view": ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32 (feature contractions in split bf16: hi*hi + hi*lo + lo*hi, fp32 accumulate)",
+            "data": "synthetic (seeded config-4 distribution)",
+            "config": {"workload": "config4: one 1920x1080 view split by tile rows, full fwd+bwd+Adam step",
+                       "gaussians": s.n, "channels": C, "parallelism": f"tile-row bands x{world}",
+                       "bands": trainer.bands, "l2": "inputs larger than L2 (feature table "
+                       f"{s.n * C * 4 / 1e9:.1f} GB)"},
+            "call_ms_per_step": {k: v / args.steps for k, v in sorted(calls.items(), key=lambda kv: -kv[1])},
+            "gpu_launches": launches, "clocks": clock_info,
+            "e2e": {"value": args.steps / (ms_e2e / 1000.0), "unit": "views/s",
+                    "h2d_bytes_per_step": H * W * 3, "d2h_bytes_per_step": 4},
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def native_launches():
+    from hds_b200 import native
+
+    return native.lib.hds_launch_count()
+
+
 def main():
     args = parse_args()
     rank = int(os.environ.get("RANK", "0"))
@@ -714,6 +837,9 @@ def main():
     from hds_b200 import native
 
     timer = CallTimer(native)
+    if args.split == "rows":
+        run_band_split(args, device, rank, world, dist, timer)
+        return
     wl = make_workload(args, device, rank, world)
     n = args.gaussians
 

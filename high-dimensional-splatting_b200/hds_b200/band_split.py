@@ -1,0 +1,278 @@
+"""One view split into bands of tile rows across the ranks of a process group.
+
+The tile-row form of data parallelism for a single large view (the benchmark's stress configuration:
+4M gaussians, one 1920x1080 view, C = 512 features, on N GPUs of one node).  The reference is
+single-GPU; this module is the multi-GPU plan built around its rasterizer:
+
+* Geometry and SH (59 floats per gaussian) are replicated.  Every rank projects every gaussian with
+  the full camera and evaluates its colour, then bins and renders only its band of tile rows with
+  ``origin_y`` = the band's first row, so its pixels equal those rows of the full render bit for bit.
+* The feature table (C floats per gaussian, the bulk of the model) is sharded: rank r owns the rows
+  of one contiguous block of gaussians and their Adam state (FeatureShards).  Before rendering, each
+  rank fetches the rows of the gaussians that can reach its band from their owners (all-to-all
+  "dispatch"); after the backward it sends their gradients back, and each owner adds the
+  contributions of every band (all-to-all "combine").  A gaussian that straddles a band boundary is
+  reduced by its owner; a rank moves only the rows its band needs, not the table.
+* The loss keeps the full image's value and gradient.  L1 and the feature-image gradient are sums
+  over pixels, so a band's share is its own rows.  SSIM's 11x11 window needs 5 rows of each
+  neighbouring band: ranks exchange those rows (HaloExchange), each rank's SSIM covers the windows
+  centred on its own rows, and the part of its SSIM gradient that falls on a neighbour's rows is sent
+  back to that neighbour (BandSSIM).
+* Geometry and SH gradients are partial sums over each band's pixels: one all-reduce of their flat
+  bucket gives every rank the full gradient, and every rank applies the same Adam step.
+
+Collectives are torch.distributed calls (NCCL on GPUs, gloo on CPU), issued in the same order on
+every rank.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .parallel import row_bands
+
+HALO = 5  # rows of a neighbouring band the 11x11 SSIM window reaches
+
+
+def band_reach_mask(means2D: torch.Tensor, radii: torch.Tensor, y0: int, y1: int) -> torch.Tensor:
+    """Gaussians that can touch a tile of the rows [y0, y1): visible (radius > 0) and within reach of
+    the band's tile rows.  A superset of the gaussians the band bins: the opacity-aware half-height
+    k sqrt(Sigma_yy) (k <= sqrt(2 ln 255) < 3.34) is at most 1.12 radius (radius = 3 sqrt(lambda_max)),
+    and tile rows round outwards by less than 16 pixels."""
+    reach = radii * 1.12 + 1.0
+    v = means2D[:, 1]
+    return (radii > 0) & (v + reach >= float(y0 - 16)) & (v - reach < float(y1 + 16))
+
+
+class FeatureShards:
+    """The feature table split in contiguous row blocks over the group's ranks.
+
+    rows [n_local, C] is this rank's block (a leaf: its gradient is `rows.grad`, summed over every
+    band by combine()).  dispatch(ids) returns the rows of any sorted set of global ids, fetched from
+    their owners; combine(ids, grads) adds per-row gradients into the owners' rows.grad."""
+
+    def __init__(self, n: int, channels: int, rank: int, world: int, device, group=None, init=None):
+        self.n, self.channels, self.rank, self.world, self.group = n, channels, rank, world, group
+        self.starts = [n * r // world for r in range(world + 1)]
+        self.start, self.end = self.starts[rank], self.starts[rank + 1]
+        local = self.end - self.start
+        rows = init(self.start, self.end) if init is not None else torch.zeros(local, channels)
+        self.rows = rows.to(device=device, dtype=torch.float32).contiguous().requires_grad_(True)
+        self.rows.grad = torch.zeros_like(self.rows)
+        self._bounds = torch.tensor(self.starts[1:], dtype=torch.int64, device=device)
+        self._plan = None
+
+    def _owner_counts(self, ids: torch.Tensor) -> torch.Tensor:
+        owner = torch.searchsorted(self._bounds, ids, right=True)
+        return torch.bincount(owner, minlength=self.world)
+
+    def dispatch(self, ids: torch.Tensor) -> torch.Tensor:
+        """Rows of the sorted global ids `ids` ([M] int64), in that order ([M, C])."""
+        if self.world == 1:
+            self._plan = None
+            return self.rows.detach()[ids - self.start]
+        send_counts = self._owner_counts(ids)
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        send, recv = send_counts.tolist(), recv_counts.tolist()
+        # Requests: the ids each owner must serve (sorted ids and contiguous owners keep every
+        # rank's requests in one slice of ids).
+        wanted = torch.empty(sum(recv), dtype=ids.dtype, device=ids.device)
+        dist.all_to_all_single(wanted, ids.contiguous(), output_split_sizes=recv, input_split_sizes=send,
+                               group=self.group)
+        served = self.rows.detach()[wanted - self.start].contiguous()
+        out = torch.empty(ids.numel(), self.channels, dtype=served.dtype, device=served.device)
+        dist.all_to_all_single(out, served, output_split_sizes=send, input_split_sizes=recv, group=self.group)
+        self._plan = (send, recv, wanted)
+        return out
+
+    def combine(self, ids: torch.Tensor, grads: torch.Tensor) -> None:
+        """Adds grads ([M, C], rows of the ids of the last dispatch) into the owners' rows.grad."""
+        if self.world == 1:
+            self.rows.grad.index_add_(0, ids - self.start, grads)
+            return
+        send, recv, wanted = self._plan
+        back = torch.empty(sum(recv), self.channels, dtype=grads.dtype, device=grads.device)
+        dist.all_to_all_single(back, grads.contiguous(), output_split_sizes=recv, input_split_sizes=send,
+                               group=self.group)
+        self.rows.grad.index_add_(0, wanted - self.start, back)
+
+
+class HaloExchange:
+    """Neighbouring bands' rows for a band image: extend() returns the band with up to HALO rows of the
+    band above and below it (fewer at the image's top and bottom edges); fold() takes a gradient over
+    that extended image, sends the halo rows' parts to their owners and adds what the neighbours
+    send into the band's own rows.  Every band must have at least HALO rows."""
+
+    def __init__(self, bands: list[tuple[int, int]], rank: int, group=None):
+        self.bands, self.rank, self.group = bands, rank, group
+        self.world = len(bands)
+        y0, y1 = bands[rank]
+        if y1 - y0 < HALO and self.world > 1:
+            raise ValueError(f"band {rank} has {y1 - y0} rows; the SSIM halo needs at least {HALO}")
+        self.top = HALO if rank > 0 else 0
+        self.bottom = HALO if rank < self.world - 1 else 0
+
+    def _swap(self, up: torch.Tensor | None, down: torch.Tensor | None, like: torch.Tensor):
+        """Sends `up` to the rank above and `down` to the rank below; returns what they send back."""
+        ops, from_up, from_down = [], None, None
+        shape = (HALO,) + tuple(like.shape[1:])
+        if self.rank > 0:
+            from_up = torch.empty(shape, dtype=like.dtype, device=like.device)
+            ops += [dist.P2POp(dist.isend, up.contiguous(), self.rank - 1, group=self.group),
+                    dist.P2POp(dist.irecv, from_up, self.rank - 1, group=self.group)]
+        if self.rank < self.world - 1:
+            from_down = torch.empty(shape, dtype=like.dtype, device=like.device)
+            ops += [dist.P2POp(dist.isend, down.contiguous(), self.rank + 1, group=self.group),
+                    dist.P2POp(dist.irecv, from_down, self.rank + 1, group=self.group)]
+        if ops:
+            for req in dist.batch_isend_irecv(ops):
+                req.wait()
+        return from_up, from_down
+
+    def extend(self, band: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return band
+        above, below = self._swap(band[:HALO], band[-HALO:], band)
+        parts = ([above] if above is not None else []) + [band] + ([below] if below is not None else [])
+        return torch.cat(parts, dim=0)
+
+    def fold(self, grad_ext: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return grad_ext
+        h = grad_ext.shape[0] - self.top - self.bottom
+        own = grad_ext[self.top:self.top + h].clone()
+        up = grad_ext[:self.top] if self.top else None
+        down = grad_ext[self.top + h:] if self.bottom else None
+        from_up, from_down = self._swap(up, down, grad_ext)
+        if from_up is not None:
+            own[:HALO] += from_up
+        if from_down is not None:
+            own[-HALO:] += from_down
+        return own
+
+
+class BandSSIM(torch.autograd.Function):
+    """This band's share of the full image's mean SSIM: the sum of the SSIM map over the band's own
+    rows divided by the full image's H * W * 3, computed on the band extended by the halo rows, so
+    every window sees the pixels the full image's would.  The backward keeps only the own rows'
+    windows (the neighbours' windows are theirs) and folds the halo part of the gradient back.
+
+    ssim_fns = (forward(rendered, gt) -> (map, d_mu, d_aa, d_ab), backward(grad_mean [1], rendered, gt,
+    d_mu, d_aa, d_ab) -> grad), the fused SSIM pair, whose backward scales by 1 / (rows * W * 3) of
+    the image it is given."""
+
+    @staticmethod
+    def forward(ctx, band, gt_ext, halo: HaloExchange, ssim_fns, full_height: int):
+        ext = halo.extend(band.contiguous())
+        smap, d_mu, d_aa, d_ab = ssim_fns[0](ext, gt_ext)
+        h = band.shape[0]
+        own = smap[halo.top:halo.top + h]
+        ctx.save_for_backward(ext, gt_ext, d_mu, d_aa, d_ab)
+        ctx.halo, ctx.fns, ctx.h, ctx.full_height = halo, ssim_fns, h, full_height
+        return own.sum(dtype=torch.float64).to(torch.float32) / float(full_height * band.shape[1] * 3)
+
+    @staticmethod
+    def backward(ctx, grad):
+        ext, gt_ext, d_mu, d_aa, d_ab = ctx.saved_tensors
+        halo, h = ctx.halo, ctx.h
+        keep = torch.zeros(ext.shape[0], 1, 1, dtype=ext.dtype, device=ext.device)
+        keep[halo.top:halo.top + h] = 1.0
+        # The kernel divides by the extended image's size; rescale to the full image's.
+        grad_mean = (grad.reshape(1) * (ext.shape[0] / ctx.full_height)).to(ext.dtype).contiguous()
+        g_ext = ctx.fns[1](grad_mean, ext, gt_ext, d_mu * keep, d_aa * keep, d_ab * keep)
+        return halo.fold(g_ext), None, None, None, None
+
+
+def gpu_ssim_fns():
+    """The fused SSIM kernels of this library as BandSSIM's ssim_fns."""
+    from .rasterizer import _get_rasterizer
+
+    ext = _get_rasterizer()
+    return ext.ssim_forward, ext.ssim_backward
+
+
+class BandSplitTrainer:
+    """Training steps of one view split by tile rows over the ranks of `group` (see the module
+    docstring).  Holds the replicated geometry + SH leaves with their gradient bucket and Adam, the
+    feature shards with theirs, and the band layout; step() runs one forward + backward of the view
+    and one optimizer step, and returns the full image's loss (an all-reduce of the bands' shares).
+
+    raw: dict of replicated raw parameters on this rank's device (means, log_scales, quats,
+    opacity_logits, sh_dc, sh_rest); features: FeatureShards; lrs: per-parameter learning rates
+    (raw's order, then the features')."""
+
+    def __init__(self, raw: dict, features: FeatureShards, camera, lrs: list[float], rank: int, world: int,
+                 group=None, row_weights=None):
+        from .optim import FlatAdam
+        from .parallel import GradBucket
+
+        self.raw, self.features, self.camera = raw, features, camera
+        self.rank, self.world, self.group = rank, world, group
+        self.bands = row_bands(camera.height, world, row_weights)
+        self.y0, self.y1 = self.bands[rank]
+        self.halo = HaloExchange(self.bands, rank, group)
+        self.leaves = list(raw.values())
+        self.bucket = GradBucket(self.leaves)
+        self.opt = FlatAdam(self.leaves, lrs[:len(self.leaves)], eps=1e-15, bucket=self.bucket)
+        self.feature_opt = FlatAdam([features.rows], lrs[len(self.leaves):], eps=1e-15)
+        self.full_feat = None  # [n, C] scratch: the dispatched rows at their global ids (world > 1)
+        self.ssim_fns = gpu_ssim_fns()
+
+    def _feature_table(self, ids: torch.Tensor) -> torch.Tensor:
+        f = self.features
+        if self.world == 1:
+            return f.rows  # one shard holds the whole table
+        rows = f.dispatch(ids)
+        if self.full_feat is None:
+            self.full_feat = torch.zeros(f.n, f.channels, device=rows.device).requires_grad_(True)
+            self.full_feat.grad = torch.zeros_like(self.full_feat)
+        with torch.no_grad():
+            self.full_feat.index_copy_(0, ids, rows)
+            self.full_feat.grad.index_fill_(0, ids, 0.0)
+        return self.full_feat
+
+    def step(self, gt: torch.Tensor, feature_grad: torch.Tensor) -> torch.Tensor:
+        """One forward + backward of the view and one optimizer step.  gt: the full view's [H, W, 3]
+        float ground truth (on this device; each rank reads its band and halo rows); feature_grad: the
+        fixed gradient of this band's [y1 - y0, W, C] feature image (the harness scope).  Returns the
+        full image's loss as a device scalar (summed over the ranks)."""
+        from .projection import project_gaussians_raw
+        from .rasterizer import accumulate_leaf_grads, rasterize
+        from .sh import view_colors
+
+        cam, L = self.camera, self.raw
+        H, W = cam.height, cam.width
+        y0, y1 = self.y0, self.y1
+        self.bucket.zero_async()
+        self.feature_opt.bucket.zero()
+        pose = cam.world_to_camera
+        center = -(pose[:3, :3].T @ pose[:3, 3])
+        with accumulate_leaf_grads():
+            means2D, depths, radii, conics, opacities = project_gaussians_raw(
+                L["means"], L["log_scales"], L["quats"], L["opacity_logits"], pose, cam.fx, cam.fy, cam.cx, cam.cy, W,
+                H)
+            colors = view_colors(L["sh_dc"], L["sh_rest"], L["means"], center, 3, radii)
+            with torch.no_grad():
+                ids = torch.nonzero(band_reach_mask(means2D, radii, y0, y1)).squeeze(1)
+            table = self._feature_table(ids)
+            image, feat = rasterize(means2D, depths, radii, conics, colors, opacities, W, y1 - y0,
+                                    torch.zeros(3, device=means2D.device), table, origin_y=y0)
+        e0, e1 = y0 - self.halo.top, y1 + self.halo.bottom
+        gt_band = gt[y0:y1]
+        # 0.8 L1 + 0.2 (1 - SSIM), the training loop's loss (main.py:179-182), as this band's share.
+        l1_share = (image - gt_band).abs().sum(dtype=torch.float64).to(torch.float32) / float(H * W * 3)
+        ssim_share = BandSSIM.apply(image, gt[e0:e1].contiguous(), self.halo, self.ssim_fns, H)
+        loss = 0.8 * l1_share + 0.2 * ((y1 - y0) / H - ssim_share)
+        self.bucket.ready()
+        torch.autograd.backward([loss, feat], [None, feature_grad.contiguous()])
+        # Feature gradients back to their owners; geometry and SH summed over the bands.
+        if self.world > 1:
+            self.features.combine(ids, self.full_feat.grad[ids])
+            self.bucket.all_reduce(self.group)
+        self.opt.step()
+        self.feature_opt.step()
+        total = loss.detach().reshape(1)
+        if self.world > 1:
+            dist.all_reduce(total, group=self.group)
+        return total

@@ -1,0 +1,123 @@
+"""The tile-row split's exchange logic on CPU, over three gloo ranks (hds_b200.band_split):
+
+* FeatureShards: rows dispatched from their owners equal the full table's rows; gradients combined
+  from every band land summed on the owners.
+* HaloExchange + BandSSIM (with the oracle's SSIM): the bands' shares add up to the full image's mean
+  SSIM, and the folded band gradients equal the full image's SSIM gradient row for row.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+import oracle
+from helpers import assert_grads_close
+
+WORLD = 3
+N, C = 1000, 8
+H, W = 80, 48
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def table_rows(start, end):
+    g = torch.arange(start, end, dtype=torch.float32)[:, None]
+    return g * C + torch.arange(C, dtype=torch.float32)[None, :]
+
+
+def rank_ids(rank):
+    rng = np.random.default_rng(rank)
+    return torch.from_numpy(np.unique(rng.integers(0, N, 300))).long()
+
+
+def oracle_ssim_fns():
+    def fwd(a, b):
+        return tuple(torch.from_numpy(x) for x in oracle.ssim_forward(a.detach().numpy(), b.numpy()))
+
+    def bwd(grad_mean, a, b, d_mu, d_aa, d_ab):
+        return torch.from_numpy(oracle.ssim_backward(float(grad_mean[0]), a.detach().numpy(), b.numpy(),
+                                                     d_mu.numpy(), d_aa.numpy(), d_ab.numpy()))
+
+    return fwd, bwd
+
+
+def images():
+    rng = np.random.default_rng(9)
+    gt = rng.random((H, W, 3), dtype=np.float32)
+    img = np.clip(gt + 0.2 * rng.standard_normal((H, W, 3)).astype(np.float32), 0, 1).astype(np.float32)
+    return img, gt
+
+
+def _worker(rank, port, queue):
+    import torch.distributed as dist
+
+    from hds_b200 import band_split, parallel
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    try:
+        shards = band_split.FeatureShards(N, C, rank, WORLD, "cpu", init=table_rows)
+        ids = rank_ids(rank)
+        rows = shards.dispatch(ids)
+        rows_ok = torch.equal(rows, table_rows(0, N)[ids])
+        shards.combine(ids, torch.full((len(ids), C), float(rank + 1)))
+        grads = [None] * WORLD
+        dist.all_gather_object(grads, (shards.start, shards.rows.grad.numpy().copy()))
+
+        img, gt = images()
+        bands = parallel.row_bands(H, WORLD)
+        y0, y1 = bands[rank]
+        halo = band_split.HaloExchange(bands, rank)
+        band = torch.from_numpy(img[y0:y1].copy()).requires_grad_(True)
+        gt_ext = torch.from_numpy(gt[y0 - halo.top:y1 + halo.bottom].copy())
+        share = band_split.BandSSIM.apply(band, gt_ext, halo, oracle_ssim_fns(), H)
+        share.backward()
+        shares = [None] * WORLD
+        dist.all_gather_object(shares, (float(share), band.grad.numpy().copy()))
+        queue.put((rank, {"rows_ok": rows_ok, "grads": grads, "ssim": shares}))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.fixture(scope="module")
+def results():
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_worker, args=(r, port, queue)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    out = dict(queue.get(timeout=240) for _ in range(WORLD))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    return out
+
+
+def test_feature_shards_dispatch_and_combine(results):
+    assert all(results[r]["rows_ok"] for r in range(WORLD))
+    want = np.zeros((N, C), np.float32)
+    for r in range(WORLD):
+        want[rank_ids(r).numpy()] += r + 1
+    got = np.zeros((N, C), np.float32)
+    for start, g in results[0]["grads"]:
+        got[start:start + len(g)] = g
+    assert np.array_equal(got, want)
+
+
+def test_band_ssim_matches_full_image(results):
+    img, gt = images()
+    smap, d_mu, d_aa, d_ab = oracle.ssim_forward(img, gt)
+    full_grad = oracle.ssim_backward(1.0, img, gt, d_mu, d_aa, d_ab)
+    shares = results[0]["ssim"]
+    total = sum(s for s, _ in shares)
+    np.testing.assert_allclose(total, smap.astype(np.float64).mean(), rtol=1e-6)
+    stitched = np.concatenate([g for _, g in shares], axis=0)
+    assert_grads_close(stitched, full_grad, "SSIM gradient stitched from bands")

@@ -1,0 +1,95 @@
+"""The tile-row split end to end on two GPUs (hds_b200.band_split over NCCL): one training step of a
+config-4-like view split into two bands gives the same loss and the same gradients -- geometry and SH
+after their all-reduce, features after the combine at their owners -- as the whole view on one GPU.
+Needs two GPUs; skipped otherwise."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+N, C = 60_000, 32
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _run(rank, world, port, queue):
+    import torch.distributed as dist
+
+    from hds_b200 import band_split, optim, scenes
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    device = torch.device("cuda", rank)
+    torch.cuda.set_device(device)
+    if world > 1:
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=device)
+    try:
+        s = scenes.config4(1, channels=0, n=N)
+        cam = s.cameras[0].to(device)
+        op = s.opacities.clamp(1e-6, 1 - 1e-6)
+        raw = {"means": s.means, "log_scales": torch.log(s.scales), "quats": s.quats,
+               "opacity_logits": torch.log(op / (1 - op)), "sh_dc": s.sh_dc, "sh_rest": s.sh_rest}
+        raw = {k: v.to(device).contiguous().requires_grad_(True) for k, v in raw.items()}
+        table = torch.randn(N, C, generator=torch.Generator().manual_seed(3))
+        feats = band_split.FeatureShards(N, C, rank, world, device, init=lambda a, b: table[a:b].clone())
+        lrs = [optim.REFERENCE_LRS[k] for k in raw] + [optim.REFERENCE_LRS["features"]]
+        trainer = band_split.BandSplitTrainer(raw, feats, cam, lrs, rank, world)
+        H, W = cam.height, cam.width
+        gt = torch.rand(H, W, 3, generator=torch.Generator().manual_seed(4)).to(device)
+        fgrad = torch.rand(H, W, C, generator=torch.Generator().manual_seed(5)).to(device) / (H * W)
+        loss = trainer.step(gt, fgrad[trainer.y0:trainer.y1])
+        out = {"loss": float(loss), "geometry": trainer.bucket.flat.cpu().numpy(),
+               "features": (feats.start, feats.rows.grad.cpu().numpy()), "bands": trainer.bands}
+        queue.put((rank, out))
+    finally:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+def _launch(world):
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_run, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = dict(queue.get(timeout=600) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    return out
+
+
+def test_two_band_step_matches_one_gpu():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("the tile-row split test needs two GPUs")
+    from helpers import assert_grads_close
+
+    one = _launch(1)[0]
+    two = _launch(2)
+    assert len(two[0]["bands"]) == 2
+    np.testing.assert_allclose(two[0]["loss"], one["loss"], rtol=1e-5)
+    assert two[0]["loss"] == two[1]["loss"]
+    assert np.array_equal(two[0]["geometry"], two[1]["geometry"]), "ranks disagree after the all-reduce"
+    off = 0
+    for name, width in (("means", 3), ("log_scales", 3), ("quats", 4), ("opacity_logits", 1), ("sh_dc", 3),
+                        ("sh_rest", 45)):
+        seg = slice(off, off + N * width)
+        assert_grads_close(two[0]["geometry"][seg], one["geometry"][seg], f"{name} gradients, 2 bands vs 1 GPU")
+        off += N * width
+    assert off == len(one["geometry"])
+    got = np.zeros((N, C), np.float32)
+    for r in range(2):
+        start, g = two[r]["features"]
+        got[start:start + len(g)] = g
+    assert_grads_close(got, one["features"][1], "feature gradients, 2 bands vs 1 GPU")
