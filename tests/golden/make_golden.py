@@ -2,12 +2,15 @@
 
 Run in a container that holds the reference checkout (it is not needed anywhere else):
 
-    python tests/golden/make_golden.py /path/to/high-dimensional-splatting
+    python tests/golden/make_golden.py /path/to/high-dimensional-splatting [--only model_init]
 
 It imports, from the reference:
   * tests/oracle.py::rasterize_reference       -- the fp64 dense blend (forward; autograd = backward)
   * tests/test_sh.py::eval_sh_reference        -- the term-by-term SH reference
   * gaussian_splatting/utils/loss.py::ssim     -- the torch SSIM path (CPU tensors take it)
+  * gaussian_splatting/utils/gaussian.py::GaussianModel -- the point-cloud initialisation (model_init.npz;
+    its module imports pycolmap through utils/dataset.py, which is stubbed for the import since the
+    initialisation does not use it)
 and runs them on seeded inputs.  The 2-D inputs of the projected scenes come from the oracle's
 projection (oracle/hds_oracle.c), since the reference has no CPU projection.  The fixtures hold
 inputs and reference outputs; tests/test_oracle_golden.py checks the oracle against them.
@@ -201,5 +204,35 @@ def main(root: Path) -> None:
     print("fixtures written to", HERE)
 
 
+def model_init_fixture(root: Path) -> None:
+    """GaussianModel(point_cloud, device='cpu').params of a seeded cloud of 500 points."""
+    import types
+
+    sys.path.insert(0, str(root))
+    stub = types.ModuleType("pycolmap")
+    stub.Image = stub.Reconstruction = object  # only used in annotations of the dataset loader
+    sys.modules.setdefault("pycolmap", stub)
+    from gaussian_splatting.utils.dataset import PointCloud  # type: ignore
+    from gaussian_splatting.utils.gaussian import GaussianModel  # type: ignore
+
+    rng = np.random.default_rng(77)
+    points = rng.normal(0.0, 1.5, (500, 3)).astype(np.float32)
+    points[7] = points[3]  # a duplicate point: zero distance to its nearest neighbour (the 1e-7 clamp)
+    colors = rng.random((500, 3), dtype=np.float32)
+    model = GaussianModel(PointCloud(points=points, colors=colors), device="cpu")
+    out = {"points": points, "colors": colors}
+    out.update({f"param_{k}": v.detach().numpy() for k, v in model.params.items()})
+    np.savez_compressed(HERE / "model_init.npz", **out)
+    print("model_init.npz written to", HERE)
+
+
 if __name__ == "__main__":
-    main(Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    root = Path(args[0] if args else "/root/reference")
+    if "--only" in sys.argv:
+        parts = sys.argv[sys.argv.index("--only") + 1].split(",")
+        if "model_init" in parts:
+            model_init_fixture(root)
+    else:
+        main(root)
+        model_init_fixture(root)
