@@ -780,10 +780,18 @@ def run_band_split(args, device, rank, world, dist, timer):
 
     clocks = ClockSampler(int(str(device).split(":")[-1]) if ":" in str(device) else 0)
     clocks.start()
+    trainer.timer.enabled = True
     ms = timed(e2e=False, record_calls=True)
+    trainer.timer.enabled = False
+    phases = {k: v / args.steps for k, v in trainer.timer.totals().items()}
     launches = timed.launches
     clock_info = clocks.stop()
     calls, counts = timer.totals_ms(), timer.counts()
+    band_sizes = torch.tensor([trainer.band_gaussians], device=device)
+    if dist is not None:
+        gathered = [torch.zeros_like(band_sizes) for _ in range(world)]
+        dist.all_gather(gathered, band_sizes)
+        band_sizes = torch.cat(gathered)
     ms_e2e = timed(e2e=True, record_calls=False)
     if rank == 0:
         line = {
@@ -797,6 +805,8 @@ def run_band_split(args, device, rank, world, dist, timer):
                        "bands": trainer.bands, "l2": "inputs larger than L2 (feature table "
                        f"{s.n * C * 4 / 1e9:.1f} GB)"},
             "call_ms_per_step": {k: v / args.steps for k, v in sorted(calls.items(), key=lambda kv: -kv[1])},
+            "phase_ms_per_step_rank0": phases,
+            "band_gaussians": band_sizes.tolist(),
             "gpu_launches": launches, "clocks": clock_info,
             "e2e": {"value": args.steps / (ms_e2e / 1000.0), "unit": "views/s",
                     "h2d_bytes_per_step": H * W * 3, "d2h_bytes_per_step": 4},

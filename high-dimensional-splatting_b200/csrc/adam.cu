@@ -9,10 +9,10 @@
 // update is the reference's own Adam form (sh.cu:90-102): m += (1 - b1) (g - m),
 // v = b2 v + (1 - b2) g g, p -= (lr / (1 - b1^t)) m / (sqrt(v) / sqrt(1 - b2^t) + eps).
 //
-// Layout and traffic: 16-byte loads and stores of whole float4s (grid-stride over float4 chunks, two
-// chunks in flight per thread); a chunk that straddles two segments, or the tail of a length that is
-// not a multiple of four, goes element by element.  Unaligned buffers take the element path
-// throughout.
+// Layout and traffic: 16-byte loads and stores of whole float4s (grid-stride over float4 chunks, four
+// chunks in flight per thread), with the streaming cache hint (each byte is touched once); a chunk
+// that straddles two segments, or the tail of a length that is not a multiple of four, goes element by
+// element.  Unaligned buffers take the element path throughout.
 #include <algorithm>
 
 #include "hds_common.cuh"
@@ -42,7 +42,7 @@ __device__ __forceinline__ void adam_one(float& p, float& m, float& v, float g, 
 }
 
 constexpr int ADAM_THREADS = 256;
-constexpr int ADAM_UNROLL = 2;
+constexpr int ADAM_UNROLL = 4;
 
 __global__ void __launch_bounds__(ADAM_THREADS) adam_flat_kernel(int64_t n, float* __restrict__ params,
                                                                  float* __restrict__ exp_avg,
@@ -63,10 +63,10 @@ __global__ void __launch_bounds__(ADAM_THREADS) adam_flat_kernel(int64_t n, floa
             for (int u = 0; u < ADAM_UNROLL; u++) {
                 const int64_t c = c0 + u * stride;
                 if (c < chunks) {
-                    p[u] = p4[c];
-                    m[u] = m4[c];
-                    v[u] = v4[c];
-                    g[u] = __ldg(g4 + c);
+                    p[u] = __ldcs(p4 + c);
+                    m[u] = __ldcs(m4 + c);
+                    v[u] = __ldcs(v4 + c);
+                    g[u] = __ldcs(g4 + c);
                 }
             }
 #pragma unroll
@@ -87,9 +87,9 @@ __global__ void __launch_bounds__(ADAM_THREADS) adam_flat_kernel(int64_t n, floa
                     adam_one(p[u].z, m[u].z, v[u].z, g[u].z, t.step_size[segment_of(t, e + 2)], t);
                     adam_one(p[u].w, m[u].w, v[u].w, g[u].w, t.step_size[segment_of(t, e + 3)], t);
                 }
-                p4[c] = p[u];
-                m4[c] = m[u];
-                v4[c] = v[u];
+                __stcs(p4 + c, p[u]);
+                __stcs(m4 + c, m[u]);
+                __stcs(v4 + c, v[u]);
             }
         }
         // The last n % 4 elements.

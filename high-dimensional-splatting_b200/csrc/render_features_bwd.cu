@@ -179,23 +179,37 @@ __global__ void __launch_bounds__(THREADS, 1) feature_backward_kernel(
 
         // Stage G (dL/dout of the half tile and slice) as bf16 hi + lo.  Each warp instruction
         // reads 8 pixels x 64 contiguous bytes and writes two 128-byte runs of shared memory.
+        // Two rounds of 2 x CK/16 loads, all of a round issued before its first conversion, so that each
+        // thread has 2 CK/16 loads of dL/dout in flight (the staging is bound by their latency).
+        constexpr int GROUPS = 2;
 #pragma unroll 1
-        for (int pp = 0; pp < 4; pp++) {
+        for (int pp0 = 0; pp0 < 4; pp0 += GROUPS) {
+            float4 v[GROUPS][CK / 16];
 #pragma unroll
-            for (int j = 0; j < CK / 16; j++) {
-                const int p = pp * 32 + ow * 8 + (lane >> 2);
-                const int c4 = j * 4 + (lane & 3);
+            for (int gi = 0; gi < GROUPS; gi++) {
+                const int p = (pp0 + gi) * 32 + ow * 8 + (lane >> 2);
                 const int2 lp = half_tile_pixel(p);
                 const int px = x0 + lp.x, py = y0 + lp.y;
-                float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                if (px < width && py < height)
-                    v = __ldg(reinterpret_cast<const float4*>(grad_out + ((size_t)py * width + px) * C + c0) + c4);
-                uint32_t h0, l0, h1, l1;
-                split_bf16(v.x, v.y, h0, l0);
-                split_bf16(v.z, v.w, h1, l1);
-                const uint32_t off = (c4 >> 1) * 2048 + p * 16 + (c4 & 1) * 8;
-                st_shared_v2(g_hi + off, h0, h1);
-                st_shared_v2(g_lo + off, l0, l1);
+                const bool in = px < width && py < height;
+                const float4* src = reinterpret_cast<const float4*>(grad_out + ((size_t)(in ? py : 0) * width +
+                                                                                 (in ? px : 0)) * C + c0);
+#pragma unroll
+                for (int j = 0; j < CK / 16; j++)
+                    v[gi][j] = in ? __ldg(src + j * 4 + (lane & 3)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+#pragma unroll
+            for (int gi = 0; gi < GROUPS; gi++) {
+                const int p = (pp0 + gi) * 32 + ow * 8 + (lane >> 2);
+#pragma unroll
+                for (int j = 0; j < CK / 16; j++) {
+                    const int c4 = j * 4 + (lane & 3);
+                    uint32_t h0, l0, h1, l1;
+                    split_bf16(v[gi][j].x, v[gi][j].y, h0, l0);
+                    split_bf16(v[gi][j].z, v[gi][j].w, h1, l1);
+                    const uint32_t off = (c4 >> 1) * 2048 + p * 16 + (c4 & 1) * 8;
+                    st_shared_v2(g_hi + off, h0, h1);
+                    st_shared_v2(g_lo + off, l0, l1);
+                }
             }
         }
         // The dF MMA reads 128 channel rows of G: zero the rows past the slice.

@@ -192,6 +192,87 @@ def gpu_ssim_fns():
     return ext.ssim_forward, ext.ssim_backward
 
 
+def bin_band(means2D, depths, radii, conics, colors, opacities, width: int, y0: int, y1: int):
+    """Bins the band [y0, y1) over the whole scene (no gradient) and compacts it: ids [M] (sorted global
+    ids of the gaussians in the band's lists), values [pairs] renamed to positions in ids, ranges, and
+    the packed conic / color_opacity rows of ids."""
+    from .gaussian_rasterizer import _bin
+
+    with torch.no_grad():
+        conic, co, values, ranges, _ = _bin(means2D.contiguous(), depths.contiguous(), radii.contiguous(),
+                                            conics.contiguous(), colors.contiguous(), opacities.contiguous(), width,
+                                            y1 - y0, origin_y=y0)
+        n = means2D.shape[0]
+        mask = torch.zeros(n, dtype=torch.bool, device=means2D.device)
+        mask[values.long()] = True
+        ids = torch.nonzero(mask).squeeze(1)
+        rename = torch.empty(n, dtype=torch.int32, device=means2D.device)
+        rename[ids] = torch.arange(ids.numel(), dtype=torch.int32, device=means2D.device)
+        values_c = rename[values.long()].contiguous()
+        return ids, values_c, ranges, conic[ids].contiguous(), co[ids].contiguous()
+
+
+class CompactBandRender(torch.autograd.Function):
+    """The fused RGB + feature blend of a band over the compact set of gaussians its lists hold: the
+    kernels see exactly the per-entry data and list order of the full-scene call, so the outputs are the
+    same bit for bit; the backward runs the fused walk on the compact rows and scatters the geometric
+    gradients back to the scene's rows (the feature rows' gradient stays compact, for the owners)."""
+
+    @staticmethod
+    def forward(ctx, means2D, conics, colors, opacities, rows, binned, background, width: int, y0: int, y1: int):
+        from .gaussian_rasterizer import render_binned_with_features
+
+        ids, values_c, ranges, conic_c, co_c = binned
+        m2c = means2D.detach()[ids].contiguous()
+        image, feat, final_T, n_contrib = render_binned_with_features(values_c, ranges, m2c, conic_c, co_c,
+                                                                      rows.contiguous(), background, width, y1 - y0,
+                                                                      origin_y=y0)
+        ctx.save_for_backward(m2c, conic_c, co_c, values_c, ranges, final_T, n_contrib, rows, background, ids)
+        ctx.meta = (width, y0, y1, means2D.shape[0])
+        return image, feat
+
+    @staticmethod
+    def backward(ctx, grad_image, grad_feat):
+        from .gaussian_rasterizer import rasterize_backward_fused
+
+        m2c, conic_c, co_c, values_c, ranges, final_T, n_contrib, rows, background, ids = ctx.saved_tensors
+        width, y0, y1, n = ctx.meta
+        if grad_feat is None:
+            grad_feat = torch.zeros(y1 - y0, width, rows.shape[1], device=rows.device)
+        gm, gc, gcol, go, gf = rasterize_backward_fused(
+            grad_image.contiguous() if grad_image is not None else None, background, grad_feat.contiguous(),
+            rows.contiguous(), m2c, conic_c, co_c, values_c, ranges, final_T, n_contrib, width, y1 - y0, origin_y=y0)
+        dev = rows.device
+
+        def scatter(g, width_):
+            out = torch.zeros(n, width_, device=dev)
+            return out.index_add_(0, ids, g)
+
+        g_colors = scatter(gcol, 3) if gcol is not None else torch.zeros(n, 3, device=dev)
+        return (scatter(gm, 2), scatter(gc, 3), g_colors, scatter(go, 1), gf, None, None, None, None, None)
+
+
+class PhaseTimer:
+    """CUDA events around the phases of a step (when enabled); ms per phase summed over steps."""
+
+    def __init__(self):
+        self.enabled = False
+        self.marks = []
+
+    def mark(self, name):
+        if self.enabled:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self.marks.append((name, e))
+
+    def totals(self):
+        out = {}
+        for (name, a), (_, b) in zip(self.marks, self.marks[1:]):
+            if name != "end":
+                out[name] = out.get(name, 0.0) + a.elapsed_time(b)
+        return out
+
+
 class BandSplitTrainer:
     """Training steps of one view split by tile rows over the ranks of `group` (see the module
     docstring).  Holds the replicated geometry + SH leaves with their gradient bucket and Adam, the
@@ -216,21 +297,9 @@ class BandSplitTrainer:
         self.bucket = GradBucket(self.leaves)
         self.opt = FlatAdam(self.leaves, lrs[:len(self.leaves)], eps=1e-15, bucket=self.bucket)
         self.feature_opt = FlatAdam([features.rows], lrs[len(self.leaves):], eps=1e-15)
-        self.full_feat = None  # [n, C] scratch: the dispatched rows at their global ids (world > 1)
         self.ssim_fns = gpu_ssim_fns()
-
-    def _feature_table(self, ids: torch.Tensor) -> torch.Tensor:
-        f = self.features
-        if self.world == 1:
-            return f.rows  # one shard holds the whole table
-        rows = f.dispatch(ids)
-        if self.full_feat is None:
-            self.full_feat = torch.zeros(f.n, f.channels, device=rows.device).requires_grad_(True)
-            self.full_feat.grad = torch.zeros_like(self.full_feat)
-        with torch.no_grad():
-            self.full_feat.index_copy_(0, ids, rows)
-            self.full_feat.grad.index_fill_(0, ids, 0.0)
-        return self.full_feat
+        self.timer = PhaseTimer()
+        self.band_gaussians = 0  # gaussians in this rank's band lists at the last step
 
     def step(self, gt: torch.Tensor, feature_grad: torch.Tensor) -> torch.Tensor:
         """One forward + backward of the view and one optimizer step.  gt: the full view's [H, W, 3]
@@ -241,38 +310,57 @@ class BandSplitTrainer:
         from .rasterizer import accumulate_leaf_grads, rasterize
         from .sh import view_colors
 
-        cam, L = self.camera, self.raw
+        cam, L, t = self.camera, self.raw, self.timer
         H, W = cam.height, cam.width
         y0, y1 = self.y0, self.y1
+        t.mark("clear")
         self.bucket.zero_async()
         self.feature_opt.bucket.zero()
         pose = cam.world_to_camera
         center = -(pose[:3, :3].T @ pose[:3, 3])
+        bg = torch.zeros(3, device=pose.device)
+        t.mark("project_sh")
         with accumulate_leaf_grads():
             means2D, depths, radii, conics, opacities = project_gaussians_raw(
                 L["means"], L["log_scales"], L["quats"], L["opacity_logits"], pose, cam.fx, cam.fy, cam.cx, cam.cy, W,
                 H)
             colors = view_colors(L["sh_dc"], L["sh_rest"], L["means"], center, 3, radii)
-            with torch.no_grad():
-                ids = torch.nonzero(band_reach_mask(means2D, radii, y0, y1)).squeeze(1)
-            table = self._feature_table(ids)
-            image, feat = rasterize(means2D, depths, radii, conics, colors, opacities, W, y1 - y0,
-                                    torch.zeros(3, device=means2D.device), table, origin_y=y0)
+            if self.world == 1:
+                # One band is the whole view: the plain fused path, the shard is the whole table.
+                t.mark("render")
+                image, feat = rasterize(means2D, depths, radii, conics, colors, opacities, W, H, bg,
+                                        self.features.rows)
+                ids = None
+            else:
+                t.mark("bin")
+                binned = bin_band(means2D, depths, radii, conics, colors, opacities, W, y0, y1)
+                ids = binned[0]
+                self.band_gaussians = ids.numel()
+                t.mark("dispatch")
+                rows = self.features.dispatch(ids).requires_grad_(True)
+                t.mark("render")
+                image, feat = CompactBandRender.apply(means2D, conics, colors, opacities, rows, binned, bg, W, y0,
+                                                      y1)
+        t.mark("loss")
         e0, e1 = y0 - self.halo.top, y1 + self.halo.bottom
-        gt_band = gt[y0:y1]
         # 0.8 L1 + 0.2 (1 - SSIM), the training loop's loss (main.py:179-182), as this band's share.
-        l1_share = (image - gt_band).abs().sum(dtype=torch.float64).to(torch.float32) / float(H * W * 3)
+        l1_share = (image - gt[y0:y1]).abs().sum(dtype=torch.float64).to(torch.float32) / float(H * W * 3)
         ssim_share = BandSSIM.apply(image, gt[e0:e1].contiguous(), self.halo, self.ssim_fns, H)
         loss = 0.8 * l1_share + 0.2 * ((y1 - y0) / H - ssim_share)
         self.bucket.ready()
+        t.mark("backward")
         torch.autograd.backward([loss, feat], [None, feature_grad.contiguous()])
         # Feature gradients back to their owners; geometry and SH summed over the bands.
         if self.world > 1:
-            self.features.combine(ids, self.full_feat.grad[ids])
+            t.mark("combine")
+            self.features.combine(ids, rows.grad)
+            t.mark("all_reduce")
             self.bucket.all_reduce(self.group)
+        t.mark("adam")
         self.opt.step()
         self.feature_opt.step()
         total = loss.detach().reshape(1)
         if self.world > 1:
             dist.all_reduce(total, group=self.group)
+        t.mark("end")
         return total

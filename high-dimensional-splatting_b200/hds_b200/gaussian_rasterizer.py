@@ -115,6 +115,29 @@ def rasterize_with_features(means2D, depths, radii, conics, colors, opacities, b
     return out[..., :3], feature_image, final_T, n_contrib, values, ranges, conic, color_opacity
 
 
+def render_binned_with_features(values_sorted, tile_ranges, means2D, conic, color_opacity, features, background,
+                                image_width: int, image_height: int, *, origin_y: int = 0):
+    """The fused RGB + feature blend over lists binned earlier (values_sorted, tile_ranges of an image of
+    this size and origin) and packed conic / color_opacity rows; no counterpart in the reference.  The
+    gaussian ids in values_sorted index means2D, conic, color_opacity and features, which may be any
+    compact subset of a scene's gaussians.  Returns (image [H,W,3], feature_image [H,W,D], final_T,
+    n_contrib)."""
+    if not (features.is_cuda and features.is_contiguous() and features.dtype == _F32):
+        raise RuntimeError("features must be a contiguous float32 CUDA tensor")
+    width, height = int(image_width), int(image_height)
+    dev = features.device
+    n, d = features.shape
+    out = torch.empty(height, width, 4, dtype=_F32, device=dev)
+    feature_image = torch.empty(height, width, d, dtype=_F32, device=dev)
+    final_T = torch.empty(height, width, dtype=_F32, device=dev)
+    n_contrib = torch.empty(height, width, dtype=_I32, device=dev)
+    check(lib.hds_render_features_forward(n, d, width, height, int(origin_y), ptr(tile_ranges), ptr(values_sorted),
+                                          ptr(means2D), ptr(conic), ptr(color_opacity), ptr(features),
+                                          ptr(background), ptr(feature_image), ptr(final_T), ptr(n_contrib), ptr(out),
+                                          stream_of(dev)))
+    return out[..., :3], feature_image, final_T, n_contrib
+
+
 def rasterize_backward(grad_image, means2D, conic, color_opacity, values_sorted, tile_ranges, final_transmittance,
                        n_contrib, background, image_width: int, image_height: int, *, origin_y: int = 0):
     """backward.cu:166-226.  Returns (dL/dmeans2D [N,2], dL/dconics [N,3], dL/dcolors [N,3], dL/dopacities [N,1])."""

@@ -52,6 +52,9 @@ SIGNATURES = {
     "hds_ssim_backward": [c_int, c_int, P, P, P, P, P, P, P, S],
     "hds_adam_step": [c_int64, P, P, P, P, c_int, ctypes.POINTER(c_int64), ctypes.POINTER(c_float), c_float, c_float,
                       c_float, c_float, c_float, c_float, S],
+    "hds_densify_stats": [c_int, P, P, c_int, c_int, P, P, P, S],
+    "hds_densify_apply": [c_int, c_int, c_int, ctypes.POINTER(c_int), c_int, c_int, c_float, P, P, P, P, P, P, P, P,
+                          P, S],
     "hds_device_status": [ctypes.POINTER(c_int), S],
     "hds_rasterize_bin_noalloc": [c_int, P, P, P, P, P, P, c_int, c_int, P, P, P, c_int64, P,
                                   ctypes.POINTER(c_int64), S],

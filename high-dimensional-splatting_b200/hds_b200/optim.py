@@ -83,6 +83,28 @@ class FlatAdam:
         self.bucket = bucket
         self.step_count = 0
 
+    @classmethod
+    def from_buffers(cls, shapes: list[tuple], flat: torch.Tensor, exp_avg: torch.Tensor, exp_avg_sq: torch.Tensor,
+                     lrs: list[float], step_count: int = 0, betas=(0.9, 0.999), eps: float = 1e-15) -> "FlatAdam":
+        """A FlatAdam over existing flat buffers (e.g. written by hds_densify_apply): new leaf tensors of
+        the given shapes as views of `flat`, with their own gradient bucket, and the given moments."""
+        self = cls.__new__(cls)
+        self.flat, self.exp_avg, self.exp_avg_sq = flat, exp_avg, exp_avg_sq
+        self.lrs, self.betas, self.eps, self.step_count = [float(x) for x in lrs], betas, eps, step_count
+        params, ends, off = [], [], 0
+        for shape in shapes:
+            n = 1
+            for d in shape:
+                n *= d
+            params.append(flat[off:off + n].view(shape).detach().requires_grad_(True))
+            off += n
+            ends.append(off)
+        if off != flat.numel():
+            raise ValueError("the shapes do not cover the flat buffer")
+        self.params, self.segment_ends = params, ends
+        self.bucket = GradBucket(params)
+        return self
+
     def set_lr(self, index: int, lr: float) -> None:
         self.lrs[index] = float(lr)
 

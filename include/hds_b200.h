@@ -266,6 +266,31 @@ int hds_adam_step(int64_t n, float* params, float* exp_avg, float* exp_avg_sq, c
                   const int64_t* segment_ends, const float* segment_lrs, float step, float beta1, float beta2,
                   float one_minus_beta1, float one_minus_beta2, float eps, hds_stream_t stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * Densification on the device.  Replace the host-driven torch indexing of utils/gaussian.py:143-296.
+ *
+ * hds_densify_stats (add_densification_stats, gaussian.py:143-160): for each gaussian with radius > 0,
+ * max_radii2D = max(max_radii2D, radius), grad_accum += |dL/dmeans2D * (W/2, H/2)|, denom += 1.
+ * All [n] fp32 (grad_means2D [n,2], 8-byte aligned).
+ *
+ * hds_densify_apply (the parameter and Adam surgery of _clone / _split / _prune, gaussian.py:194-296):
+ * the old and new flat buffers hold `segments` parameter tensors back to back, segment s being
+ * [n_old, widths[s]] (resp. [n_new, widths[s]]).  New row j copies old row src_row[j] of every segment
+ * of params, exp_avg and exp_avg_sq; flags[j] & HDS_DENSIFY_FRESH_STATE zeroes its moments (appended
+ * rows); flags[j] & HDS_DENSIFY_SPLIT_CHILD adds child_offset[j] (3 floats) to the means segment and
+ * sets the log-scales segment to log(exp(log_scale) / child_scale_div).  means_segment /
+ * log_scales_segment may be -1 (none).  widths is a host array; the rest are device pointers.
+ * ------------------------------------------------------------------------------------------- */
+#define HDS_DENSIFY_MAX_SEGMENTS 16
+#define HDS_DENSIFY_SPLIT_CHILD 1
+#define HDS_DENSIFY_FRESH_STATE 2
+int hds_densify_stats(int n, const float* grad_means2D, const float* radii, int width, int height, float* max_radii2D,
+                      float* grad_accum, float* denom, hds_stream_t stream);
+int hds_densify_apply(int n_old, int n_new, int segments, const int* widths, int means_segment, int log_scales_segment,
+                      float child_scale_div, const int32_t* src_row, const uint8_t* flags, const float* child_offset,
+                      const float* old_params, const float* old_exp_avg, const float* old_exp_avg_sq, float* new_params,
+                      float* new_exp_avg, float* new_exp_avg_sq, hds_stream_t stream);
+
 /* Reads and clears the device-side failure word that kernels with bounded waits set (0 = none).
  * Synchronises `stream`. */
 int hds_device_status(int* status, hds_stream_t stream);

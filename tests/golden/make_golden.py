@@ -2,13 +2,14 @@
 
 Run in a container that holds the reference checkout (it is not needed anywhere else):
 
-    python tests/golden/make_golden.py /path/to/high-dimensional-splatting [--only model_init]
+    python tests/golden/make_golden.py /path/to/high-dimensional-splatting [--only model_init,densify]
 
 It imports, from the reference:
   * tests/oracle.py::rasterize_reference       -- the fp64 dense blend (forward; autograd = backward)
   * tests/test_sh.py::eval_sh_reference        -- the term-by-term SH reference
   * gaussian_splatting/utils/loss.py::ssim     -- the torch SSIM path (CPU tensors take it)
-  * gaussian_splatting/utils/gaussian.py::GaussianModel -- the point-cloud initialisation (model_init.npz;
+  * gaussian_splatting/utils/gaussian.py::GaussianModel -- the point-cloud initialisation (model_init.npz) and
+    densify_and_prune with its Adam surgery (densify.npz; torch.normal's draws recorded;
     its module imports pycolmap through utils/dataset.py, which is stubbed for the import since the
     initialisation does not use it)
 and runs them on seeded inputs.  The 2-D inputs of the projected scenes come from the oracle's
@@ -226,6 +227,73 @@ def model_init_fixture(root: Path) -> None:
     print("model_init.npz written to", HERE)
 
 
+def densify_fixture(root: Path) -> None:
+    """GaussianModel.densify_and_prune (utils/gaussian.py:162-296) on a seeded CPU model whose sizes,
+    opacities and accumulated 2-D gradients straddle every threshold, with an Adam state from one
+    step; torch.normal's draws for the split children are recorded so that the device version can
+    be fed the same offsets."""
+    import types
+
+    sys.path.insert(0, str(root))
+    stub = types.ModuleType("pycolmap")
+    stub.Image = stub.Reconstruction = object
+    sys.modules.setdefault("pycolmap", stub)
+    from gaussian_splatting.config import TrainingParams  # type: ignore
+    from gaussian_splatting.utils.dataset import PointCloud  # type: ignore
+    from gaussian_splatting.utils.gaussian import GaussianModel  # type: ignore
+
+    torch.manual_seed(5)
+    rng = np.random.default_rng(88)
+    n = 600
+    points = rng.normal(0.0, 1.0, (n, 3)).astype(np.float32)
+    colors = rng.random((n, 3), dtype=np.float32)
+    model = GaussianModel(PointCloud(points=points, colors=colors), device="cpu")
+    params = TrainingParams()
+    extent = 2.0
+    with torch.no_grad():
+        # scales around percent_dense * extent (0.02) and 0.1 * extent; opacities around min_opacity.
+        model.params["scales"].copy_(torch.from_numpy(rng.normal(np.log(0.02), 1.2, (n, 3)).astype(np.float32)))
+        model.params["quats"].copy_(torch.from_numpy(rng.normal(0, 1, (n, 4)).astype(np.float32)))
+        model.params["opacities"].copy_(torch.from_numpy(rng.normal(-4.0, 2.0, (n, 1)).astype(np.float32)))
+        model.params["sh_rest"].copy_(torch.from_numpy(rng.normal(0, 0.1, (n, 15, 3)).astype(np.float32)))
+    optimizer = torch.optim.Adam(model.get_optimizer_params(params, extent), eps=1e-15)
+    for group in optimizer.param_groups:
+        p = group["params"][0]
+        p.grad = torch.from_numpy(rng.normal(0, 1e-3, tuple(p.shape)).astype(np.float32))
+    optimizer.step()
+    model.means2D_grad_accum = torch.from_numpy(rng.random((n, 1), dtype=np.float32) * 4e-3)
+    model.denom = torch.from_numpy(rng.integers(0, 12, (n, 1)).astype(np.float32))
+    model.max_radii2D = torch.from_numpy(rng.random(n, dtype=np.float32) * 40.0)
+    before = {f"in_param_{k}": v.detach().numpy().copy() for k, v in model.params.items()}
+    for group in optimizer.param_groups:
+        st = optimizer.state[group["params"][0]]
+        before[f"in_m_{group['name']}"] = st["exp_avg"].numpy().copy()
+        before[f"in_v_{group['name']}"] = st["exp_avg_sq"].numpy().copy()
+    stats = {"in_grad_accum": model.means2D_grad_accum.numpy().copy(), "in_denom": model.denom.numpy().copy(),
+             "in_max_radii2D": model.max_radii2D.numpy().copy()}
+    drawn = []
+    real_normal = torch.normal
+
+    def recording_normal(*a, **k):
+        out = real_normal(*a, **k)
+        drawn.append(out.detach().clone())
+        return out
+
+    torch.normal = recording_normal
+    try:
+        model.densify_and_prune(optimizer, params, extent, max_screen_size=params.max_screen_size)
+    finally:
+        torch.normal = real_normal
+    out = {**before, **stats, "extent": np.float32(extent), "normals": drawn[0].numpy()}
+    out.update({f"out_param_{k}": v.detach().numpy() for k, v in model.params.items()})
+    for group in optimizer.param_groups:
+        st = optimizer.state[group["params"][0]]
+        out[f"out_m_{group['name']}"] = st["exp_avg"].numpy()
+        out[f"out_v_{group['name']}"] = st["exp_avg_sq"].numpy()
+    np.savez_compressed(HERE / "densify.npz", **out)
+    print("densify.npz written to", HERE, {k: v.shape for k, v in out.items() if k.startswith("out_param")})
+
+
 if __name__ == "__main__":
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
     root = Path(args[0] if args else "/root/reference")
@@ -233,6 +301,9 @@ if __name__ == "__main__":
         parts = sys.argv[sys.argv.index("--only") + 1].split(",")
         if "model_init" in parts:
             model_init_fixture(root)
+        if "densify" in parts:
+            densify_fixture(root)
     else:
         main(root)
         model_init_fixture(root)
+        densify_fixture(root)

@@ -109,3 +109,18 @@ def test_adam_step_rejects_bad_tables_on_the_host():
     assert lib.hds_adam_step(5, None, None, None, None, 2, back, lrs, 1.0, *args) == 1
     zero = (ctypes.c_int64 * 1)(0)
     assert lib.hds_adam_step(0, None, None, None, None, 1, zero, lrs, 1.0, *args) == 0
+
+
+def test_densify_entry_points_reject_bad_arguments_on_the_host():
+    from hds_b200 import native
+
+    lib = native.lib
+    widths = (ctypes.c_int * 2)(3, 3)
+    assert lib.hds_densify_apply(10, 5, 0, widths, 0, 1, 1.6, *([None] * 10)) == 1
+    assert b"segments" in lib.hds_last_error()
+    assert lib.hds_densify_apply(10, 5, 2, widths, 0, 1, 0.0, *([None] * 10)) == 1
+    bad = (ctypes.c_int * 2)(4, 3)
+    assert lib.hds_densify_apply(10, 5, 2, bad, 0, 1, 1.6, *([None] * 10)) == 1
+    assert b"means segment" in lib.hds_last_error()
+    assert lib.hds_densify_apply(10, 0, 2, widths, 0, 1, 1.6, *([None] * 10)) == 0
+    assert lib.hds_densify_stats(-1, None, None, 16, 16, None, None, None, None) == 1
