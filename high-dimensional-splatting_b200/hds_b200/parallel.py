@@ -28,8 +28,11 @@ def shard_views(n_views: int, rank: int, world: int) -> list[int]:
 
 def row_bands(height: int, world: int, row_weights: list[float] | None = None) -> list[tuple[int, int]]:
     """Splits [0, height) into `world` bands of whole tile rows, balanced by per-tile-row weights
-    (e.g. the number of (tile, gaussian) pairs per tile row; uniform when None)."""
+    (e.g. the number of (tile, gaussian) pairs per tile row; uniform when None).  Every band holds at
+    least one tile row, so `world` may not exceed the view's tile rows: ValueError otherwise."""
     rows = math.ceil(height / TILE)
+    if world < 1 or world > rows:
+        raise ValueError(f"{world} bands of a {height}-row view: 1 to {rows} (its tile rows) supported")
     w = list(row_weights) if row_weights is not None else [1.0] * rows
     assert len(w) == rows
     total = sum(w)

@@ -34,6 +34,15 @@ def test_row_bands_partition_whole_tile_rows(height, world):
             assert y0 % 16 == 0 and y1 > y0
 
 
+def test_row_bands_reject_more_bands_than_tile_rows():
+    """A 2-tile-row view across 4 ranks would leave two ranks without rows: refused up front."""
+    with pytest.raises(ValueError):
+        parallel.row_bands(32, 4)
+    with pytest.raises(ValueError):
+        parallel.row_bands(17, 0)
+    assert parallel.row_bands(32, 2) == [(0, 16), (16, 32)]
+
+
 def test_bucket_zero_async_on_cpu_is_zero():
     params = [torch.randn(10, 3, requires_grad=True), torch.randn(4, requires_grad=True)]
     bucket = parallel.GradBucket(params)
