@@ -16,7 +16,10 @@
 //     compute their slice's dF^T = G^T W on the tensor cores and add it to dL/dfeatures;
 //   * block r's operand warps reduce u = dL/dalpha G over its quadrant into the geometric
 //     gradients, and with grad_image the walk also carries the RGB backward (backward.cu:7-164)
-//     for the block's pixels.
+//     for the block's pixels;
+//   * block r's drain warps move each chunk's dF out of TMEM and add it into dL/dfeatures (one
+//     coalesced reduction per entry and warp), concurrently with the operand warps' geometry and
+//     feature staging.
 // The exchanges are asynchronous stores into the peer's shared memory (st.async) that complete bytes
 // of the peer's mbarrier: the sender never waits, and the receiver's barrier phase completes once its
 // local writers have arrived (one of them posting the bytes the three peers owe) and every byte has
@@ -38,21 +41,24 @@ using namespace fbwd;
 constexpr int CLUSTER = 4;           // blocks per half tile: channel slices, and the walk's pixel quadrants
 constexpr int QPIX = PIX / CLUSTER;  // 32 pixels per quadrant
 constexpr int STAGES = 4;
-// Warp roles: pixel warps 0-7, list warp 8, operand warps 9-12, MMA warp 13.
+// Warp roles: pixel warps 0-7, list warp 8, operand warps 9-12, MMA warp 13, drain warps 14-17.
 constexpr int PIXEL_WARPS = 8, LIST_WARP = 8, OPERAND_WARP0 = 9, OPERAND_WARPS = 4, MMA_WARP = 13;
-constexpr int THREADS = (MMA_WARP + 1) * 32;
+constexpr int DRAIN_WARP0 = 14, DRAIN_WARPS = 4;
+constexpr int THREADS = (DRAIN_WARP0 + DRAIN_WARPS) * 32;
 static_assert(LIST_WARP == PIXEL_WARPS && OPERAND_WARP0 == LIST_WARP + 1 &&
-                  MMA_WARP == OPERAND_WARP0 + OPERAND_WARPS,
+                  MMA_WARP == OPERAND_WARP0 + OPERAND_WARPS && DRAIN_WARP0 == MMA_WARP + 1,
               "warp roles must partition the block");
 static_assert(PIXEL_WARPS * 32 == QPIX * 8, "eight walk threads per pixel of the quadrant");
-enum class Role { Pixel, List, Operand, Mma };
+static_assert(OPERAND_WARPS == 4 && DRAIN_WARPS == 4, "four consecutive warps reach all four TMEM lane quadrants");
+enum class Role { Pixel, List, Operand, Mma, Drain };
 __device__ __forceinline__ Role role_of(int warp) {
     return warp < PIXEL_WARPS ? Role::Pixel
            : warp == LIST_WARP ? Role::List
            : warp < OPERAND_WARP0 + OPERAND_WARPS ? Role::Operand
-                                                   : Role::Mma;
+           : warp == MMA_WARP ? Role::Mma
+                              : Role::Drain;
 }
-constexpr int OPERAND_BAR = 2;
+constexpr int OPERAND_BAR = 2, DRAIN_BAR = 3;
 constexpr int G_BYTES = PIX * 128 * 2;  // one bf16 copy of G: [c/8][p][c%8], 128 channel rows (the dF M)
 // One bf16 copy of W as [p/8][k/8][p%8][k%8], so that quadrant q is the 2 KB at 2048 q.
 constexpr int W_BYTES = PIX * KC * 2;
@@ -109,7 +115,7 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
     extern __shared__ uint8_t smem_raw[];
     __shared__ BwdChunk s_list[LIST_SLOTS];
     __shared__ uint64_t s_ready[STAGES], s_dot_full[STAGES], s_recv_full[STAGES], s_w_full[STAGES];
-    __shared__ uint64_t s_walk_done[STAGES], s_df_full[STAGES];
+    __shared__ uint64_t s_walk_done[STAGES], s_df_full[STAGES], s_tmem_free[STAGES];
     __shared__ uint64_t s_list_full[LIST_SLOTS], s_list_free[LIST_SLOTS];
     __shared__ uint32_t s_tmem;
     __shared__ int s_fail;
@@ -143,10 +149,12 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
             tc::mbar_init(&s_w_full[s], PIXEL_WARPS);     // the pixel warps writing this block's quadrant
             tc::mbar_init(&s_walk_done[s], PIXEL_WARPS);
             tc::mbar_init(&s_df_full[s], 1);
+            tc::mbar_init(&s_tmem_free[s], DRAIN_WARPS);  // every drain warp has read the chunk's dF
         }
         for (int l = 0; l < LIST_SLOTS; l++) {
             tc::mbar_init(&s_list_full[l], 1);
-            tc::mbar_init(&s_list_free[l], 1);
+            // A chunk's entries are read last by the operand warps (geometry) and the drain warps.
+            tc::mbar_init(&s_list_free[l], OPERAND_WARPS + DRAIN_WARPS);
         }
         tc::fence_mbar_init();
         s_fail = 0;
@@ -246,7 +254,7 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
 
         int n_real = -1;  // number of non-empty chunks, known once the empty chunk arrives
         for (int c = 0;; c++) {
-            if (n_real >= 0 && c - STAGES >= n_real) break;  // every chunk is drained
+            if (n_real >= 0 && c - STAGES >= n_real) break;  // every chunk's geometry is reduced
             const int s = c % STAGES, slot = c % LIST_SLOTS;
             const bool fresh = n_real < 0;
             int cnt = 0;
@@ -260,7 +268,7 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
                 }
                 if (tc::group_sync_count<OPERAND_BAR>(bad) != 0) break;
                 cnt = s_list[slot].count;
-                // Issue chunk c's feature loads now; they land while chunk c - STAGES is drained.
+                // Issue chunk c's feature loads now; they land while chunk c - STAGES's geometry is reduced.
                 const int k = ow * 8 + (lane >> 2);
                 const float4* row =
                     reinterpret_cast<const float4*>(features + (size_t)(k < cnt ? s_list[slot].id[k] : 0) * C + c0);
@@ -269,7 +277,7 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
                     fv[j] = k < cnt ? __ldg(row + j * 4 + (lane & 3)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             }
             if (c >= STAGES) {
-                // Drain chunk e = c - STAGES (stage s, list slot e % LIST_SLOTS).
+                // Geometric gradients of chunk e = c - STAGES (stage s, list slot e % LIST_SLOTS).
                 const int e = c - STAGES;
                 const BwdChunk& ce = s_list[e % LIST_SLOTS];
                 const uint32_t par = (e / STAGES) & 1;
@@ -354,39 +362,24 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
                         }
                     }
                 }
-                // dF of the chunk: wait for its MMA, then drain TMEM (lane = channel).
+                // This warp is done with the chunk's list entries (the drain warps release them too).
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&s_list_free[e % LIST_SLOTS]);
+            }
+            if (!fresh) continue;
+            if (c >= STAGES && cnt > 0) {
+                // Stage s holds chunk c - STAGES's W until its dF MMA has read it; the geometry above
+                // read it too, and the group barrier below orders those reads before the stores.
+                bool bad = false;
                 if (otid == 0) {
-                    bad = *(volatile int*)&s_fail || !tc::mbar_wait_bounded(&s_df_full[s], par, WAIT_LIMIT);
+                    bad = *(volatile int*)&s_fail ||
+                          !tc::mbar_wait_bounded(&s_df_full[s], ((c - STAGES) / STAGES) & 1, WAIT_LIMIT);
                     if (bad) s_fail = 1;
                 }
                 if (tc::group_sync_count<OPERAND_BAR>(bad) != 0) break;
-                tc::fence_after_sync();
-                float v[32];
-                tc::tmem_ld32(tmem + lane_base + 128 + s * 32, v);
-                // Transpose dF^T (lane = channel) through the stage buffer (its W has been read by the
-                // dF MMA) into one row of CK floats per entry; the TMA unit adds each row into
-                // dL/dfeatures (one bulk reduction per entry).
-                const int cl = q4 * 32 + lane;
-                if (cl < CK) {
-#pragma unroll
-                    for (int k = 0; k < KC; k++)
-                        if (k < ecnt) st_shared_f32(fw(s) + (k * CK + cl) * 4, v[k]);
-                }
-                tc::fence_before_sync();
-                tc::fence_proxy_async();  // the rows are read by the bulk reductions
-                tc::group_sync<OPERAND_BAR>();
-                if (otid < ecnt) {
-                    tc::bulk_reduce_add_f32(grad_features + (size_t)ce.id[otid] * C + c0, fw(s) + otid * CK * 4, CK * 4);
-                    tc::bulk_commit();
-                    tc::bulk_wait_read();  // the stage buffer is refilled below
-                }
-                tc::group_sync<OPERAND_BAR>();
-                if (otid == 0) tc::mbar_arrive(&s_list_free[e % LIST_SLOTS]);
             }
-            if (!fresh) continue;
             if (cnt > 0) {
-                // Chunk c's features as bf16 hi + lo (zeros past cnt).  Stage s is free: chunk
-                // c - STAGES has been drained above.
+                // Chunk c's features as bf16 hi + lo (zeros past cnt) into stage s.
                 const int k = ow * 8 + (lane >> 2);
                 const uint32_t fh = fw(s), fl = fh + K::F_BYTES;
 #pragma unroll
@@ -406,7 +399,6 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
             if (otid == 0) tc::mbar_arrive(&s_ready[s]);
             if (cnt == 0) n_real = c;
         }
-        tc::bulk_wait_all();  // every reduction into dL/dfeatures has landed
     } else if (role == Role::Mma) {
         // ------------------------------------------------------------------ MMA warp 13 (one lane)
         // Polls two queues: the dot of the next published chunk, and the dF of the oldest chunk
@@ -442,7 +434,11 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
                     }
                     progress = true;
                 }
-                if (cf < cd && tc::mbar_try_wait_cluster(&s_w_full[cf % STAGES], (cf / STAGES) & 1)) {
+                // dF of chunk cf overwrites the TMEM columns of chunk cf - STAGES: the drain warps must
+                // have read them.
+                if (cf < cd &&
+                    (cf < STAGES || tc::mbar_try_wait(&s_tmem_free[cf % STAGES], ((cf - STAGES) / STAGES) & 1)) &&
+                    tc::mbar_try_wait_cluster(&s_w_full[cf % STAGES], (cf / STAGES) & 1)) {
                     // dF^T of chunk cf = G^T W: A = G MN-major (SBO 2048 between channel blocks, LBO 128
                     // between pixel groups), B = W MN-major (SBO 128 between entry blocks, LBO 512
                     // between pixel groups).
@@ -477,6 +473,49 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
                 }
             }
             if (last_bar != nullptr && !tc::mbar_wait_bounded(last_bar, last_par, WAIT_LIMIT)) s_fail = 1;
+        }
+    } else if (role == Role::Drain) {
+        // ------------------------------------------------------------------ drain warps 14-17
+        // dF of each chunk out of TMEM (lane = channel) into dL/dfeatures: one coalesced 128-byte
+        // reduction per entry and warp.  The TMEM columns are released as soon as they are read; the
+        // reductions then run beside the next chunks' work.
+        const int q4 = warp & 3;                               // TMEM subpartition of this warp
+        const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;  // its lanes (channels of dF^T)
+        const int cl = q4 * 32 + lane;
+        float* const dst = grad_features + c0 + cl;
+        for (int e = 0;; e++) {
+            const int s = e % STAGES;
+            const uint32_t par = (e / STAGES) & 1;
+            const BwdChunk& ce = s_list[e % LIST_SLOTS];
+            // The list slot holds chunk e until these warps (and the operand warps) release it, so its
+            // barrier cannot run a phase ahead of them (the publication of the chunk to the walk could).
+            bool ok = true;
+            if (lane == 0) {
+                ok = !*(volatile int*)&s_fail &&
+                     tc::mbar_wait_bounded(&s_list_full[e % LIST_SLOTS], (e / LIST_SLOTS) & 1, WAIT_LIMIT);
+                if (!ok) s_fail = 1;
+            }
+            if (!__shfl_sync(FULL_MASK, ok, 0)) break;
+            const int ecnt = ce.count;
+            if (ecnt == 0) break;  // the empty chunk: every chunk is drained
+            if (lane == 0) {
+                ok = !*(volatile int*)&s_fail && tc::mbar_wait_bounded(&s_df_full[s], par, WAIT_LIMIT);
+                if (!ok) s_fail = 1;
+            }
+            if (!__shfl_sync(FULL_MASK, ok, 0)) break;
+            tc::fence_after_sync();
+            float v[32];
+            tc::tmem_ld32(tmem + lane_base + 128 + s * 32, v);
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&s_tmem_free[s]);
+            if (cl < CK) {
+#pragma unroll
+                for (int k = 0; k < KC; k++)
+                    if (k < ecnt && v[k] != 0.0f) atomicAdd(dst + (size_t)ce.id[k] * C, v[k]);
+            }
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&s_list_free[e % LIST_SLOTS]);
         }
     } else {  // Role::Pixel
         // ------------------------------------------------------------------ pixel warps 0-7
