@@ -102,7 +102,9 @@ __device__ __forceinline__ float4 ld_shared_f4(uint32_t addr) {
     return v;
 }
 
-template <int CK, bool RGB>
+// PACKED: the half tiles' lists were cut ahead (cut_half_tile_lists_kernel, `lists`); otherwise each
+// block's list warp cuts them from the tile lists.
+template <int CK, bool RGB, bool PACKED>
 __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) feature_backward_cluster_kernel(
     int C, int width, int height, int tiles_x, int origin_y, int helper_every, const int2* __restrict__ ranges,
     const int32_t* __restrict__ values,
@@ -110,7 +112,7 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
     const float* __restrict__ features, const float* __restrict__ final_T_in, const int32_t* __restrict__ n_contrib,
     const float* __restrict__ grad_out, float* __restrict__ grad_means2D, float* __restrict__ grad_conics,
     float* __restrict__ grad_features, float* __restrict__ grad_opacities, const float* __restrict__ grad_image,
-    const float* __restrict__ background, float* __restrict__ grad_colors) {
+    const float* __restrict__ background, float* __restrict__ grad_colors, HalfTileLists lists) {
     using K = Cfg<CK>;
     extern __shared__ uint8_t smem_raw[];
     __shared__ BwdChunk s_list[LIST_SLOTS];
@@ -169,19 +171,23 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
     const Role role = role_of(warp);
     if (role == Role::List) {
         // ------------------------------------------------------------------ list warp 8
-        // Every block of the cluster cuts the same chunks (same half tile, same inputs); the hit
+        // Every block of the cluster takes the same chunks (same half tile, same inputs); the hit
         // mask is its own quadrant's (an 8 x 4 block).
-        list_producer<RGB>(lane, x0, y0, origin_y, width, height, range, values, means2D, conic4, color_opacity, n_contrib,
-                           s_list, s_list_full, s_list_free, &s_fail, [&](BwdChunk& ch, int filled) {
-                               const bool valid = lane < filled;
-                               const float2 m = valid ? ch.mean[lane] : make_float2(0.0f, 0.0f);
-                               const float2 e = valid ? ch.ext[lane] : make_float2(-1e30f, -1e30f);
-                               const float bx0 = (float)(x0 + (rank & 1) * 8) + 0.5f;
-                               const float by0 = (float)(y0 + origin_y + (rank >> 1) * 4) + 0.5f;
-                               const unsigned mask = __ballot_sync(
-                                   FULL_MASK, valid && box_hits(m, e, bx0, bx0 + 7.0f, by0, by0 + 3.0f));
-                               if (lane == 0) ch.hits[0] = mask;
-                           });
+        auto mark_hits = [&](BwdChunk& ch, int filled) {
+            const bool valid = lane < filled;
+            const float2 m = valid ? ch.mean[lane] : make_float2(0.0f, 0.0f);
+            const float2 e = valid ? ch.ext[lane] : make_float2(-1e30f, -1e30f);
+            const float bx0 = (float)(x0 + (rank & 1) * 8) + 0.5f;
+            const float by0 = (float)(y0 + origin_y + (rank >> 1) * 4) + 0.5f;
+            const unsigned mask =
+                __ballot_sync(FULL_MASK, valid && box_hits(m, e, bx0, bx0 + 7.0f, by0, by0 + 3.0f));
+            if (lane == 0) ch.hits[0] = mask;
+        };
+        if (PACKED)
+            list_reader<RGB>(lane, half_id, range, lists, s_list, s_list_full, s_list_free, &s_fail, mark_hits);
+        else
+            list_producer<RGB>(lane, x0, y0, origin_y, width, height, range, values, means2D, conic4, color_opacity,
+                               n_contrib, s_list, s_list_full, s_list_free, &s_fail, mark_hits);
     } else if (role == Role::Operand) {
         // ------------------------------------------------------------------ operand warps 9-12
         const int otid = tid - OPERAND_WARP0 * 32, ow = otid >> 5;
@@ -564,48 +570,60 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
             return ok;
         };
 
-        for (int c = 0;; c++) {
+        // Send: this warp's 32 pixels x 16 entries of chunk c's slice dot to the quadrant's owner.
+        // Returns the chunk's entry count (0: the empty chunk, nothing sent), -1 after a timeout.
+        auto send = [&](int c) -> int {
+            const int s = c % STAGES;
+            const uint32_t par = (c / STAGES) & 1;
+            if (!warp_wait(&s_ready[s], par, false)) return -1;
+            const int cnt = s_list[c % LIST_SLOTS].count;
+            if (cnt == 0) return 0;
+            if (!warp_wait(&s_dot_full[s], par, false)) return -1;
+            tc::fence_after_sync();
+            float v[16];
+            tc::tmem_ld16(t_send + s * 32, v);
+            tc::fence_before_sync();
+            if (q == rank) {
+                // This block's own quadrant: plain stores; the first of the two warps also posts the
+                // bytes the three peers' partials will complete.
+                const uint32_t dst = recv_local + s * K::STAGE_BYTES;
+#pragma unroll
+                for (int m4 = 0; m4 < 4; m4++) {
+                    const uint32_t seg = (uint32_t)((4 * h + m4) ^ (lane & 7));
+                    st_shared_v4(dst + seg * 16, __float_as_uint(v[4 * m4]), __float_as_uint(v[4 * m4 + 1]),
+                                 __float_as_uint(v[4 * m4 + 2]), __float_as_uint(v[4 * m4 + 3]));
+                }
+                __syncwarp();
+                if (lane == 0) {
+                    if (h == 0)
+                        tc::mbar_arrive_expect_tx(&s_recv_full[s], (CLUSTER - 1) * RECV_SLICE_BYTES);
+                    else
+                        tc::mbar_arrive(&s_recv_full[s]);
+                }
+            } else {
+                const uint32_t dst = recv_dst + s * K::STAGE_BYTES, bar = recv_bar + s * 8;
+#pragma unroll
+                for (int m4 = 0; m4 < 4; m4++) {
+                    const uint32_t seg = (uint32_t)((4 * h + m4) ^ (lane & 7));
+                    tc::st_async_v4(dst + seg * 16, v[4 * m4], v[4 * m4 + 1], v[4 * m4 + 2], v[4 * m4 + 3], bar);
+                }
+            }
+            return cnt;
+        };
+
+        // Chunk c + 1's partial dots go out before chunk c is walked, so that the peers' arrive while
+        // it is.  The owner's receive buffer of chunk c + 1 last held chunk c - 3, which it has walked:
+        // a block that passed chunk c's receive barrier holds every peer's chunk-c partial, sent by
+        // each peer after its own walk of chunk c - 2.
+        int next = send(0);
+        for (int c = 0; next > 0; c++) {
             const int s = c % STAGES;
             const BwdChunk& ch = s_list[c % LIST_SLOTS];
             const uint32_t par = (c / STAGES) & 1;
-            if (!warp_wait(&s_ready[s], par, false)) break;
-            const int cnt = ch.count;
-            if (cnt == 0) break;
-            if (!warp_wait(&s_dot_full[s], par, false)) break;
-            tc::fence_after_sync();
-
-            // Send: this warp's 32 pixels x 16 entries of the slice's dot to the quadrant's owner.
-            {
-                float v[16];
-                tc::tmem_ld16(t_send + s * 32, v);
-                tc::fence_before_sync();
-                if (q == rank) {
-                    // This block's own quadrant: plain stores; the first of the two warps also posts the
-                    // bytes the three peers' partials will complete.
-                    const uint32_t dst = recv_local + s * K::STAGE_BYTES;
-#pragma unroll
-                    for (int m4 = 0; m4 < 4; m4++) {
-                        const uint32_t seg = (uint32_t)((4 * h + m4) ^ (lane & 7));
-                        st_shared_v4(dst + seg * 16, __float_as_uint(v[4 * m4]), __float_as_uint(v[4 * m4 + 1]),
-                                     __float_as_uint(v[4 * m4 + 2]), __float_as_uint(v[4 * m4 + 3]));
-                    }
-                    __syncwarp();
-                    if (lane == 0) {
-                        if (h == 0)
-                            tc::mbar_arrive_expect_tx(&s_recv_full[s], (CLUSTER - 1) * RECV_SLICE_BYTES);
-                        else
-                            tc::mbar_arrive(&s_recv_full[s]);
-                    }
-                } else {
-                    const uint32_t dst = recv_dst + s * K::STAGE_BYTES, bar = recv_bar + s * 8;
-#pragma unroll
-                    for (int m4 = 0; m4 < 4; m4++) {
-                        const uint32_t seg = (uint32_t)((4 * h + m4) ^ (lane & 7));
-                        tc::st_async_v4(dst + seg * 16, v[4 * m4], v[4 * m4 + 1], v[4 * m4 + 2], v[4 * m4 + 3], bar);
-                    }
-                }
-            }
+            const int cnt = next;
             if (!warp_wait(&s_recv_full[s], par, true)) break;
+            next = send(c + 1);
+            if (next < 0) break;
 
             // Walk: the whole dot of this thread's four entries, summed over the four slices.
             float d[4];
@@ -729,25 +747,39 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
     if (tid == 0 && s_fail) atomicExch(&g_backward_status, HDS_ERR_DEVICE);
 }
 
+// lists: half-tile lists to cut first and read (nullptr: the list warps cut them).
 template <int CK>
 int launch_backward_cluster(int D, int width, int height, int origin_y, const int32_t* tile_ranges, const int32_t* values,
                             const float* means2D, const float* conic4, const float* color_opacity,
                             const float* features, const float* final_T, const int32_t* n_contrib,
                             const float* grad_output, float* grad_features, float* grad_means2D, float* grad_conics,
                             float* grad_opacities, const float* grad_image, const float* background,
-                            float* grad_colors, cudaStream_t stream, int helper_every = 0) {
+                            float* grad_colors, cudaStream_t stream, int helper_every = 0,
+                            const HalfTileLists* lists = nullptr) {
     using K = Cfg<CK>;
-    auto kernel = grad_image != nullptr ? feature_backward_cluster_kernel<CK, true>
-                                        : feature_backward_cluster_kernel<CK, false>;
+    const bool rgb = grad_image != nullptr, packed = lists != nullptr;
+    auto kernel = rgb ? (packed ? feature_backward_cluster_kernel<CK, true, true> : feature_backward_cluster_kernel<CK, true, false>)
+                      : (packed ? feature_backward_cluster_kernel<CK, false, true> : feature_backward_cluster_kernel<CK, false, false>);
     HDS_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, K::SMEM));
     const int tx = tiles_for(width), ty = tiles_for(height);
     const int halves = 2 * tx * ty;
     const int clusters = halves - (helper_every > 1 ? halves / helper_every : 0);
+    HalfTileLists l{};
+    if (packed) {
+        l = *lists;
+        int* status = nullptr;
+        HDS_CHECK_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_backward_status));
+        cut_half_tile_lists_kernel<<<halves, CUT_THREADS, 0, stream>>>(
+            width, height, tx, origin_y, reinterpret_cast<const int2*>(tile_ranges), values,
+            reinterpret_cast<const float2*>(means2D), reinterpret_cast<const float4*>(conic4),
+            reinterpret_cast<const float4*>(color_opacity), n_contrib, l, status);
+        HDS_CHECK_LAUNCH("cut_half_tile_lists_kernel");
+    }
     kernel<<<clusters * CLUSTER, THREADS, K::SMEM, stream>>>(
         D, width, height, tx, origin_y, helper_every, reinterpret_cast<const int2*>(tile_ranges), values,
         reinterpret_cast<const float2*>(means2D), reinterpret_cast<const float4*>(conic4),
         reinterpret_cast<const float4*>(color_opacity), features, final_T, n_contrib, grad_output, grad_means2D,
-        grad_conics, grad_features, grad_opacities, grad_image, background, grad_colors);
+        grad_conics, grad_features, grad_opacities, grad_image, background, grad_colors, l);
     HDS_CHECK_LAUNCH("feature_backward_cluster_kernel");
     return HDS_OK;
 }

@@ -672,7 +672,8 @@ int features_backward(int n, int channels, int slice_width, int width, int heigh
                       const int32_t* values_sorted, const int32_t* tile_ranges, const float* final_T,
                       const int32_t* n_contrib, float* grad_features, float* grad_means2D, float* grad_conics,
                       float* grad_opacities, bool accumulate_features, const float* grad_image,
-                      const float* background, float* grad_colors, cudaStream_t stream) {
+                      const float* background, float* grad_colors, void* workspace, size_t workspace_bytes,
+                      cudaStream_t stream) {
     clear_error();
     HDS_REQUIRE(n >= 0 && width > 0 && height > 0, HDS_ERR_INVALID, "rasterize_features_backward: bad sizes");
     HDS_REQUIRE(origin_y >= 0 && origin_y % TILE == 0, HDS_ERR_INVALID,
@@ -690,6 +691,8 @@ int features_backward(int n, int channels, int slice_width, int width, int heigh
                 HDS_ERR_INVALID, "rasterize_features_backward: features, grad_output and grad_features must be 16-byte aligned");
     HDS_REQUIRE(grad_image == nullptr || (background != nullptr && grad_colors != nullptr), HDS_ERR_INVALID,
                 "rasterize_backward_fused: grad_image needs background and grad_colors");
+    HDS_REQUIRE(((uintptr_t)workspace & 255) == 0, HDS_ERR_INVALID,
+                "rasterize_backward_fused: the workspace must be 256-byte aligned");
     if (n == 0) return HDS_OK;
     if (!accumulate_features) HDS_CHECK_CUDA(cudaMemsetAsync(grad_features, 0, sizeof(float) * (size_t)n * D, stream));
     HDS_CHECK_CUDA(cudaMemsetAsync(grad_means2D, 0, sizeof(float) * 2 * (size_t)n, stream));
@@ -700,20 +703,23 @@ int features_backward(int n, int channels, int slice_width, int width, int heigh
     // any slicing.  One block per half tile and slice of min(D, 128) channels (one walk per slice), or
     // four-block clusters (slices of D / 4, one walk per pixel).
     if (cluster_backward_enabled(D)) {
+        // With a workspace the half tiles' lists are cut by one kernel ahead of the clusters.
+        const HalfTileLists lists = half_tile_lists_in(workspace, workspace_bytes, tiles_for(width) * tiles_for(height));
+        const HalfTileLists* packed = lists.capacity > 0 ? &lists : nullptr;
         const int m = helper_every();
         if (D == 512 && m > 0 && (2 * tiles_for(width) * tiles_for(height)) / m > 0) {
             return launch_with_helper(
                 stream,
                 [&](cudaStream_t st) {
-                    return clus::launch_backward_cluster<128>(D, width, height, origin_y, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, st, m);
+                    return clus::launch_backward_cluster<128>(D, width, height, origin_y, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, st, m, packed);
                 },
                 [&](cudaStream_t st) {
                     return launch_backward<128>(D, width, height, origin_y, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, st, m);
                 });
         }
         if (D == 256)
-            return clus::launch_backward_cluster<64>(D, width, height, origin_y, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);
-        return clus::launch_backward_cluster<128>(D, width, height, origin_y, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);
+            return clus::launch_backward_cluster<64>(D, width, height, origin_y, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream, 0, packed);
+        return clus::launch_backward_cluster<128>(D, width, height, origin_y, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream, 0, packed);
     }
     switch (D) {
         case 32: return launch_backward<32>(D, width, height, origin_y, tile_ranges, values_sorted, means2D, conic4, color_opacity, features, final_T, n_contrib, grad_output, grad_features, grad_means2D, grad_conics, grad_opacities, grad_image, background, grad_colors, stream);
@@ -744,7 +750,7 @@ extern "C" int hds_render_features_backward(int n, int channels, int slice_width
                                             hds_stream_t stream) {
     return features_backward(n, channels, slice_width, width, height, origin_y, grad_output, features, means2D, conic4,
                              color_opacity, values_sorted, tile_ranges, final_T, n_contrib, grad_features,
-                             grad_means2D, grad_conics, grad_opacities, false, nullptr, nullptr, nullptr, stream);
+                             grad_means2D, grad_conics, grad_opacities, false, nullptr, nullptr, nullptr, nullptr, 0, stream);
 }
 
 extern "C" int hds_render_features_backward_accumulate(int n, int channels, int slice_width, int width, int height,
@@ -757,7 +763,7 @@ extern "C" int hds_render_features_backward_accumulate(int n, int channels, int 
                                                        hds_stream_t stream) {
     return features_backward(n, channels, slice_width, width, height, origin_y, grad_output, features, means2D, conic4,
                              color_opacity, values_sorted, tile_ranges, final_T, n_contrib, grad_features,
-                             grad_means2D, grad_conics, grad_opacities, true, nullptr, nullptr, nullptr, stream);
+                             grad_means2D, grad_conics, grad_opacities, true, nullptr, nullptr, nullptr, nullptr, 0, stream);
 }
 
 extern "C" int hds_render_backward_fused(int n, int channels, int width, int height, int origin_y,
@@ -768,10 +774,15 @@ extern "C" int hds_render_backward_fused(int n, int channels, int width, int hei
                                          const int32_t* tile_ranges, const float* final_T, const int32_t* n_contrib,
                                          float* grad_colors, float* grad_features, float* grad_means2D,
                                          float* grad_conics, float* grad_opacities, int accumulate_features,
-                                         hds_stream_t stream) {
+                                         void* workspace, size_t workspace_bytes, hds_stream_t stream) {
     return features_backward(n, channels, channels < 128 ? channels : 128, width, height, origin_y,
                              grad_feature_image, features,
                              means2D, conic4, color_opacity, values_sorted, tile_ranges, final_T, n_contrib,
                              grad_features, grad_means2D, grad_conics, grad_opacities, accumulate_features != 0,
-                             grad_image, background, grad_colors, stream);
+                             grad_image, background, grad_colors, workspace, workspace_bytes, stream);
+}
+
+extern "C" size_t hds_backward_workspace_bytes(int64_t pairs, int width, int height) {
+    if (pairs < 0 || width <= 0 || height <= 0) return 0;
+    return half_tile_lists_bytes(pairs, tiles_for(width) * tiles_for(height));
 }

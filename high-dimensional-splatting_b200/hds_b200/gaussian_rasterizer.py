@@ -223,10 +223,13 @@ def rasterize_features_backward_into(grad_features, grad_output, features, means
 
 def rasterize_backward_fused(grad_image, background, grad_feature_image, features, means2D, conic, color_opacity,
                              values_sorted, tile_ranges, final_transmittance, n_contrib, image_width: int,
-                             image_height: int, grad_features_into=None, *, origin_y: int = 0):
+                             image_height: int, grad_features_into=None, *, origin_y: int = 0,
+                             half_tile_lists: bool = True):
     """The RGB and feature backward in one walk (no counterpart in the reference, which runs
     rasterize_backward and rasterize_features_backward).  grad_image may be None (no RGB terms).
     grad_features_into, if given, is an [N, D] fp32 buffer that dL/dfeatures is added to.
+    half_tile_lists: at 256 and 512 channels, cut every half tile's list in one kernel ahead of the
+    walk (a workspace of hds_backward_workspace_bytes); False lets each block cut its own.
 
     Returns (dL/dmeans2D [N,2], dL/dconics [N,3], dL/dcolors [N,3] or None, dL/dopacities [N,1],
     dL/dfeatures [N,D] or None when added into grad_features_into)."""
@@ -247,12 +250,16 @@ def rasterize_backward_fused(grad_image, background, grad_feature_image, feature
     gc = torch.empty(n, 3, dtype=_F32, device=dev)
     go = torch.empty(n, 1, dtype=_F32, device=dev)
     gcol = torch.empty(n, 3, dtype=_F32, device=dev) if grad_image is not None else None
+    ws, ws_bytes = None, 0
+    if half_tile_lists and d in (256, 512):
+        ws_bytes = int(lib.hds_backward_workspace_bytes(values_sorted.numel(), int(image_width), int(image_height)))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     check(lib.hds_render_backward_fused(
         n, d, int(image_width), int(image_height), int(origin_y), ptr(grad_image) if grad_image is not None else None,
         ptr(background) if grad_image is not None else None, ptr(grad_feature_image), ptr(features), ptr(means2D),
         ptr(conic), ptr(color_opacity), ptr(values_sorted), ptr(tile_ranges), ptr(final_transmittance),
         ptr(n_contrib), ptr(gcol) if gcol is not None else None, ptr(gf), ptr(gm), ptr(gc), ptr(go), accumulate,
-        stream_of(dev)))
+        ptr(ws), ws_bytes, stream_of(dev)))
     return gm, gc, gcol, go, (None if accumulate else gf)
 
 

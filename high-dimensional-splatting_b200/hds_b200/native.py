@@ -12,7 +12,7 @@ from ctypes import c_float, c_int, c_int64, c_size_t, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libhds_b200.so"
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 P = c_void_p  # device pointer
 S = c_void_p  # cudaStream_t
@@ -47,7 +47,8 @@ SIGNATURES = {
     "hds_render_features_backward_accumulate": [c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P,
                                                 P, P, P, S],
     "hds_render_backward_fused": [c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P,
-                                  c_int, S],
+                                  c_int, P, c_size_t, S],
+    "hds_backward_workspace_bytes": [c_int64, c_int, c_int],
     "hds_ssim_forward": [c_int, c_int, P, P, P, P, P, P, S],
     "hds_ssim_backward": [c_int, c_int, P, P, P, P, P, P, P, S],
     "hds_adam_step": [c_int64, P, P, P, P, c_int, ctypes.POINTER(c_int64), ctypes.POINTER(c_float), c_float, c_float,
@@ -65,6 +66,7 @@ SIGNATURES = {
 RESTYPES = {
     "hds_rasterize_prepare_scratch_bytes": c_size_t,
     "hds_rasterize_sort_scratch_bytes": c_size_t,
+    "hds_backward_workspace_bytes": c_size_t,
     "hds_last_error": ctypes.c_char_p,
     "hds_launch_count": ctypes.c_ulonglong,
 }

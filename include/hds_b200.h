@@ -50,7 +50,7 @@ int hds_abi_version(void);
 
 /* Number of kernels this library has launched in the process so far (all threads and devices). */
 unsigned long long hds_launch_count(void);
-#define HDS_ABI_VERSION 2
+#define HDS_ABI_VERSION 3
 
 /* ---------------------------------------------------------------------------------------------
  * Projection.  Replaces project_gaussians (projection.cu:210-231; autograd glue projection.py:25-96).
@@ -229,14 +229,24 @@ int hds_render_features_backward_accumulate(int n, int channels, int slice_width
  *  - grad_feature_image [H,W,C]: the feature terms; channels as hds_render_features_backward.
  *  - Outputs dL/dcolors [n,3], dL/dfeatures [n,C] (added to the buffer when accumulate_features is
  *    non-zero, otherwise overwritten), dL/dmeans2D [n,2], dL/dconics [n,3], dL/dopacities [n]: the
- *    sums of both passes. */
+ *    sums of both passes.
+ *  - workspace (256-byte aligned, workspace_bytes >= hds_backward_workspace_bytes(pairs, width,
+ *    height), pairs = the frame's (tile, gaussian) pair count), or NULL: at 256 and 512 channels a
+ *    first kernel cuts every half tile's list of contributing entries into it, which the walk then
+ *    streams; without it every block cuts its own list from values_sorted.  The results are the same.
+ *    A workspace too small for the frame's pairs leaves the lists empty and records HDS_ERR_TOO_LARGE
+ *    in the device status (hds_device_status). */
 int hds_render_backward_fused(int n, int channels, int width, int height, int origin_y, const float* grad_image,
                               const float* background, const float* grad_feature_image, const float* features,
                               const float* means2D, const float* conic4, const float* color_opacity,
                               const int32_t* values_sorted, const int32_t* tile_ranges, const float* final_T,
                               const int32_t* n_contrib, float* grad_colors, float* grad_features,
                               float* grad_means2D, float* grad_conics, float* grad_opacities,
-                              int accumulate_features, hds_stream_t stream);
+                              int accumulate_features, void* workspace, size_t workspace_bytes, hds_stream_t stream);
+
+/* Bytes of the hds_render_backward_fused workspace for a frame of `pairs` (tile, gaussian) pairs:
+ * 48 bytes per pair and half tile plus a count per half tile.  No counterpart in the reference. */
+size_t hds_backward_workspace_bytes(int64_t pairs, int width, int height);
 
 /* ---------------------------------------------------------------------------------------------
  * SSIM (11x11 gaussian window, sigma 1.5).  Replace ssim_forward (ssim.cu:306-338) and

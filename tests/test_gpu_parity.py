@@ -200,7 +200,7 @@ def test_fused_backward_cluster_helper_split(ext, golden, monkeypatch, name, hel
 @pytest.mark.parametrize("channels", [32, 128, 256, 512])
 @pytest.mark.parametrize("name", ["raster_ref_scene", "raster_config0", "dense_tile", "size3", "config1_20k"])
 @pytest.mark.parametrize("with_rgb", [True, False])
-def test_fused_backward(ext, golden, name, channels, with_rgb):
+def test_fused_backward(ext, golden, name, channels, with_rgb, half_tile_lists=True):
     """hds_render_backward_fused: the RGB and feature backward in one walk, against the oracle run with
     both gradients at once (and with the feature terms alone)."""
     inputs, w, h = case(name, golden)
@@ -218,7 +218,7 @@ def test_fused_backward(ext, golden, name, channels, with_rgb):
     _, _, final_T, n_contrib, values, ranges, conic, co = ext.rasterize_with_features(*t_in, f, w, h)
     got_m, got_c, got_col, got_o, got_f = ext.rasterize_backward_fused(
         cuda(grad_i)[0] if with_rgb else None, t_in[6], cuda(grad_f)[0], f, t_in[0], conic, co, values, ranges,
-        final_T, n_contrib, w, h)
+        final_T, n_contrib, w, h, half_tile_lists=half_tile_lists)
     from hds_b200.native import device_status
 
     assert device_status() == 0, "a bounded wait in the feature backward ran out"
@@ -229,6 +229,51 @@ def test_fused_backward(ext, golden, name, channels, with_rgb):
         assert_grads_close(host(got_col), gcol, "colors")
     else:
         assert got_col is None
+
+
+@pytest.mark.parametrize("channels", [256, 512])
+@pytest.mark.parametrize("name", ["raster_ref_scene", "dense_tile", "size3"])
+def test_fused_backward_blocks_cut_their_own_lists(ext, golden, monkeypatch, name, channels):
+    """Without a workspace every cluster block cuts its half tile's list from the tile list itself;
+    the gradients are the oracle's as with the lists cut ahead (256 channels on clusters too)."""
+    monkeypatch.setenv("HDS_FEATURE_BWD_CLUSTER", "1")
+    test_fused_backward(ext, golden, name, channels, True, half_tile_lists=False)
+
+
+@pytest.mark.parametrize("name", ["raster_ref_scene", "dense_tile", "size3"])
+def test_fused_backward_lists_cut_ahead_256_on_clusters(ext, golden, monkeypatch, name):
+    monkeypatch.setenv("HDS_FEATURE_BWD_CLUSTER", "1")
+    test_fused_backward(ext, golden, name, 256, True)
+
+
+def test_fused_backward_workspace_too_small_is_reported(ext, golden):
+    """A workspace without room for the frame's pairs: no list is written past it, and the device
+    status reports HDS_ERR_TOO_LARGE (the gradients are then incomplete)."""
+    import ctypes
+
+    from hds_b200.native import device_status, lib, ptr, stream_of
+
+    inputs, w, h = case("raster_ref_scene", golden)
+    feats = features_for(len(inputs[1]), 512)
+    t_in = cuda(*inputs, BACKGROUND)
+    f = cuda(feats)[0]
+    _, _, final_T, n_contrib, values, ranges, conic, co = ext.rasterize_with_features(*t_in, f, w, h)
+    n = f.shape[0]
+    full = int(lib.hds_backward_workspace_bytes(values.numel(), w, h))
+    small = full - 48 * values.numel()  # room for half the slots
+    ws = torch.zeros(full, dtype=torch.uint8, device="cuda")
+    outs = [torch.zeros(n, k, device="cuda") for k in (3, 512, 2, 3, 1)]
+    grad_f = torch.rand(h, w, 512, device="cuda")
+    assert device_status() == 0
+    rc = lib.hds_render_backward_fused(n, 512, w, h, 0, None, None, ptr(grad_f), ptr(f), ptr(t_in[0]), ptr(conic),
+                                       ptr(co), ptr(values), ptr(ranges), ptr(final_T), ptr(n_contrib), None,
+                                       *[ptr(t) for t in outs[1:]], 0, ptr(ws), ctypes.c_size_t(small),
+                                       stream_of(f.device))
+    assert rc == 0
+    assert device_status() == 5  # HDS_ERR_TOO_LARGE
+    assert device_status() == 0  # read and cleared
+    # Nothing was written past the first `small` bytes.
+    assert int(ws[small:].count_nonzero()) == 0
 
 
 def test_unsupported_widths_are_rejected(ext, golden):
