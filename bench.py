@@ -181,11 +181,17 @@ def make_workload(args, device, rank, world):
            "opacity_logits": torch.log(op / (1 - op)), "sh_dc": scene.sh_dc, "sh_rest": scene.sh_rest,
            "features": scene.features}
     leaves = {k: v.to(device).contiguous().requires_grad_(True) for k, v in raw.items()}
-    bucket = parallel.GradBucket(list(leaves.values()))
     # The step ends with the training loop's optimizer step (main.py:194): one fused Adam kernel over
     # every parameter, at the reference's learning rates (the means' scaled by a scene extent of 5).
+    # With N ranks the gradients are reduce-scattered, each rank steps its 1/N of the parameters and
+    # the stepped shards are all-gathered (ShardedFlatAdam): an all-reduce's traffic, 1/N of the
+    # optimizer's memory traffic per rank.
     lrs = [optim.REFERENCE_LRS[k] * (5.0 if k == "means" else 1.0) for k in leaves]
-    opt = optim.FlatAdam(list(leaves.values()), lrs, eps=1e-15, bucket=bucket)
+    if world > 1:
+        opt = optim.ShardedFlatAdam(list(leaves.values()), lrs, eps=1e-15)
+    else:
+        opt = optim.FlatAdam(list(leaves.values()), lrs, eps=1e-15)
+    bucket = opt.bucket
     return {"bucket": bucket, "optimizer": opt, "scene": scene, "cams": cams, "views": views, "gt_host": gt_host, "pose_host": pose_host,
             "gt_dev": [g.to(device) for g in gt_host], "pose_dev": [p.to(device) for p in pose_host],
             "feat_grad": feat_grad, "leaves": leaves, "bg": torch.zeros(3, device=device)}
@@ -231,9 +237,7 @@ def run_step(wl, dist, e2e: bool):
         else:
             pose, gt = wl["pose_dev"][i], wl["gt_dev"][i]
         losses.append(render_view(wl, i, pose, gt))
-    if dist is not None:
-        wl["bucket"].all_reduce()  # one NCCL all-reduce of every per-gaussian gradient
-    wl["optimizer"].step()
+    wl["optimizer"].step()  # with N ranks: reduce-scatter, Adam on this rank's shard, all-gather
     loss = torch.stack(losses).sum()
     if e2e:
         return loss.item()  # device -> host read of the step's result
@@ -306,7 +310,7 @@ STAGES = {
 }
 
 
-def stage_model(stage, st, C, n, rgb_terms=True):
+def stage_model(stage, st, C, n, rgb_terms=True, world=1):
     """(bound, algorithmic bytes or flops, formula) of one view's stage."""
     P, V, D, vis = st["pixels"], st["visited"], st["pairs"], st["visible"]
     if stage == "preprocess":
@@ -326,11 +330,14 @@ def stage_model(stage, st, C, n, rgb_terms=True):
     if stage in ("ssim_forward", "ssim_backward"):
         return "hbm", 72 * P, "72 B per pixel (3 channels x 4 B x 6 maps)"
     if stage == "optimizer":
+        if world > 1:  # ShardedFlatAdam: each rank steps 1/world of the parameters
+            return "hbm", 28 * (59 + C) * n / world, (f"28 B per parameter of this rank's 1/{world} shard (param, "
+                                                      "2 moments, grad in; param, 2 moments out)")
         return "hbm", 28 * (59 + C) * n, "28 B per parameter (param, 2 moments, grad in; param, 2 moments out)"
     raise KeyError(stage)
 
 
-def rooflines(call_ms, counts, launches_per_view, st, C, n, peaks):
+def rooflines(call_ms, counts, launches_per_view, st, C, n, peaks, world=1):
     """Per stage of one view (the optimizer: of one step): device time (CUDA events on the launch
     stream, per launch of each of the stage's calls, summed), algorithmic bytes or flops, and the
     fraction of the measured peak."""
@@ -339,7 +346,7 @@ def rooflines(call_ms, counts, launches_per_view, st, C, n, peaks):
         ms = sum(call_ms.get(c, 0.0) / max(1, counts.get(c, 0)) * launches_per_view.get(c, 0) for c in calls)
         if ms <= 0:
             continue
-        bound, amount, formula = stage_model(stage, st, C, n)
+        bound, amount, formula = stage_model(stage, st, C, n, world=world)
         if bound == "tensor":
             peak = peaks["bf16_tflops"] / 2.0
             ach = amount / (ms * 1e-3) / 1e12
@@ -905,7 +912,7 @@ def main():
     peaks = load_peaks()
     stats = tile_stats(wl, device)
     per_view = {k: 1 for k in calls}
-    stages = rooflines(calls, counts, per_view, stats, args.channels, n, peaks)
+    stages = rooflines(calls, counts, per_view, stats, args.channels, n, peaks, world)
     dominant = max(stages, key=lambda k: stages[k]["ms"])
     roof = dict(stages[dominant])
     roof["kernel"] = dominant + " (" + ", ".join(c for c in STAGES[dominant] if c in calls) + ")"

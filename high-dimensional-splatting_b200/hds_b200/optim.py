@@ -117,3 +117,81 @@ class FlatAdam:
         self.step_count += 1
         adam_step(self.flat, self.exp_avg, self.exp_avg_sq, self.bucket.flat, self.segment_ends, self.lrs,
                   self.step_count, self.betas, self.eps)
+
+
+def shard_segments(segment_ends, lo: int, length: int) -> list[int]:
+    """The segment ends of a flat buffer's slice [lo, lo + length), relative to the slice; the last
+    segment is extended to the slice's end (zero padding past the parameters steps as a no-op)."""
+    ends = [min(max(int(e) - lo, 0), length) for e in segment_ends]
+    ends[-1] = length
+    return ends
+
+
+class ShardedFlatAdam:
+    """FlatAdam for data parallelism over a process group: each rank steps 1/world of the flat
+    parameter buffer.
+
+    step() reduce-scatters the gradient bucket (every rank receives the sum over ranks of its shard),
+    runs the Adam kernel over its shard with its own shard of both moments, and all-gathers the
+    stepped shards back into every rank's full parameter buffer.  On the wire this is an all-reduce
+    (a reduce-scatter plus an all-gather); the optimizer's memory traffic and the moments' storage
+    per rank are 1/world of FlatAdam's.  Element for element the update is FlatAdam's applied to the
+    all-reduced gradients."""
+
+    ALIGN = 64  # elements: shards start on 256-byte boundaries
+
+    def __init__(self, params: list[torch.Tensor], lrs: list[float], group=None, betas=(0.9, 0.999),
+                 eps: float = 1e-15):
+        import torch.distributed as dist
+
+        if not params or len(params) != len(lrs):
+            raise ValueError("one learning rate per parameter")
+        if len(params) > MAX_SEGMENTS:
+            raise ValueError(f"at most {MAX_SEGMENTS} parameters")
+        dev = params[0].device
+        for p in params:
+            if not (p.is_leaf and p.dtype == torch.float32 and p.device == dev):
+                raise ValueError("parameters must be float32 leaves on one device")
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.params, self.lrs, self.betas, self.eps = params, [float(x) for x in lrs], betas, eps
+        n = sum(p.numel() for p in params)
+        per = -(-n // self.world)
+        self.shard = -(-per // self.ALIGN) * self.ALIGN
+        padded = self.shard * self.world
+        with torch.no_grad():
+            self.flat = torch.zeros(padded, dtype=torch.float32, device=dev)
+            ends, off = [], 0
+            for p in params:
+                k = p.numel()
+                self.flat[off:off + k].copy_(p.detach().reshape(-1))
+                p.data = self.flat[off:off + k].view_as(p)
+                off += k
+                ends.append(off)
+        self.segment_ends = ends
+        self.bucket = GradBucket(params, capacity=padded)
+        self.lo = self.rank * self.shard
+        self.local_ends = shard_segments(ends, self.lo, self.shard)
+        self.exp_avg = torch.zeros(self.shard, dtype=torch.float32, device=dev)
+        self.exp_avg_sq = torch.zeros_like(self.exp_avg)
+        self.grad_shard = torch.empty_like(self.exp_avg)
+        self.step_count = 0
+
+    def set_lr(self, index: int, lr: float) -> None:
+        self.lrs[index] = float(lr)
+
+    def zero_grad(self) -> None:
+        self.bucket.zero()
+
+    @torch.no_grad()
+    def step(self) -> None:
+        import torch.distributed as dist
+
+        self.bucket.ready()
+        dist.reduce_scatter_tensor(self.grad_shard, self.bucket.flat, group=self.group)
+        self.step_count += 1
+        mine = self.flat[self.lo:self.lo + self.shard]
+        adam_step(mine, self.exp_avg, self.exp_avg_sq, self.grad_shard, self.local_ends, self.lrs, self.step_count,
+                  self.betas, self.eps)
+        dist.all_gather_into_tensor(self.flat, mine, group=self.group)

@@ -71,10 +71,12 @@ class GradBucket:
     attach() points every parameter's .grad at its slice, so autograd accumulates in place across
     views; all_reduce() then sums all gradients over ranks with a single collective."""
 
-    def __init__(self, params: list[torch.Tensor]):
+    def __init__(self, params: list[torch.Tensor], capacity: int = 0):
+        """capacity: the flat buffer's length when it must exceed the parameters' (zero padding at
+        the end, e.g. to split it evenly across ranks)."""
         self.params = params
         total = sum(p.numel() for p in params)
-        self.flat = torch.zeros(total, dtype=torch.float32, device=params[0].device)
+        self.flat = torch.zeros(max(total, capacity), dtype=torch.float32, device=params[0].device)
         self.views = []
         off = 0
         for p in params:

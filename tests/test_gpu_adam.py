@@ -79,3 +79,42 @@ def test_adam_step_unaligned_buffers_take_the_element_path():
         want_p[a:b] = oracle.adam(p0[a:b], np.zeros(b - a, np.float32), np.zeros(b - a, np.float32), g0[a:b], 1, lr,
                                   0.9, 0.999, 1e-15)[0]
     assert np.array_equal(bufs[0].cpu().numpy(), want_p)
+
+
+def test_sharded_flat_adam_on_one_rank_equals_flat_adam():
+    """ShardedFlatAdam over a one-rank NCCL group (the reduce-scatter and all-gather are copies, the
+    padded shard holds every parameter) steps exactly as FlatAdam: three steps, bit for bit.  The
+    sharding across ranks is checked with gloo ranks on the CPU."""
+    import os
+    import socket
+
+    import torch.distributed as dist
+
+    from hds_b200.optim import FlatAdam, ShardedFlatAdam
+
+    if dist.is_initialized():
+        pytest.skip("a process group is already initialised in this process")
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("nccl", rank=0, world_size=1, device_id=torch.device("cuda", 0))
+    try:
+        a, b = _leaves(3), _leaves(3)
+        flat = FlatAdam(a, LRS, eps=1e-15)
+        sharded = ShardedFlatAdam(b, LRS, eps=1e-15)
+        assert sharded.shard % 64 == 0 and sharded.shard >= flat.flat.numel()
+        for step in range(1, 4):
+            grads = _grads(3, step)
+            flat.zero_grad()
+            sharded.zero_grad()
+            for p, q, gr in zip(a, b, grads):
+                p.grad.add_(gr)
+                q.grad.add_(gr)
+            flat.step()
+            sharded.step()
+        torch.cuda.synchronize()
+        for p, q in zip(a, b):
+            assert torch.equal(p.detach(), q.detach())
+    finally:
+        dist.destroy_process_group()

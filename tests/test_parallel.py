@@ -149,3 +149,74 @@ def test_two_gloo_ranks_bucket_and_band_split():
         assert np.array_equal(r["image"], full["image"]), "stitched bands differ from the full render"
         for name, got, w in zip(("means2D", "conics", "colors", "opacities"), r["grads"], want[:4]):
             assert_grads_close(got, w, name)
+
+
+def _adam_reference(params, exp_avg, exp_avg_sq, grads, segment_ends, segment_lrs, step, betas=(0.9, 0.999),
+                    eps=1e-15):
+    """The Adam element update of hds_adam_step in torch (CPU stand-in for the kernel in the host-logic
+    test below; the kernel itself is checked against torch.optim.Adam on the GPU)."""
+    b1, b2 = betas
+    start = 0
+    for end, lr in zip(segment_ends, segment_lrs):
+        sl = slice(start, int(end))
+        g = grads[sl]
+        exp_avg[sl] += (1.0 - b1) * (g - exp_avg[sl])
+        exp_avg_sq[sl] = b2 * exp_avg_sq[sl] + (1.0 - b2) * g * g
+        step_size = lr / (1.0 - b1 ** step)
+        params[sl] -= step_size * exp_avg[sl] / (exp_avg_sq[sl].sqrt() / (1.0 - b2 ** step) ** 0.5 + eps)
+        start = int(end)
+
+
+def _sharded_adam_worker(rank, world, port, queue):
+    import torch.distributed as dist
+
+    from hds_b200 import optim
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        optim.adam_step = _adam_reference  # the kernel needs a GPU; the host logic is under test
+        gen = torch.Generator().manual_seed(5)
+        shapes = [(1001, 3), (77,), (513, 16)]
+        params = [torch.randn(s, generator=gen).requires_grad_(True) for s in shapes]
+        opt = optim.ShardedFlatAdam(params, [1e-3, 2e-2, 5e-4], group=None)
+        grads_seen = []
+        for step in range(3):
+            opt.zero_grad()
+            for p in params:
+                g = torch.randn(p.shape, generator=torch.Generator().manual_seed(100 * step + rank + 7))
+                p.grad.add_(g)
+            grads_seen.append(torch.cat([p.grad.reshape(-1).clone() for p in params]))
+            opt.step()
+        queue.put((rank, [p.detach().clone() for p in params], grads_seen, opt.shard, opt.world))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_adam_over_two_gloo_ranks_equals_adam_on_summed_gradients():
+    """Reduce-scatter, per-rank Adam over its shard and all-gather give every rank the parameters of
+    one Adam step on the all-reduced gradients, three steps in a row (segments crossing shard
+    boundaries, padding at the end)."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_sharded_adam_worker, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {r: (ps, gs, shard, w) for r, ps, gs, shard, w in (queue.get(timeout=240) for _ in range(world))}
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert results[0][2] % 64 == 0 and results[0][2] * world >= 1001 * 3 + 77 + 513 * 16
+    gen = torch.Generator().manual_seed(5)
+    shapes = [(1001, 3), (77,), (513, 16)]
+    ref = torch.cat([torch.randn(s, generator=gen).reshape(-1) for s in shapes])
+    m, v = torch.zeros_like(ref), torch.zeros_like(ref)
+    ends = list(np.cumsum([int(np.prod(s)) for s in shapes]))
+    for step in range(3):
+        g = results[0][1][step] + results[1][1][step]
+        _adam_reference(ref, m, v, g, ends, [1e-3, 2e-2, 5e-4], step + 1)
+    for r in range(world):
+        got = torch.cat([p.reshape(-1) for p in results[r][0]])
+        assert torch.equal(got, ref), f"rank {r}: max diff {float((got - ref).abs().max())}"
