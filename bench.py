@@ -286,12 +286,16 @@ def projected_stats(means2D, depths, radii, conics, opacities, cam, device):
             "visible": int((radii > 0).sum())}
 
 
-# DRAM traffic per launch of the dominant call (dram__bytes_read.sum + dram__bytes_write.sum), from
-# one-pass ncu captures of two small cases of this bench's workload (one view, the bench's C, N
-# gaussians), fitted as a + b N and evaluated at the bench's N: the per-pixel terms (dL/dout, the
-# image) do not grow with N, the per-gaussian ones do.  (call, channels) -> (a bytes, b bytes per
-# gaussian, summary under profiles/).
-TRAFFIC_FIT = {}
+# DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum), from one-pass ncu captures of
+# two small cases of this bench's workload (one view, C = 512, 100K and 300K gaussians), fitted as
+# a + b V in the visited (tile, gaussian) pairs V and evaluated at the run's V: the per-pixel terms
+# (dL/dout, the image) are the constant, the feature rows read and reduced per visited pair the slope.
+# The backward's figure is the cluster kernel plus its one-block helper.  (call, channels) ->
+# (a bytes, b bytes per visited pair, summary under profiles/).
+TRAFFIC_FIT = {
+    ("hds_render_backward_fused", 512): (0.978e9, 2585.0, "profiles/feature_backward_traffic_fit_c512.md"),
+    ("hds_render_features_forward", 512): (0.966e9, 907.0, "profiles/feature_backward_traffic_fit_c512.md"),
+}
 
 # The algorithmic model of each stage of one view (the hot-path table's measurement row): bytes that
 # must cross HBM, or tensor flops for the feature blend.  P pixels, V visited (tile, gaussian) pairs
@@ -920,8 +924,9 @@ def main():
     for call in STAGES[dominant]:
         fit = TRAFFIC_FIT.get((call, args.channels))
         if fit is not None and call in calls:
-            roof["traffic"] = fit[0] + fit[1] * n
-            roof["traffic_source"] = f"a + b N fitted to two small one-pass captures, {fit[2]}"
+            roof["traffic"] = fit[0] + fit[1] * stats["visited"]
+            roof["traffic_source"] = (f"a + b V (V = {stats['visited']} visited pairs) fitted to two small one-pass "
+                                      f"captures, {fit[2]}")
     line = {
         "metric": METRIC, "value": value, "unit": "views/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "ms_per_view": ms / (args.steps * args.views),
