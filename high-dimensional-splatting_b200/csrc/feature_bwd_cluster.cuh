@@ -7,7 +7,8 @@
 // Block r of the cluster owns channel slice r (CK = C / 4 channels) and pixel quadrant r (32 of the
 // half tile's 128 pixels, TMEM lanes 32r..32r+31):
 //   * each block computes its slice's dot for all 128 pixels on the tensor cores (split bf16, as the
-//     one-block kernel) and sends quadrant q of it to block q over distributed shared memory;
+//     one-block kernel), and its drain warp q sends quadrant q of it to block q over distributed
+//     shared memory as soon as it is in TMEM, chunks ahead of the walk;
 //   * block r adds the four partial dots of its quadrant and walks its 32 pixels with eight
 //     threads per pixel: each thread takes four consecutive entries of the 32-entry chunk, the
 //     eight segments are joined by a scan of their affine maps (T_out = P T_in,
@@ -17,9 +18,9 @@
 //   * block r's operand warps reduce u = dL/dalpha G over its quadrant into the geometric
 //     gradients, and with grad_image the walk also carries the RGB backward (backward.cu:7-164)
 //     for the block's pixels;
-//   * block r's drain warps move each chunk's dF out of TMEM and add it into dL/dfeatures (one
-//     coalesced reduction per entry and warp), concurrently with the operand warps' geometry and
-//     feature staging.
+//   * block r's drain warps also move each chunk's dF out of TMEM and add it into dL/dfeatures
+//     (one coalesced reduction per entry and warp), concurrently with the operand warps' geometry
+//     and feature staging.
 // The exchanges are asynchronous stores into the peer's shared memory (st.async) that complete bytes
 // of the peer's mbarrier: the sender never waits, and the receiver's barrier phase completes once its
 // local writers have arrived (one of them posting the bytes the three peers owe) and every byte has
@@ -147,7 +148,7 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
         for (int s = 0; s < STAGES; s++) {
             tc::mbar_init(&s_ready[s], 1);
             tc::mbar_init(&s_dot_full[s], 1);
-            tc::mbar_init(&s_recv_full[s], 2);            // the two warps sending this block's own quadrant
+            tc::mbar_init(&s_recv_full[s], 1);            // the drain warp storing this block's own quadrant
             tc::mbar_init(&s_w_full[s], PIXEL_WARPS);     // the pixel warps writing this block's quadrant
             tc::mbar_init(&s_walk_done[s], PIXEL_WARPS);
             tc::mbar_init(&s_df_full[s], 1);
@@ -482,51 +483,96 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
         }
     } else if (role == Role::Drain) {
         // ------------------------------------------------------------------ drain warps 14-17
-        // dF of each chunk out of TMEM (lane = channel) into dL/dfeatures: one coalesced 128-byte
-        // reduction per entry and warp.  The TMEM columns are released as soon as they are read; the
-        // reductions then run beside the next chunks' work.
-        const int q4 = warp & 3;                               // TMEM subpartition of this warp
-        const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;  // its lanes (channels of dF^T)
+        // Warp q (= warp & 3, its TMEM lane quadrant) has two jobs, polled in turn:
+        //  * send: as soon as chunk x's dot is in TMEM, its quadrant q (32 pixels x 32 entries of this
+        //    block's channel slice) goes to block q -- into this block's own receive buffer when
+        //    q == rank, else by st.async into the peer's.  The owner's buffer of chunk x last held
+        //    chunk x - STAGES, which it has walked: the dot of chunk x needed this block's stage,
+        //    whose W of chunk x - STAGES came from every block's walk of that chunk.
+        //  * drain: chunk e's dF out of TMEM (lane = channel) into dL/dfeatures, one coalesced
+        //    128-byte reduction per entry.  The TMEM columns are released as soon as they are read.
+        const int q4 = warp & 3;
+        const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
         const int cl = q4 * 32 + lane;
         float* const dst = grad_features + c0 + cl;
-        for (int e = 0;; e++) {
-            const int s = e % STAGES;
-            const uint32_t par = (e / STAGES) & 1;
-            const BwdChunk& ce = s_list[e % LIST_SLOTS];
-            // The list slot holds chunk e until these warps (and the operand warps) release it, so its
-            // barrier cannot run a phase ahead of them (the publication of the chunk to the walk could).
-            bool ok = true;
-            if (lane == 0) {
-                ok = !*(volatile int*)&s_fail &&
-                     tc::mbar_wait_bounded(&s_list_full[e % LIST_SLOTS], (e / LIST_SLOTS) & 1, WAIT_LIMIT);
-                if (!ok) s_fail = 1;
-            }
-            if (!__shfl_sync(FULL_MASK, ok, 0)) break;
-            const int ecnt = ce.count;
-            if (ecnt == 0) break;  // the empty chunk: every chunk is drained
-            if (lane == 0) {
-                ok = !*(volatile int*)&s_fail && tc::mbar_wait_bounded(&s_df_full[s], par, WAIT_LIMIT);
-                if (!ok) s_fail = 1;
-            }
-            if (!__shfl_sync(FULL_MASK, ok, 0)) break;
-            tc::fence_after_sync();
-            float v[32];
-            tc::tmem_ld32(tmem + lane_base + 128 + s * 32, v);
-            tc::fence_before_sync();
-            __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&s_tmem_free[s]);
-            if (cl < CK) {
+        // Where this lane's partial goes: owner q4's receive buffer, slice `rank`, pixel `lane`.
+        const uint32_t recv_local = recv(0) + rank * RECV_SLICE_BYTES + lane * 128;
+        const uint32_t recv_dst = tc::map_shared(recv_local, q4);
+        const uint32_t recv_bar = tc::map_shared(tc::smem_addr(&s_recv_full[0]), q4);
+        auto poll = [&](uint64_t* bar, uint32_t par) {
+            int done = 0;
+            if (lane == 0) done = tc::mbar_try_wait(bar, par) ? 1 : 0;
+            return __shfl_sync(FULL_MASK, done, 0) != 0;
+        };
+        int xs = 0, e = 0, n_end = -1;
+        uint32_t idle = 0;
+        while (n_end < 0 || e < n_end) {
+            if (*(volatile int*)&s_fail) break;
+            bool progress = false;
+            // The list slot of a chunk is released by these warps (and the operand warps) after its
+            // drain, so its barrier cannot run a phase ahead of them.
+            if (n_end < 0 && poll(&s_list_full[xs % LIST_SLOTS], (xs / LIST_SLOTS) & 1)) {
+                if (s_list[xs % LIST_SLOTS].count == 0) {
+                    n_end = xs;
+                    progress = true;
+                } else if (poll(&s_dot_full[xs % STAGES], (xs / STAGES) & 1)) {
+                    const int s = xs % STAGES;
+                    tc::fence_after_sync();
+                    float v[32];
+                    tc::tmem_ld32(tmem + lane_base + s * 32, v);
+                    tc::fence_before_sync();
+                    if (q4 == rank) {
+                        const uint32_t d = recv_local + s * K::STAGE_BYTES;
 #pragma unroll
-                for (int k = 0; k < KC; k++)
-                    if (k < ecnt && v[k] != 0.0f) atomicAdd(dst + (size_t)ce.id[k] * C, v[k]);
+                        for (int m8 = 0; m8 < 8; m8++) {
+                            const uint32_t seg = (uint32_t)(m8 ^ (lane & 7));
+                            st_shared_v4(d + seg * 16, __float_as_uint(v[4 * m8]), __float_as_uint(v[4 * m8 + 1]),
+                                         __float_as_uint(v[4 * m8 + 2]), __float_as_uint(v[4 * m8 + 3]));
+                        }
+                        __syncwarp();
+                        if (lane == 0) tc::mbar_arrive_expect_tx(&s_recv_full[s], (CLUSTER - 1) * RECV_SLICE_BYTES);
+                    } else {
+                        const uint32_t d = recv_dst + s * K::STAGE_BYTES, bar = recv_bar + s * 8;
+#pragma unroll
+                        for (int m8 = 0; m8 < 8; m8++) {
+                            const uint32_t seg = (uint32_t)(m8 ^ (lane & 7));
+                            tc::st_async_v4(d + seg * 16, v[4 * m8], v[4 * m8 + 1], v[4 * m8 + 2], v[4 * m8 + 3], bar);
+                        }
+                    }
+                    xs++;
+                    progress = true;
+                }
             }
-            __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&s_list_free[e % LIST_SLOTS]);
+            if (e < xs && poll(&s_df_full[e % STAGES], (e / STAGES) & 1)) {
+                const int s = e % STAGES;
+                const BwdChunk& ce = s_list[e % LIST_SLOTS];
+                const int ecnt = ce.count;
+                tc::fence_after_sync();
+                float v[32];
+                tc::tmem_ld32(tmem + lane_base + 128 + s * 32, v);
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&s_tmem_free[s]);
+                if (cl < CK) {
+#pragma unroll
+                    for (int k = 0; k < KC; k++)
+                        if (k < ecnt && v[k] != 0.0f) atomicAdd(dst + (size_t)ce.id[k] * C, v[k]);
+                }
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&s_list_free[e % LIST_SLOTS]);
+                e++;
+                progress = true;
+            }
+            if (progress) {
+                idle = 0;
+            } else if (++idle > WAIT_LIMIT) {
+                if (lane == 0) s_fail = 1;
+                break;
+            }
         }
     } else {  // Role::Pixel
         // ------------------------------------------------------------------ pixel warps 0-7
-        // Sender: warp w carries quadrant q = w & 3 (its TMEM lanes), entries 16 (w >> 2) ..+16.
-        // Walker: eight threads per pixel of this block's quadrant; thread j takes entries 4j..4j+3.
+        // Eight threads per pixel of this block's quadrant; thread j takes entries 4j..4j+3.
         const int pq = warp * 4 + (lane >> 3), j = lane & 7;
         const int p = rank * QPIX + pq;
         const int2 lp = half_tile_pixel(p);
@@ -552,12 +598,6 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
                 s_gp[pq][2] = gpb;
             }
         }
-        const int q = warp & 3, h = warp >> 2;
-        const uint32_t t_send = tmem + ((uint32_t)(q * 32) << 16) + 16 * h;
-        // Where this lane's partial goes: owner q's receive buffer, slice `rank`, pixel `lane`.
-        const uint32_t recv_local = recv(0) + rank * RECV_SLICE_BYTES + lane * 128;
-        const uint32_t recv_dst = tc::map_shared(recv_local, q);
-        const uint32_t recv_bar = tc::map_shared(tc::smem_addr(&s_recv_full[0]), q);
         const uint32_t w_off = w_offset(p, 4 * j);
         const uint32_t u_off = pq * 128 + ((j ^ ((pq >> 3) << 1)) << 4);
         const uint32_t r_off = pq * 128 + ((j ^ (pq & 7)) << 4);
@@ -570,60 +610,17 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
             return ok;
         };
 
-        // Send: this warp's 32 pixels x 16 entries of chunk c's slice dot to the quadrant's owner.
-        // Returns the chunk's entry count (0: the empty chunk, nothing sent), -1 after a timeout.
-        auto send = [&](int c) -> int {
-            const int s = c % STAGES;
-            const uint32_t par = (c / STAGES) & 1;
-            if (!warp_wait(&s_ready[s], par, false)) return -1;
-            const int cnt = s_list[c % LIST_SLOTS].count;
-            if (cnt == 0) return 0;
-            if (!warp_wait(&s_dot_full[s], par, false)) return -1;
-            tc::fence_after_sync();
-            float v[16];
-            tc::tmem_ld16(t_send + s * 32, v);
-            tc::fence_before_sync();
-            if (q == rank) {
-                // This block's own quadrant: plain stores; the first of the two warps also posts the
-                // bytes the three peers' partials will complete.
-                const uint32_t dst = recv_local + s * K::STAGE_BYTES;
-#pragma unroll
-                for (int m4 = 0; m4 < 4; m4++) {
-                    const uint32_t seg = (uint32_t)((4 * h + m4) ^ (lane & 7));
-                    st_shared_v4(dst + seg * 16, __float_as_uint(v[4 * m4]), __float_as_uint(v[4 * m4 + 1]),
-                                 __float_as_uint(v[4 * m4 + 2]), __float_as_uint(v[4 * m4 + 3]));
-                }
-                __syncwarp();
-                if (lane == 0) {
-                    if (h == 0)
-                        tc::mbar_arrive_expect_tx(&s_recv_full[s], (CLUSTER - 1) * RECV_SLICE_BYTES);
-                    else
-                        tc::mbar_arrive(&s_recv_full[s]);
-                }
-            } else {
-                const uint32_t dst = recv_dst + s * K::STAGE_BYTES, bar = recv_bar + s * 8;
-#pragma unroll
-                for (int m4 = 0; m4 < 4; m4++) {
-                    const uint32_t seg = (uint32_t)((4 * h + m4) ^ (lane & 7));
-                    tc::st_async_v4(dst + seg * 16, v[4 * m4], v[4 * m4 + 1], v[4 * m4 + 2], v[4 * m4 + 3], bar);
-                }
-            }
-            return cnt;
-        };
-
-        // Chunk c + 1's partial dots go out before chunk c is walked, so that the peers' arrive while
-        // it is.  The owner's receive buffer of chunk c + 1 last held chunk c - 3, which it has walked:
-        // a block that passed chunk c's receive barrier holds every peer's chunk-c partial, sent by
-        // each peer after its own walk of chunk c - 2.
-        int next = send(0);
-        for (int c = 0; next > 0; c++) {
+        for (int c = 0;; c++) {
             const int s = c % STAGES;
             const BwdChunk& ch = s_list[c % LIST_SLOTS];
             const uint32_t par = (c / STAGES) & 1;
-            const int cnt = next;
+            // The list slot is released after this warp's walk of the chunk (through the operand warps'
+            // geometry), so its barrier cannot run a phase ahead.
+            if (!warp_wait(&s_list_full[c % LIST_SLOTS], (c / LIST_SLOTS) & 1, false)) break;
+            const int cnt = ch.count;
+            if (cnt == 0) break;
+            // The four slices' partial dots of the quadrant, sent by the drain warps of the cluster.
             if (!warp_wait(&s_recv_full[s], par, true)) break;
-            next = send(c + 1);
-            if (next < 0) break;
 
             // Walk: the whole dot of this thread's four entries, summed over the four slices.
             float d[4];
