@@ -60,6 +60,9 @@ __device__ __forceinline__ Role role_of(int warp) {
                               : Role::Drain;
 }
 constexpr int OPERAND_BAR = 2, DRAIN_BAR = 3;
+// Polls without progress before a multi-queue polling loop (MMA warp, drain warps) gives up: their
+// test_wait never suspends, so a poll costs tens of cycles, not try_wait's bounded suspension.
+constexpr uint32_t POLL_LIMIT = 1u << 26;
 constexpr int G_BYTES = PIX * 128 * 2;  // one bf16 copy of G: [c/8][p][c%8], 128 channel rows (the dF M)
 // One bf16 copy of W as [p/8][k/8][p%8][k%8], so that quadrant q is the 2 KB at 2048 q.
 constexpr int W_BYTES = PIX * KC * 2;
@@ -70,9 +73,10 @@ constexpr int RECV_SLICE_BYTES = QPIX * KC * 4;
 constexpr int RECV_BYTES = CLUSTER * RECV_SLICE_BYTES;
 // u = dL/dalpha G of the quadrant: [pixel][entry] fp32, 16-byte groups permuted by 2 (pixel / 8).
 constexpr int U_BYTES = QPIX * KC * 4;
-// TMEM columns: dots at s*32, dF^T at 128 + s*32, and G as the dot's A operand from G_TMEM (lane =
-// pixel; hi: CK / 2 columns of channel pairs, then lo).
-constexpr uint32_t TMEM_COLS = 512, G_TMEM = 256;
+// TMEM columns: dots at s*32, dF^T at 128 + s*32, G as the dot's A operand from G_TMEM (lane =
+// pixel; hi: CK / 2 columns of channel pairs, then lo), and G^T as the dF's A operand from GT_TMEM
+// (lane = channel, rows past the slice zero; hi: 64 columns of pixel pairs, then lo).
+constexpr uint32_t TMEM_COLS = 512, G_TMEM = 256, GT_TMEM = 384;
 
 template <int CK>
 struct Cfg {
@@ -84,7 +88,7 @@ struct Cfg {
     static constexpr int SMEM = 2 * G_BYTES + STAGES * STAGE_BYTES + 1024;
     static constexpr int F_LBO = (KC / 8) * 128;
     static constexpr uint32_t IDESC_DOT = tc::idesc_bf16(128, KC, false, false);
-    static constexpr uint32_t IDESC_DF = tc::idesc_bf16(128, KC, true, true);
+    static constexpr uint32_t IDESC_DF = tc::idesc_bf16(128, KC, false, true);  // A = G^T from TMEM
     static_assert(CK == 64 || CK == 128, "cluster slices are 64 or 128 channels");
 };
 
@@ -255,6 +259,27 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
                     tc::tmem_st16(dst + cb0 * 4, r);
                 }
             }
+            // And G^T as the dF MMA's A operand: lane = channel c (this warp's 32), column j = pixels
+            // 2j and 2j + 1; the staged rows past the slice are zero.
+            const int c = q4 * 32 + lane;
+#pragma unroll
+            for (int half = 0; half < 2; half++) {
+                const uint32_t src = (half ? g_lo : g_hi) + (c >> 3) * 2048 + (c & 7) * 2;
+                const uint32_t dst = tmem + ((uint32_t)(q4 * 32) << 16) + GT_TMEM + half * (PIX / 2);
+#pragma unroll 1
+                for (int j0 = 0; j0 < PIX / 2; j0 += 16) {
+                    uint32_t r[16];
+#pragma unroll
+                    for (int t = 0; t < 16; t++) {
+                        const uint32_t a = src + (uint32_t)(2 * (j0 + t)) * 16;
+                        uint16_t lo16, hi16;
+                        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(lo16) : "r"(a));
+                        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(hi16) : "r"(a + 16));
+                        r[t] = (uint32_t)lo16 | ((uint32_t)hi16 << 16);
+                    }
+                    tc::tmem_st16(dst + j0, r);
+                }
+            }
             tc::tmem_wait_st();
         }
         tc::fence_before_sync();
@@ -417,7 +442,7 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
             while (n_end < 0 || cf < n_end) {
                 if (*(volatile int*)&s_fail) break;
                 bool progress = false;
-                if (n_end < 0 && tc::mbar_try_wait(&s_ready[cd % STAGES], (cd / STAGES) & 1)) {
+                if (n_end < 0 && tc::mbar_test_wait(&s_ready[cd % STAGES], (cd / STAGES) & 1)) {
                     const int s = cd % STAGES;
                     if (s_list[cd % LIST_SLOTS].count == 0) {
                         n_end = cd;
@@ -444,11 +469,10 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
                 // dF of chunk cf overwrites the TMEM columns of chunk cf - STAGES: the drain warps must
                 // have read them.
                 if (cf < cd &&
-                    (cf < STAGES || tc::mbar_try_wait(&s_tmem_free[cf % STAGES], ((cf - STAGES) / STAGES) & 1)) &&
-                    tc::mbar_try_wait_cluster(&s_w_full[cf % STAGES], (cf / STAGES) & 1)) {
-                    // dF^T of chunk cf = G^T W: A = G MN-major (SBO 2048 between channel blocks, LBO 128
-                    // between pixel groups), B = W MN-major (SBO 128 between entry blocks, LBO 512
-                    // between pixel groups).
+                    (cf < STAGES || tc::mbar_test_wait(&s_tmem_free[cf % STAGES], ((cf - STAGES) / STAGES) & 1)) &&
+                    tc::mbar_test_wait_cluster(&s_w_full[cf % STAGES], (cf / STAGES) & 1)) {
+                    // dF^T of chunk cf = G^T W: A = G^T from TMEM, B = W MN-major (SBO 128 between entry
+                    // blocks, LBO 512 between pixel groups).
                     const int s = cf % STAGES;
                     // The peers' quadrants were written by st.async (the generic proxy): order them
                     // before the tensor cores' reads.
@@ -457,14 +481,13 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
                     const uint32_t wh = fw(s), wl = wh + W_BYTES;
 #pragma unroll
                     for (int ks = 0; ks < PIX / 16; ks++) {
-                        const uint64_t ah = tc::smem_desc(g_hi + ks * 256, 128, 2048);
-                        const uint64_t al = tc::smem_desc(g_lo + ks * 256, 128, 2048);
+                        const uint32_t ah = tmem + GT_TMEM + ks * 8, al = ah + PIX / 2;
                         const uint64_t bh = tc::smem_desc(wh + ks * 1024, 512, 128);
                         const uint64_t bl = tc::smem_desc(wl + ks * 1024, 512, 128);
                         const uint32_t d = tmem + 128 + s * 32;
-                        tc::mma_bf16(d, ah, bh, K::IDESC_DF, ks > 0 ? 1u : 0u);
-                        tc::mma_bf16(d, ah, bl, K::IDESC_DF, 1u);
-                        tc::mma_bf16(d, al, bh, K::IDESC_DF, 1u);
+                        tc::mma_bf16_ta(d, ah, bh, K::IDESC_DF, ks > 0 ? 1u : 0u);
+                        tc::mma_bf16_ta(d, ah, bl, K::IDESC_DF, 1u);
+                        tc::mma_bf16_ta(d, al, bh, K::IDESC_DF, 1u);
                     }
                     tc::commit(&s_df_full[s]);
                     last_bar = &s_df_full[s];
@@ -474,7 +497,7 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
                 }
                 if (progress) {
                     idle = 0;
-                } else if (++idle > WAIT_LIMIT) {
+                } else if (++idle > POLL_LIMIT) {
                     s_fail = 1;
                     break;
                 }
@@ -501,7 +524,7 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
         const uint32_t recv_bar = tc::map_shared(tc::smem_addr(&s_recv_full[0]), q4);
         auto poll = [&](uint64_t* bar, uint32_t par) {
             int done = 0;
-            if (lane == 0) done = tc::mbar_try_wait(bar, par) ? 1 : 0;
+            if (lane == 0) done = tc::mbar_test_wait(bar, par) ? 1 : 0;
             return __shfl_sync(FULL_MASK, done, 0) != 0;
         };
         int xs = 0, e = 0, n_end = -1;
@@ -565,7 +588,7 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
             }
             if (progress) {
                 idle = 0;
-            } else if (++idle > WAIT_LIMIT) {
+            } else if (++idle > POLL_LIMIT) {
                 if (lane == 0) s_fail = 1;
                 break;
             }
