@@ -730,7 +730,9 @@ def run_band_split(args, device, rank, world, dist, timer):
     once over all ranks (strong scaling) -- projection, SH, band binning and blend, 0.8 L1 + 0.2 (1 -
     SSIM) with the SSIM halo exchange, a fixed feature-image gradient, the backward, the feature
     gradients combined at their owners, the geometry/SH all-reduce and both Adam steps.  Bands are
-    balanced by (tile, gaussian) pairs per tile row of a first binning pass."""
+    balanced by (tile, gaussian) pairs per tile row of a first binning pass; the feature table is split
+    in contiguous row blocks (measured faster here than band_split.band_owner's map, whose local rows
+    still pass through the dispatch and combine copies)."""
     import torch
 
     from hds_b200 import band_split, gaussian_rasterizer, optim, scenes
@@ -803,6 +805,10 @@ def run_band_split(args, device, rank, world, dist, timer):
         gathered = [torch.zeros_like(band_sizes) for _ in range(world)]
         dist.all_gather(gathered, band_sizes)
         band_sizes = torch.cat(gathered)
+    all_phases = [phases]
+    if dist is not None:
+        all_phases = [None] * world
+        dist.all_gather_object(all_phases, phases)
     ms_e2e = timed(e2e=True, record_calls=False)
     if rank == 0:
         line = {
@@ -816,7 +822,7 @@ def run_band_split(args, device, rank, world, dist, timer):
                        "bands": trainer.bands, "l2": "inputs larger than L2 (feature table "
                        f"{s.n * C * 4 / 1e9:.1f} GB)"},
             "call_ms_per_step": {k: v / args.steps for k, v in sorted(calls.items(), key=lambda kv: -kv[1])},
-            "phase_ms_per_step_rank0": phases,
+            "phase_ms_per_step": all_phases,
             "band_gaussians": band_sizes.tolist(),
             "gpu_launches": launches, "clocks": clock_info,
             "e2e": {"value": args.steps / (ms_e2e / 1000.0), "unit": "views/s",

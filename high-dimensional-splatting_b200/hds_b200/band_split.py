@@ -45,64 +45,104 @@ def band_reach_mask(means2D: torch.Tensor, radii: torch.Tensor, y0: int, y1: int
 
 
 class FeatureShards:
-    """The feature table split in contiguous row blocks over the group's ranks.
+    """The feature table split over the group's ranks: by contiguous row blocks, or by an owner map.
 
-    rows [n_local, C] is this rank's block (a leaf: its gradient is `rows.grad`, summed over every
-    band by combine()).  dispatch(ids) returns the rows of any sorted set of global ids, fetched from
-    their owners; combine(ids, grads) adds per-row gradients into the owners' rows.grad."""
+    rows [n_local, C] holds the rows this rank owns, in ascending global id (a leaf: its gradient is
+    `rows.grad`, summed over every band by combine()).  dispatch(ids) returns the rows of any sorted
+    set of global ids, fetched from their owners; combine(ids, grads) adds per-row gradients into the
+    owners' rows.grad.
 
-    def __init__(self, n: int, channels: int, rank: int, world: int, device, group=None, init=None):
+    owner: optional [n] tensor of owning ranks.  Giving each row to the band whose pixels hold its
+    gaussian's centre keeps most of a band's rows on its own rank, so that dispatch and combine move
+    only the rows of gaussians that reach across a band boundary.  With an owner map, init takes the
+    owned global ids (a 1-D int64 tensor) instead of a [start, end) block."""
+
+    def __init__(self, n: int, channels: int, rank: int, world: int, device, group=None, init=None, owner=None):
         self.n, self.channels, self.rank, self.world, self.group = n, channels, rank, world, group
-        self.starts = [n * r // world for r in range(world + 1)]
-        self.start, self.end = self.starts[rank], self.starts[rank + 1]
-        local = self.end - self.start
-        rows = init(self.start, self.end) if init is not None else torch.zeros(local, channels)
+        if owner is None:
+            self.owner = None
+            self.starts = [n * r // world for r in range(world + 1)]
+            self.start, self.end = self.starts[rank], self.starts[rank + 1]
+            local = self.end - self.start
+            rows = init(self.start, self.end) if init is not None else torch.zeros(local, channels)
+            self._bounds = torch.tensor(self.starts[1:], dtype=torch.int64, device=device)
+        else:
+            self.owner = owner.to(device=device, dtype=torch.int64)
+            if self.owner.shape != (n,) or (n and (int(self.owner.min()) < 0 or int(self.owner.max()) >= world)):
+                raise ValueError("owner must hold one rank in [0, world) per row")
+            self.ids_local = torch.nonzero(self.owner == rank).squeeze(1)
+            self.local_of = torch.full((n,), -1, dtype=torch.int64, device=device)
+            self.local_of[self.ids_local] = torch.arange(self.ids_local.numel(), device=device)
+            local = self.ids_local.numel()
+            rows = init(self.ids_local) if init is not None else torch.zeros(local, channels)
         self.rows = rows.to(device=device, dtype=torch.float32).contiguous().requires_grad_(True)
         self.rows.grad = torch.zeros_like(self.rows)
-        self._bounds = torch.tensor(self.starts[1:], dtype=torch.int64, device=device)
         self._plan = None
 
-    def _owner_counts(self, ids: torch.Tensor) -> torch.Tensor:
-        owner = torch.searchsorted(self._bounds, ids, right=True)
-        return torch.bincount(owner, minlength=self.world)
+    def _local(self, ids: torch.Tensor) -> torch.Tensor:
+        """Positions in rows of owned global ids."""
+        return ids - self.start if self.owner is None else self.local_of[ids]
 
     def dispatch(self, ids: torch.Tensor) -> torch.Tensor:
         """Rows of the sorted global ids `ids` ([M] int64), in that order ([M, C])."""
         if self.world == 1:
             self._plan = None
-            return self.rows.detach()[ids - self.start]
-        send_counts = self._owner_counts(ids)
+            return self.rows.detach()[self._local(ids)]
+        if self.owner is None:
+            # Sorted ids and contiguous owners keep every owner's requests in one slice of ids.
+            own = torch.searchsorted(self._bounds, ids, right=True)
+            perm, grouped = None, ids
+        else:
+            own = self.owner[ids]
+            perm = torch.argsort(own, stable=True)  # requests grouped by owner, ascending within each
+            grouped = ids[perm]
+        send_counts = torch.bincount(own, minlength=self.world)
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts, group=self.group)
         send, recv = send_counts.tolist(), recv_counts.tolist()
-        # Requests: the ids each owner must serve (sorted ids and contiguous owners keep every
-        # rank's requests in one slice of ids).
         wanted = torch.empty(sum(recv), dtype=ids.dtype, device=ids.device)
-        dist.all_to_all_single(wanted, ids.contiguous(), output_split_sizes=recv, input_split_sizes=send,
+        dist.all_to_all_single(wanted, grouped.contiguous(), output_split_sizes=recv, input_split_sizes=send,
                                group=self.group)
-        served = self.rows.detach()[wanted - self.start].contiguous()
-        out = torch.empty(ids.numel(), self.channels, dtype=served.dtype, device=served.device)
-        dist.all_to_all_single(out, served, output_split_sizes=send, input_split_sizes=recv, group=self.group)
-        self._plan = (send, recv, wanted)
-        return out
+        local = self._local(wanted)
+        served = self.rows.detach()[local].contiguous()
+        got = torch.empty(ids.numel(), self.channels, dtype=served.dtype, device=served.device)
+        dist.all_to_all_single(got, served, output_split_sizes=send, input_split_sizes=recv, group=self.group)
+        if perm is not None:
+            out = torch.empty_like(got)
+            out[perm] = got
+            got = out
+        self._plan = (send, recv, local, perm)
+        return got
 
     def combine(self, ids: torch.Tensor, grads: torch.Tensor) -> None:
         """Adds grads ([M, C], rows of the ids of the last dispatch) into the owners' rows.grad."""
         if self.world == 1:
-            self.rows.grad.index_add_(0, ids - self.start, grads)
+            self.rows.grad.index_add_(0, self._local(ids), grads)
             return
-        send, recv, wanted = self._plan
+        send, recv, local, perm = self._plan
+        outgoing = grads if perm is None else grads[perm]
         back = torch.empty(sum(recv), self.channels, dtype=grads.dtype, device=grads.device)
-        dist.all_to_all_single(back, grads.contiguous(), output_split_sizes=recv, input_split_sizes=send,
+        dist.all_to_all_single(back, outgoing.contiguous(), output_split_sizes=recv, input_split_sizes=send,
                                group=self.group)
-        # Each requester's ids are sorted and distinct, so within its slice every row is added once:
-        # a gather, an add and a scatter per slice instead of one float atomic per element.
-        g, local, off = self.rows.grad, wanted - self.start, 0
+        # Each requester's ids are distinct, so within its slice every row is added once: a gather, an
+        # add and a scatter per slice instead of one float atomic per element.
+        g, off = self.rows.grad, 0
         for k in recv:
             if k:
                 idx = local[off:off + k]
                 g[idx] = g[idx] + back[off:off + k]
             off += k
+
+
+def band_owner(means2D: torch.Tensor, radii: torch.Tensor, bands: list[tuple[int, int]]) -> torch.Tensor:
+    """An owner map for FeatureShards: each visible gaussian goes to the band whose rows hold its
+    projected centre (clamped into the image), each invisible one to rank id % world."""
+    n, world = means2D.shape[0], len(bands)
+    ends = torch.tensor([b[1] for b in bands[:-1]], dtype=torch.float32, device=means2D.device)
+    y = means2D[:, 1].detach().clamp(0.0, float(bands[-1][1] - 1))
+    owner = torch.searchsorted(ends, y, right=True).to(torch.int64)
+    spare = torch.arange(n, device=means2D.device) % world
+    return torch.where(radii > 0, owner, spare)
 
 
 class HaloExchange:

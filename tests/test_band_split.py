@@ -1,7 +1,8 @@
 """The tile-row split's exchange logic on CPU, over three gloo ranks (hds_b200.band_split):
 
 * FeatureShards: rows dispatched from their owners equal the full table's rows; gradients combined
-  from every band land summed on the owners.
+  from every band land summed on the owners -- with contiguous row blocks, and with an owner map
+  (band_owner on a scene's projected centres).
 * HaloExchange + BandSSIM (with the oracle's SSIM): the bands' shares add up to the full image's mean
   SSIM, and the folded band gradients equal the full image's SSIM gradient row for row.
 """
@@ -71,6 +72,18 @@ def _worker(rank, port, queue):
         grads = [None] * WORLD
         dist.all_gather_object(grads, (shards.start, shards.rows.grad.numpy().copy()))
 
+        # The same through an owner map: each row owned by the band that holds its centre.
+        gen = torch.Generator().manual_seed(4)
+        means2D = torch.rand(N, 2, generator=gen) * torch.tensor([float(W), float(H)])
+        radii = (torch.rand(N, generator=gen) > 0.1).float() * 3.0
+        owner = band_split.band_owner(means2D, radii, parallel.row_bands(H, WORLD))
+        mapped = band_split.FeatureShards(N, C, rank, WORLD, "cpu", init=lambda g: table_rows(0, N)[g], owner=owner)
+        rows_m = mapped.dispatch(ids)
+        mapped_ok = torch.equal(rows_m, table_rows(0, N)[ids])
+        mapped.combine(ids, torch.full((len(ids), C), float(rank + 1)))
+        grads_m = [None] * WORLD
+        dist.all_gather_object(grads_m, (mapped.ids_local.numpy().copy(), mapped.rows.grad.numpy().copy()))
+
         img, gt = images()
         bands = parallel.row_bands(H, WORLD)
         y0, y1 = bands[rank]
@@ -81,7 +94,8 @@ def _worker(rank, port, queue):
         share.backward()
         shares = [None] * WORLD
         dist.all_gather_object(shares, (float(share), band.grad.numpy().copy()))
-        queue.put((rank, {"rows_ok": rows_ok, "grads": grads, "ssim": shares}))
+        queue.put((rank, {"rows_ok": rows_ok, "grads": grads, "ssim": shares, "mapped_ok": mapped_ok,
+                          "grads_mapped": grads_m, "owner": owner.numpy()}))
     finally:
         dist.destroy_process_group()
 
@@ -110,6 +124,19 @@ def test_feature_shards_dispatch_and_combine(results):
     for start, g in results[0]["grads"]:
         got[start:start + len(g)] = g
     assert np.array_equal(got, want)
+
+
+def test_feature_shards_with_an_owner_map(results):
+    assert all(results[r]["mapped_ok"] for r in range(WORLD))
+    want = np.zeros((N, C), np.float32)
+    for r in range(WORLD):
+        want[rank_ids(r).numpy()] += r + 1
+    got = np.full((N, C), np.nan, np.float32)
+    owner = results[0]["owner"]
+    for r, (ids_local, g) in enumerate(results[0]["grads_mapped"]):
+        assert np.array_equal(owner[ids_local], np.full(len(ids_local), r))
+        got[ids_local] = g
+    assert np.array_equal(got, want)  # every row owned exactly once, gradients summed
 
 
 def test_band_ssim_matches_full_image(results):

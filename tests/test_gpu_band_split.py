@@ -1,7 +1,7 @@
 """The tile-row split end to end on two GPUs (hds_b200.band_split over NCCL): one training step of a
 config-4-like view split into two bands gives the same loss and the same gradients -- geometry and SH
-after their all-reduce, features after the combine at their owners -- as the whole view on one GPU.
-Needs two GPUs; skipped otherwise."""
+after their all-reduce, features after the combine at their owners -- as the whole view on one GPU,
+with the feature table split in row blocks or by an owner map.  Needs two GPUs; skipped otherwise."""
 import os
 import socket
 
@@ -20,7 +20,7 @@ def free_port():
         return s.getsockname()[1]
 
 
-def _run(rank, world, port, queue):
+def _run(rank, world, port, queue, owner_map=False):
     import torch.distributed as dist
 
     from hds_b200 import band_split, optim, scenes
@@ -38,7 +38,14 @@ def _run(rank, world, port, queue):
                "opacity_logits": torch.log(op / (1 - op)), "sh_dc": s.sh_dc, "sh_rest": s.sh_rest}
         raw = {k: v.to(device).contiguous().requires_grad_(True) for k, v in raw.items()}
         table = torch.randn(N, C, generator=torch.Generator().manual_seed(3))
-        feats = band_split.FeatureShards(N, C, rank, world, device, init=lambda a, b: table[a:b].clone())
+        if owner_map and world > 1:
+            owner = torch.randint(0, world, (N,), generator=torch.Generator().manual_seed(6))
+            feats = band_split.FeatureShards(N, C, rank, world, device, init=lambda ids: table[ids.cpu()].clone(),
+                                             owner=owner)
+            ids_local = feats.ids_local.cpu().numpy()
+        else:
+            feats = band_split.FeatureShards(N, C, rank, world, device, init=lambda a, b: table[a:b].clone())
+            ids_local = np.arange(feats.start, feats.end)
         lrs = [optim.REFERENCE_LRS[k] for k in raw] + [optim.REFERENCE_LRS["features"]]
         trainer = band_split.BandSplitTrainer(raw, feats, cam, lrs, rank, world)
         H, W = cam.height, cam.width
@@ -46,7 +53,7 @@ def _run(rank, world, port, queue):
         fgrad = torch.rand(H, W, C, generator=torch.Generator().manual_seed(5)).to(device) / (H * W)
         loss = trainer.step(gt, fgrad[trainer.y0:trainer.y1])
         out = {"loss": float(loss), "geometry": trainer.bucket.flat.cpu().numpy(),
-               "features": (feats.start, feats.rows.grad.cpu().numpy()), "bands": trainer.bands}
+               "features": (ids_local, feats.rows.grad.cpu().numpy()), "bands": trainer.bands}
         queue.put((rank, out))
     finally:
         if world > 1:
@@ -54,13 +61,13 @@ def _run(rank, world, port, queue):
             dist.destroy_process_group()
 
 
-def _launch(world):
+def _launch(world, owner_map=False):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=_run, args=(r, world, port, queue)) for r in range(world)]
+    procs = [ctx.Process(target=_run, args=(r, world, port, queue, owner_map)) for r in range(world)]
     for p in procs:
         p.start()
     out = dict(queue.get(timeout=600) for _ in range(world))
@@ -70,13 +77,14 @@ def _launch(world):
     return out
 
 
-def test_two_band_step_matches_one_gpu():
+@pytest.mark.parametrize("owner_map", [False, True])
+def test_two_band_step_matches_one_gpu(owner_map):
     if torch.cuda.device_count() < 2:
         pytest.skip("the tile-row split test needs two GPUs")
     from helpers import assert_grads_close
 
     one = _launch(1)[0]
-    two = _launch(2)
+    two = _launch(2, owner_map)
     assert len(two[0]["bands"]) == 2
     np.testing.assert_allclose(two[0]["loss"], one["loss"], rtol=1e-5)
     assert two[0]["loss"] == two[1]["loss"]
@@ -88,8 +96,8 @@ def test_two_band_step_matches_one_gpu():
         assert_grads_close(two[0]["geometry"][seg], one["geometry"][seg], f"{name} gradients, 2 bands vs 1 GPU")
         off += N * width
     assert off == len(one["geometry"])
-    got = np.zeros((N, C), np.float32)
+    got = np.full((N, C), np.nan, np.float32)
     for r in range(2):
-        start, g = two[r]["features"]
-        got[start:start + len(g)] = g
+        ids_local, g = two[r]["features"]
+        got[ids_local] = g
     assert_grads_close(got, one["features"][1], "feature gradients, 2 bands vs 1 GPU")
