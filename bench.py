@@ -730,9 +730,10 @@ def run_band_split(args, device, rank, world, dist, timer):
     once over all ranks (strong scaling) -- projection, SH, band binning and blend, 0.8 L1 + 0.2 (1 -
     SSIM) with the SSIM halo exchange, a fixed feature-image gradient, the backward, the feature
     gradients combined at their owners, the geometry/SH all-reduce and both Adam steps.  Bands are
-    balanced by (tile, gaussian) pairs per tile row of a first binning pass; the feature table is split
-    in contiguous row blocks (measured faster here than band_split.band_owner's map, whose local rows
-    still pass through the dispatch and combine copies)."""
+    balanced by (tile, gaussian) pairs per tile row of a first binning pass (measured faster than
+    balancing by visited pairs, which evens the blends but loads the dense band with fetched rows);
+    the feature table is split in contiguous row blocks, rendered in place
+    (band_split.bin_band_in_place)."""
     import torch
 
     from hds_b200 import band_split, gaussian_rasterizer, optim, scenes
@@ -800,7 +801,7 @@ def run_band_split(args, device, rank, world, dist, timer):
     launches = timed.launches
     clock_info = clocks.stop()
     calls, counts = timer.totals_ms(), timer.counts()
-    band_sizes = torch.tensor([trainer.band_gaussians], device=device)
+    band_sizes = torch.tensor([[trainer.band_gaussians, trainer.fetched_rows]], device=device)
     if dist is not None:
         gathered = [torch.zeros_like(band_sizes) for _ in range(world)]
         dist.all_gather(gathered, band_sizes)
@@ -823,7 +824,8 @@ def run_band_split(args, device, rank, world, dist, timer):
                        f"{s.n * C * 4 / 1e9:.1f} GB)"},
             "call_ms_per_step": {k: v / args.steps for k, v in sorted(calls.items(), key=lambda kv: -kv[1])},
             "phase_ms_per_step": all_phases,
-            "band_gaussians": band_sizes.tolist(),
+            "band_gaussians": [b[0] for b in band_sizes.tolist()],
+            "fetched_feature_rows": [b[1] for b in band_sizes.tolist()],
             "gpu_launches": launches, "clocks": clock_info,
             "e2e": {"value": args.steps / (ms_e2e / 1000.0), "unit": "views/s",
                     "h2d_bytes_per_step": H * W * 3, "d2h_bytes_per_step": 4},

@@ -83,8 +83,9 @@ class FeatureShards:
         """Positions in rows of owned global ids."""
         return ids - self.start if self.owner is None else self.local_of[ids]
 
-    def dispatch(self, ids: torch.Tensor) -> torch.Tensor:
-        """Rows of the sorted global ids `ids` ([M] int64), in that order ([M, C])."""
+    def dispatch(self, ids: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Rows of the sorted global ids `ids` ([M] int64), in that order ([M, C]; written into `out`
+        when given, a contiguous [M, C] tensor)."""
         if self.world == 1:
             self._plan = None
             return self.rows.detach()[self._local(ids)]
@@ -105,12 +106,15 @@ class FeatureShards:
                                group=self.group)
         local = self._local(wanted)
         served = self.rows.detach()[local].contiguous()
-        got = torch.empty(ids.numel(), self.channels, dtype=served.dtype, device=served.device)
+        if out is not None and perm is None:
+            got = out
+        else:
+            got = torch.empty(ids.numel(), self.channels, dtype=served.dtype, device=served.device)
         dist.all_to_all_single(got, served, output_split_sizes=send, input_split_sizes=recv, group=self.group)
         if perm is not None:
-            out = torch.empty_like(got)
-            out[perm] = got
-            got = out
+            ordered = out if out is not None else torch.empty_like(got)
+            ordered[perm] = got
+            got = ordered
         self._plan = (send, recv, local, perm)
         return got
 
@@ -259,6 +263,35 @@ def bin_band(means2D, depths, radii, conics, colors, opacities, width: int, y0: 
         return ids, values_c, ranges, conic[ids].contiguous(), co[ids].contiguous()
 
 
+def bin_band_in_place(means2D, depths, radii, conics, colors, opacities, width: int, y0: int, y1: int, start: int,
+                      end: int):
+    """bin_band for a rank that owns the feature rows [start, end): the band is rendered over a table of
+    n_local + R rows -- the owned rows in place, then the R rows of the band's other gaussians, fetched
+    from their owners.  Returns (pos_ids [n_local + R]: the global id of each table row, values
+    renamed to table rows, ranges, the packed conic / color_opacity rows of the table, remote_ids [R]:
+    the sorted ids of the fetched rows, the number of gaussians in the band's lists).  Table rows of
+    owned gaussians outside the band are unused."""
+    from .gaussian_rasterizer import _bin
+
+    with torch.no_grad():
+        dev = means2D.device
+        conic, co, values, ranges, _ = _bin(means2D.contiguous(), depths.contiguous(), radii.contiguous(),
+                                            conics.contiguous(), colors.contiguous(), opacities.contiguous(), width,
+                                            y1 - y0, origin_y=y0)
+        n, n_local = means2D.shape[0], end - start
+        mask = torch.zeros(n, dtype=torch.bool, device=dev)
+        mask[values.long()] = True
+        in_band = mask.sum()
+        mask[start:end] = False
+        remote_ids = torch.nonzero(mask).squeeze(1)
+        pos_ids = torch.cat([torch.arange(start, end, device=dev), remote_ids])
+        rename = torch.empty(n, dtype=torch.int32, device=dev)
+        rename[pos_ids] = torch.arange(pos_ids.numel(), dtype=torch.int32, device=dev)
+        values_c = rename[values.long()].contiguous()
+        return (pos_ids, values_c, ranges, conic[pos_ids].contiguous(), co[pos_ids].contiguous(), remote_ids,
+                int(in_band))
+
+
 class CompactBandRender(torch.autograd.Function):
     """The fused RGB + feature blend of a band over the compact set of gaussians its lists hold: the
     kernels see exactly the per-entry data and list order of the full-scene call, so the outputs are the
@@ -266,16 +299,19 @@ class CompactBandRender(torch.autograd.Function):
     gradients back to the scene's rows (the feature rows' gradient stays compact, for the owners)."""
 
     @staticmethod
-    def forward(ctx, means2D, conics, colors, opacities, rows, binned, background, width: int, y0: int, y1: int):
+    def forward(ctx, means2D, conics, colors, opacities, rows, binned, background, width: int, y0: int, y1: int,
+                grad_rows=None):
+        """grad_rows: when given, the feature rows' gradient is added into it (rows then takes none)."""
         from .gaussian_rasterizer import render_binned_with_features
 
-        ids, values_c, ranges, conic_c, co_c = binned
+        ids, values_c, ranges, conic_c, co_c = binned[:5]
         m2c = means2D.detach()[ids].contiguous()
         image, feat, final_T, n_contrib = render_binned_with_features(values_c, ranges, m2c, conic_c, co_c,
                                                                       rows.contiguous(), background, width, y1 - y0,
                                                                       origin_y=y0)
         ctx.save_for_backward(m2c, conic_c, co_c, values_c, ranges, final_T, n_contrib, rows, background, ids)
         ctx.meta = (width, y0, y1, means2D.shape[0])
+        ctx.grad_rows = grad_rows
         return image, feat
 
     @staticmethod
@@ -288,7 +324,8 @@ class CompactBandRender(torch.autograd.Function):
             grad_feat = torch.zeros(y1 - y0, width, rows.shape[1], device=rows.device)
         gm, gc, gcol, go, gf = rasterize_backward_fused(
             grad_image.contiguous() if grad_image is not None else None, background, grad_feat.contiguous(),
-            rows.contiguous(), m2c, conic_c, co_c, values_c, ranges, final_T, n_contrib, width, y1 - y0, origin_y=y0)
+            rows.contiguous(), m2c, conic_c, co_c, values_c, ranges, final_T, n_contrib, width, y1 - y0, origin_y=y0,
+            grad_features_into=ctx.grad_rows)
         dev = rows.device
 
         def scatter(g, width_):
@@ -296,7 +333,7 @@ class CompactBandRender(torch.autograd.Function):
             return out.index_add_(0, ids, g)
 
         g_colors = scatter(gcol, 3) if gcol is not None else torch.zeros(n, 3, device=dev)
-        return (scatter(gm, 2), scatter(gc, 3), g_colors, scatter(go, 1), gf, None, None, None, None, None)
+        return (scatter(gm, 2), scatter(gc, 3), g_colors, scatter(go, 1), gf, None, None, None, None, None, None)
 
 
 class PhaseTimer:
@@ -343,10 +380,16 @@ class BandSplitTrainer:
         self.leaves = list(raw.values())
         self.bucket = GradBucket(self.leaves)
         self.opt = FlatAdam(self.leaves, lrs[:len(self.leaves)], eps=1e-15, bucket=self.bucket)
-        self.feature_opt = FlatAdam([features.rows], lrs[len(self.leaves):], eps=1e-15)
+        # With contiguous row blocks each band renders over a table of this rank's own rows (in place,
+        # in the optimizer's flat buffer) followed by the fetched rows of other ranks' gaussians (its
+        # tail), and the backward adds straight into the same layout of the gradient bucket.
+        self.in_place = world > 1 and features.owner is None
+        tail = (features.n - features.rows.shape[0]) * features.channels if self.in_place else 0
+        self.feature_opt = FlatAdam([features.rows], lrs[len(self.leaves):], eps=1e-15, tail=tail)
         self.ssim_fns = gpu_ssim_fns()
         self.timer = PhaseTimer()
         self.band_gaussians = 0  # gaussians in this rank's band lists at the last step
+        self.fetched_rows = 0  # feature rows fetched from other ranks at the last step
 
     def step(self, gt: torch.Tensor, feature_grad: torch.Tensor) -> torch.Tensor:
         """One forward + backward of the view and one optimizer step.  gt: the full view's [H, W, 3]
@@ -378,6 +421,24 @@ class BandSplitTrainer:
                 image, feat = rasterize(means2D, depths, radii, conics, colors, opacities, W, H, bg,
                                         self.features.rows)
                 ids = None
+            elif self.in_place:
+                t.mark("bin")
+                f = self.features
+                binned = bin_band_in_place(means2D, depths, radii, conics, colors, opacities, W, y0, y1, f.start,
+                                           f.end)
+                remote = binned[5]
+                self.band_gaussians = binned[6]
+                self.fetched_rows = remote.numel()
+                n_local, Cf = f.end - f.start, f.channels
+                rows_t = (n_local + remote.numel()) * Cf
+                table = self.feature_opt.flat[:rows_t].view(-1, Cf)
+                grad_table = self.feature_opt.bucket.flat[:rows_t].view(-1, Cf)
+                t.mark("dispatch")
+                f.dispatch(remote, out=table[n_local:])
+                t.mark("render")
+                image, feat = CompactBandRender.apply(means2D, conics, colors, opacities, table, binned, bg, W, y0,
+                                                      y1, grad_table)
+                ids = remote
             else:
                 t.mark("bin")
                 binned = bin_band(means2D, depths, radii, conics, colors, opacities, W, y0, y1)
@@ -400,7 +461,11 @@ class BandSplitTrainer:
         # Feature gradients back to their owners; geometry and SH summed over the bands.
         if self.world > 1:
             t.mark("combine")
-            self.features.combine(ids, rows.grad)
+            if self.in_place:
+                n_local = self.features.end - self.features.start
+                self.features.combine(ids, grad_table[n_local:])
+            else:
+                self.features.combine(ids, rows.grad)
             t.mark("all_reduce")
             self.bucket.all_reduce(self.group)
         t.mark("adam")

@@ -49,10 +49,14 @@ class FlatAdam:
 
     On construction every parameter's data moves into one flat buffer (`self.flat`, in list order)
     and, unless a bucket over the same parameters is given, a GradBucket is made for their gradients.
-    step() runs one kernel over all parameters; lrs can change between steps (set_lr)."""
+    step() runs one kernel over all parameters; lrs can change between steps (set_lr).
+
+    tail: zero elements appended to the flat buffer and to the gradient bucket beyond the parameters
+    (not stepped, no moments): room for rows that are rendered, and differentiated, beside the
+    parameters' own (the tile-row split's fetched feature rows)."""
 
     def __init__(self, params: list[torch.Tensor], lrs: list[float], betas=(0.9, 0.999), eps: float = 1e-15,
-                 bucket: GradBucket | None = None):
+                 bucket: GradBucket | None = None, tail: int = 0):
         if not params or len(params) != len(lrs):
             raise ValueError("one learning rate per parameter")
         if len(params) > MAX_SEGMENTS:
@@ -65,8 +69,11 @@ class FlatAdam:
         self.lrs = [float(x) for x in lrs]
         self.betas = betas
         self.eps = eps
+        if tail and bucket is not None:
+            raise ValueError("a tail needs the optimizer's own bucket")
         with torch.no_grad():
-            self.flat = torch.cat([p.detach().reshape(-1) for p in params]).contiguous()
+            self.flat = torch.cat([p.detach().reshape(-1) for p in params] +
+                                  ([torch.zeros(tail, dtype=torch.float32, device=dev)] if tail else [])).contiguous()
         ends, off = [], 0
         for p in params:
             n = p.numel()
@@ -74,11 +81,12 @@ class FlatAdam:
             off += n
             ends.append(off)
         self.segment_ends = ends
-        self.exp_avg = torch.zeros_like(self.flat)
-        self.exp_avg_sq = torch.zeros_like(self.flat)
+        self.n = off
+        self.exp_avg = torch.zeros(off, dtype=torch.float32, device=dev)
+        self.exp_avg_sq = torch.zeros_like(self.exp_avg)
         if bucket is None:
-            bucket = GradBucket(params)
-        elif bucket.flat.numel() != self.flat.numel() or any(a is not b for a, b in zip(bucket.params, params)):
+            bucket = GradBucket(params, capacity=off + tail)
+        elif bucket.flat.numel() != off or any(a is not b for a, b in zip(bucket.params, params)):
             raise ValueError("the bucket must cover the same parameters in the same order")
         self.bucket = bucket
         self.step_count = 0
@@ -90,6 +98,7 @@ class FlatAdam:
         the given shapes as views of `flat`, with their own gradient bucket, and the given moments."""
         self = cls.__new__(cls)
         self.flat, self.exp_avg, self.exp_avg_sq = flat, exp_avg, exp_avg_sq
+        self.n = flat.numel()
         self.lrs, self.betas, self.eps, self.step_count = [float(x) for x in lrs], betas, eps, step_count
         params, ends, off = [], [], 0
         for shape in shapes:
@@ -115,7 +124,8 @@ class FlatAdam:
     def step(self) -> None:
         self.bucket.ready()
         self.step_count += 1
-        adam_step(self.flat, self.exp_avg, self.exp_avg_sq, self.bucket.flat, self.segment_ends, self.lrs,
+        n = self.n
+        adam_step(self.flat[:n], self.exp_avg, self.exp_avg_sq, self.bucket.flat[:n], self.segment_ends, self.lrs,
                   self.step_count, self.betas, self.eps)
 
 
