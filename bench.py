@@ -54,6 +54,17 @@ def parse_args():
     ap.add_argument("--split", choices=["views", "rows"], default="views",
                     help="views: data parallel over views (config 2/3, default); rows: one config-4 view split by "
                          "tile rows across the ranks (4M gaussians, 1920x1080, C=512 unless overridden)")
+    ap.add_argument("--row-owners", choices=["bands", "blocks"], default="bands",
+                    help="--split rows: which feature rows each rank owns -- bands: the scene is ordered once by the "
+                         "band holding each gaussian's projected centre (band_split.band_order), so a band fetches "
+                         "only the rows of gaussians that reach across its edges; blocks: equal blocks of the "
+                         "scene's own order")
+    ap.add_argument("--band-weights", choices=["pairs", "visited", "cost"], default="visited",
+                    help="--split rows: tile-row weights the bands are balanced by -- pairs: (tile, gaussian) pairs; "
+                         "visited: the list entries the blend and backward walk (per half tile, up to its last "
+                         "contributor); cost: 0.69 the row's share of the visited entries + 0.31 its share of the "
+                         "projected centres (the feature rows its band owns and steps under --row-owners bands), the "
+                         "split of a one-GPU step between blend + backward (22.1 ms) and the feature Adam (9.9 ms)")
     args = ap.parse_args()
     if args.split == "rows" and "--gaussians" not in sys.argv:
         args.gaussians = 4_000_000
@@ -724,16 +735,36 @@ def feature_block_init(device, channels, block=1 << 16, seed=1000):
     return init
 
 
+def feature_rows_init(device, channels, perm, block=1 << 16, seed=1000):
+    """feature_block_init for a scene whose rows were permuted: row i of the table is the seeded row of
+    global id perm[i]."""
+    import torch
+
+    def init(start, end):
+        ids = perm[start:end].to(device)
+        out = torch.empty(ids.numel(), channels, device=device)
+        blk = ids // block
+        for b in torch.unique(blk).tolist():
+            g = torch.Generator(device=device).manual_seed(seed + b)
+            rows = torch.randn(block, channels, generator=g, device=device)
+            sel = torch.nonzero(blk == b).squeeze(1)
+            out[sel] = rows[ids[sel] - b * block]
+        return out
+
+    return init
+
+
 def run_band_split(args, device, rank, world, dist, timer):
     """--split rows: BASELINE config 4, one view split by tile rows (hds_b200.band_split).  4M gaussians
     (80% in 200 dense clusters), one 1920x1080 view, C-channel features; every step renders the view
     once over all ranks (strong scaling) -- projection, SH, band binning and blend, 0.8 L1 + 0.2 (1 -
     SSIM) with the SSIM halo exchange, a fixed feature-image gradient, the backward, the feature
-    gradients combined at their owners, the geometry/SH all-reduce and both Adam steps.  Bands are
-    balanced by (tile, gaussian) pairs per tile row of a first binning pass (measured faster than
-    balancing by visited pairs, which evens the blends but loads the dense band with fetched rows);
-    the feature table is split in contiguous row blocks, rendered in place
-    (band_split.bin_band_in_place)."""
+    gradients combined at their owners, the sharded geometry/SH Adam step (reduce-scatter, Adam,
+    all-gather) and the feature Adam step.  Bands are balanced by the list entries the blend and
+    backward walk per tile row, from a first render (--band-weights); the feature table is split in
+    contiguous row blocks, rendered in place (band_split.bin_band_in_place).  With --row-owners bands
+    (the default) the scene is first ordered by band (band_split.band_order), so that each rank's
+    block holds its band's gaussians and only rows reaching across a band edge are fetched."""
     import torch
 
     from hds_b200 import band_split, gaussian_rasterizer, optim, scenes
@@ -754,7 +785,31 @@ def run_band_split(args, device, rank, world, dist, timer):
         tx = (W + 15) // 16
         per_row = (ranges[:, 1] - ranges[:, 0]).reshape(-1, tx).sum(dim=1).double()
         weights = (per_row + 1.0).tolist()
-    features = band_split.FeatureShards(s.n, C, rank, world, device, init=feature_block_init(device, C))
+        ty = per_row.numel()
+        if args.band_weights in ("visited", "cost"):
+            colors = torch.zeros(s.n, 3, device=device)
+            n_contrib = gaussian_rasterizer.rasterize(m2, dep, rad, con, colors, opa, torch.zeros(3, device=device),
+                                                      W, H)[2]
+            padded = torch.zeros(ty * 16, tx * 16, dtype=torch.int32, device=device)
+            padded[:H, :W] = n_contrib
+            walked = padded.view(ty * 2, 8, tx, 16).amax(dim=(1, 3))  # per half tile: entries walked
+            visited = walked.view(ty, 2 * tx).sum(dim=1).double()
+            weights = (visited + 1.0).tolist()
+        if args.band_weights == "cost":
+            vis = rad > 0
+            rows_of = (m2[vis, 1].clamp(0.0, H - 1.0) // 16).long()
+            centres = torch.bincount(rows_of, minlength=ty).double()
+            share = 0.69 * visited / visited.sum().clamp(min=1.0) + 0.31 * centres / centres.sum().clamp(min=1.0)
+            weights = (share + 1e-9).tolist()
+        starts, init = None, feature_block_init(device, C)
+        if world > 1 and args.row_owners == "bands":
+            from hds_b200.parallel import row_bands
+
+            perm, starts = band_split.band_order(m2, rad, row_bands(H, world, weights))
+            # The same scene in band order: every parameter row moves with its gaussian.
+            raw = {k: v.detach()[perm].contiguous().requires_grad_(True) for k, v in raw.items()}
+            init = feature_rows_init(device, C, perm)
+    features = band_split.FeatureShards(s.n, C, rank, world, device, init=init, starts=starts)
     lrs = [optim.REFERENCE_LRS[k] * (5.0 if k == "means" else 1.0) for k in raw] + [optim.REFERENCE_LRS["features"]]
     trainer = band_split.BandSplitTrainer(raw, features, cam, lrs, rank, world, row_weights=weights)
     y0, y1 = trainer.y0, trainer.y1
@@ -820,6 +875,8 @@ def run_band_split(args, device, rank, world, dist, timer):
             "data": "synthetic (seeded config-4 distribution)",
             "config": {"workload": "config4: one 1920x1080 view split by tile rows, full fwd+bwd+Adam step",
                        "gaussians": s.n, "channels": C, "parallelism": f"tile-row bands x{world}",
+                       "row_owners": args.row_owners if world > 1 else "one rank",
+                       "band_weights": args.band_weights,
                        "bands": trainer.bands, "l2": "inputs larger than L2 (feature table "
                        f"{s.n * C * 4 / 1e9:.1f} GB)"},
             "call_ms_per_step": {k: v / args.steps for k, v in sorted(calls.items(), key=lambda kv: -kv[1])},

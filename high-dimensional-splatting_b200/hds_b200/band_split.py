@@ -18,8 +18,10 @@ single-GPU; this module is the multi-GPU plan built around its rasterizer:
   neighbouring band: ranks exchange those rows (HaloExchange), each rank's SSIM covers the windows
   centred on its own rows, and the part of its SSIM gradient that falls on a neighbour's rows is sent
   back to that neighbour (BandSSIM).
-* Geometry and SH gradients are partial sums over each band's pixels: one all-reduce of their flat
-  bucket gives every rank the full gradient, and every rank applies the same Adam step.
+* Geometry and SH gradients are partial sums over each band's pixels: a reduce-scatter of their flat
+  bucket gives every rank the full gradient of its 1/world shard, each rank steps its shard
+  (ShardedFlatAdam) and an all-gather returns the stepped parameters to every rank -- on the wire an
+  all-reduce.
 
 Collectives are torch.distributed calls (NCCL on GPUs, gloo on CPU), issued in the same order on
 every rank.
@@ -52,16 +54,29 @@ class FeatureShards:
     set of global ids, fetched from their owners; combine(ids, grads) adds per-row gradients into the
     owners' rows.grad.
 
+    starts: optional block boundaries ([world + 1] ints from 0 to n, non-decreasing): rank r owns rows
+    [starts[r], starts[r + 1]).  Equal blocks by default; a scene ordered by band_order() passes the
+    blocks that make each rank own the rows of its band.
+
     owner: optional [n] tensor of owning ranks.  Giving each row to the band whose pixels hold its
     gaussian's centre keeps most of a band's rows on its own rank, so that dispatch and combine move
     only the rows of gaussians that reach across a band boundary.  With an owner map, init takes the
     owned global ids (a 1-D int64 tensor) instead of a [start, end) block."""
 
-    def __init__(self, n: int, channels: int, rank: int, world: int, device, group=None, init=None, owner=None):
+    def __init__(self, n: int, channels: int, rank: int, world: int, device, group=None, init=None, owner=None,
+                 starts=None):
         self.n, self.channels, self.rank, self.world, self.group = n, channels, rank, world, group
+        if owner is not None and starts is not None:
+            raise ValueError("give an owner map or block boundaries, not both")
         if owner is None:
             self.owner = None
-            self.starts = [n * r // world for r in range(world + 1)]
+            if starts is None:
+                starts = [n * r // world for r in range(world + 1)]
+            starts = [int(x) for x in starts]
+            if (len(starts) != world + 1 or starts[0] != 0 or starts[-1] != n
+                    or any(b < a for a, b in zip(starts, starts[1:]))):
+                raise ValueError("starts must rise from 0 to n in world + 1 steps")
+            self.starts = starts
             self.start, self.end = self.starts[rank], self.starts[rank + 1]
             local = self.end - self.start
             rows = init(self.start, self.end) if init is not None else torch.zeros(local, channels)
@@ -136,6 +151,42 @@ class FeatureShards:
                 idx = local[off:off + k]
                 g[idx] = g[idx] + back[off:off + k]
             off += k
+
+
+def band_order(means2D: torch.Tensor, radii: torch.Tensor, bands: list[tuple[int, int]]):
+    """An order of the scene's gaussians in which rank r's block of rows is the gaussians of its band.
+
+    Each visible gaussian goes to the band whose rows hold its projected centre (clamped into the
+    image); the invisible ones fill the ranks with the fewest rows, towards n / world each, so that
+    the feature Adam steps stay as even as the bands allow.  Returns (perm [n] int64: the global id
+    at each new position, ascending within each block; starts: the block boundaries for
+    FeatureShards).  With the scene's rows permuted by perm, in-place band rendering fetches only the
+    rows of gaussians whose footprints reach across a band boundary."""
+    n, world = means2D.shape[0], len(bands)
+    dev = means2D.device
+    ends = torch.tensor([b[1] for b in bands[:-1]], dtype=torch.float32, device=dev)
+    y = means2D[:, 1].detach().clamp(0.0, float(bands[-1][1] - 1))
+    owner = torch.searchsorted(ends, y, right=True).to(torch.int64)
+    visible = radii > 0
+    counts = torch.bincount(owner[visible], minlength=world).tolist()
+    hidden = torch.nonzero(~visible).squeeze(1)
+    left = hidden.numel()
+    # Water-fill: raise the smallest blocks first.
+    share = [0] * world
+    for r in sorted(range(world), key=lambda r: counts[r]):
+        target = n // world + (1 if r < n % world else 0)
+        take = min(left, max(0, target - counts[r]))
+        share[r] += take
+        left -= take
+    for i in range(left):
+        share[i % world] += 1
+    owner[hidden] = torch.repeat_interleave(torch.arange(world, device=dev), torch.tensor(share, device=dev))
+    perm = torch.argsort(owner, stable=True)
+    sizes = torch.bincount(owner, minlength=world).tolist()
+    starts = [0]
+    for k in sizes:
+        starts.append(starts[-1] + k)
+    return perm, starts
 
 
 def band_owner(means2D: torch.Tensor, radii: torch.Tensor, bands: list[tuple[int, int]]) -> torch.Tensor:
@@ -265,31 +316,31 @@ def bin_band(means2D, depths, radii, conics, colors, opacities, width: int, y0: 
 
 def bin_band_in_place(means2D, depths, radii, conics, colors, opacities, width: int, y0: int, y1: int, start: int,
                       end: int):
-    """bin_band for a rank that owns the feature rows [start, end): the band is rendered over a table of
-    n_local + R rows -- the owned rows in place, then the R rows of the band's other gaussians, fetched
-    from their owners.  Returns (pos_ids [n_local + R]: the global id of each table row, values
-    renamed to table rows, ranges, the packed conic / color_opacity rows of the table, remote_ids [R]:
-    the sorted ids of the fetched rows, the number of gaussians in the band's lists).  Table rows of
-    owned gaussians outside the band are unused."""
+    """bin_band for a rank that owns the feature rows [start, end): the band renders over a table of
+    rows in ascending global id -- the a reachable gaussians below start, the owned block (all of it,
+    in place), then the b reachable gaussians from end on.  Only the table's gaussians are binned:
+    every per-gaussian step of the binning is independent of the others and the sorts are stable in
+    table order, which is global-id order, so the lists are the full-scene band's lists with each id
+    replaced by its table row.  Returns (pos_ids [a + n_local + b]: the global id of each table row,
+    values in table rows, ranges, the packed conic / color_opacity rows of the table, remote_ids
+    [a + b]: the sorted ids of the rows to fetch, a).  The reach is band_reach_mask's superset, so a
+    few fetched rows (and unreachable owned rows) hold no pair."""
     from .gaussian_rasterizer import _bin
 
     with torch.no_grad():
         dev = means2D.device
-        conic, co, values, ranges, _ = _bin(means2D.contiguous(), depths.contiguous(), radii.contiguous(),
-                                            conics.contiguous(), colors.contiguous(), opacities.contiguous(), width,
-                                            y1 - y0, origin_y=y0)
-        n, n_local = means2D.shape[0], end - start
-        mask = torch.zeros(n, dtype=torch.bool, device=dev)
-        mask[values.long()] = True
-        in_band = mask.sum()
-        mask[start:end] = False
-        remote_ids = torch.nonzero(mask).squeeze(1)
-        pos_ids = torch.cat([torch.arange(start, end, device=dev), remote_ids])
-        rename = torch.empty(n, dtype=torch.int32, device=dev)
-        rename[pos_ids] = torch.arange(pos_ids.numel(), dtype=torch.int32, device=dev)
-        values_c = rename[values.long()].contiguous()
-        return (pos_ids, values_c, ranges, conic[pos_ids].contiguous(), co[pos_ids].contiguous(), remote_ids,
-                int(in_band))
+        reach = band_reach_mask(means2D, radii, y0, y1)
+        reach[start:end] = False
+        remote_ids = torch.nonzero(reach).squeeze(1)
+        a = int(torch.searchsorted(remote_ids, torch.tensor([start], device=dev)).item())
+        pos_ids = torch.cat([remote_ids[:a], torch.arange(start, end, device=dev), remote_ids[a:]])
+
+        def rows(t):
+            return t.detach()[pos_ids].contiguous()
+
+        conic, co, values, ranges, _ = _bin(rows(means2D), rows(depths), rows(radii), rows(conics), rows(colors),
+                                            rows(opacities), width, y1 - y0, origin_y=y0)
+        return pos_ids, values, ranges, conic, co, remote_ids, a
 
 
 class CompactBandRender(torch.autograd.Function):
@@ -369,7 +420,7 @@ class BandSplitTrainer:
 
     def __init__(self, raw: dict, features: FeatureShards, camera, lrs: list[float], rank: int, world: int,
                  group=None, row_weights=None):
-        from .optim import FlatAdam
+        from .optim import FlatAdam, ShardedFlatAdam
         from .parallel import GradBucket
 
         self.raw, self.features, self.camera = raw, features, camera
@@ -378,18 +429,36 @@ class BandSplitTrainer:
         self.y0, self.y1 = self.bands[rank]
         self.halo = HaloExchange(self.bands, rank, group)
         self.leaves = list(raw.values())
-        self.bucket = GradBucket(self.leaves)
-        self.opt = FlatAdam(self.leaves, lrs[:len(self.leaves)], eps=1e-15, bucket=self.bucket)
+        # Geometry and SH: with several ranks, each steps 1/world of them (reduce-scatter of the bands'
+        # partial gradients, Adam on the shard, all-gather), the same update as an all-reduce and a
+        # replicated Adam step with 1/world of the optimizer's memory traffic.
+        if world > 1:
+            self.opt = ShardedFlatAdam(self.leaves, lrs[:len(self.leaves)], group=group, eps=1e-15)
+            self.bucket = self.opt.bucket
+        else:
+            self.bucket = GradBucket(self.leaves)
+            self.opt = FlatAdam(self.leaves, lrs[:len(self.leaves)], eps=1e-15, bucket=self.bucket)
         # With contiguous row blocks each band renders over a table of this rank's own rows (in place,
-        # in the optimizer's flat buffer) followed by the fetched rows of other ranks' gaussians (its
-        # tail), and the backward adds straight into the same layout of the gradient bucket.
+        # in the optimizer's flat buffer) between the fetched rows of other ranks' gaussians (in its
+        # head and tail reserves, in global-id order), and the backward adds straight into the same
+        # layout of the gradient bucket.
         self.in_place = world > 1 and features.owner is None
-        tail = (features.n - features.rows.shape[0]) * features.channels if self.in_place else 0
-        self.feature_opt = FlatAdam([features.rows], lrs[len(self.leaves):], eps=1e-15, tail=tail)
+        head = features.start * features.channels if self.in_place else 0
+        tail = (features.n - features.end) * features.channels if self.in_place else 0
+        self.feature_opt = FlatAdam([features.rows], lrs[len(self.leaves):], eps=1e-15, head=head, tail=tail)
         self.ssim_fns = gpu_ssim_fns()
         self.timer = PhaseTimer()
-        self.band_gaussians = 0  # gaussians in this rank's band lists at the last step
+        self.band_gaussians = 0  # gaussians in this rank's band table (in place) or lists at the last step
         self.fetched_rows = 0  # feature rows fetched from other ranks at the last step
+
+    def geometry_grad(self) -> torch.Tensor:
+        """The last step's geometry + SH gradient summed over the bands (flat, the leaves' order).  With
+        several ranks this gathers the reduce-scattered shards: a collective every rank must call."""
+        if self.world == 1:
+            return self.bucket.flat
+        shards = torch.empty(self.opt.shard * self.world, device=self.opt.grad_shard.device)
+        dist.all_gather_into_tensor(shards, self.opt.grad_shard, group=self.group)
+        return shards[:sum(p.numel() for p in self.leaves)]
 
     def step(self, gt: torch.Tensor, feature_grad: torch.Tensor) -> torch.Tensor:
         """One forward + backward of the view and one optimizer step.  gt: the full view's [H, W, 3]
@@ -405,7 +474,8 @@ class BandSplitTrainer:
         y0, y1 = self.y0, self.y1
         t.mark("clear")
         self.bucket.zero_async()
-        self.feature_opt.bucket.zero()
+        if not self.in_place:
+            self.feature_opt.bucket.zero()
         pose = cam.world_to_camera
         center = -(pose[:3, :3].T @ pose[:3, 3])
         bg = torch.zeros(3, device=pose.device)
@@ -426,15 +496,24 @@ class BandSplitTrainer:
                 f = self.features
                 binned = bin_band_in_place(means2D, depths, radii, conics, colors, opacities, W, y0, y1, f.start,
                                            f.end)
-                remote = binned[5]
-                self.band_gaussians = binned[6]
+                remote, a = binned[5], binned[6]
+                self.band_gaussians = binned[0].numel()
                 self.fetched_rows = remote.numel()
                 n_local, Cf = f.end - f.start, f.channels
-                rows_t = (n_local + remote.numel()) * Cf
-                table = self.feature_opt.flat[:rows_t].view(-1, Cf)
-                grad_table = self.feature_opt.bucket.flat[:rows_t].view(-1, Cf)
+                # The table: a fetched rows, the owned block (in place), the other fetched rows -- a
+                # window of the optimizer's flat buffer around its parameters, and of its bucket.
+                lo, hi = (self.feature_opt.head // Cf - a) * Cf, (self.feature_opt.head // Cf + n_local +
+                                                                   remote.numel() - a) * Cf
+                table = self.feature_opt.flat[lo:hi].view(-1, Cf)
+                # Only the rows this step uses are cleared: the owned rows (every one is stepped) and
+                # the fetched ones; the rest of the reserve is never read.
+                grad_table = self.feature_opt.bucket.flat[lo:hi].view(-1, Cf)
+                grad_table.zero_()
+                self.feature_opt.bucket.attach()
                 t.mark("dispatch")
-                f.dispatch(remote, out=table[n_local:])
+                fetched = f.dispatch(remote)
+                table[:a] = fetched[:a]
+                table[a + n_local:] = fetched[a:]
                 t.mark("render")
                 image, feat = CompactBandRender.apply(means2D, conics, colors, opacities, table, binned, bg, W, y0,
                                                       y1, grad_table)
@@ -463,11 +542,9 @@ class BandSplitTrainer:
             t.mark("combine")
             if self.in_place:
                 n_local = self.features.end - self.features.start
-                self.features.combine(ids, grad_table[n_local:])
+                self.features.combine(ids, torch.cat([grad_table[:a], grad_table[a + n_local:]]))
             else:
                 self.features.combine(ids, rows.grad)
-            t.mark("all_reduce")
-            self.bucket.all_reduce(self.group)
         t.mark("adam")
         self.opt.step()
         self.feature_opt.step()

@@ -100,8 +100,9 @@ def densify_and_prune(opt: FlatAdam, stats: DensifyStats, grad_threshold: float,
     new_flat = torch.empty(total, device=dev)
     new_m, new_v = torch.empty_like(new_flat), torch.empty_like(new_flat)
     w_arr = (ctypes.c_int * len(widths))(*widths)
+    params = opt.flat[opt.head:opt.head + opt.n]  # the parameters, past any head reserve
     check(lib.hds_densify_apply(n, n_new, len(widths), w_arr, LAYOUT.index("means"), LAYOUT.index("log_scales"),
-                                float(0.8 * into), ptr(src), ptr(flags), ptr(child_offset), ptr(opt.flat),
+                                float(0.8 * into), ptr(src), ptr(flags), ptr(child_offset), ptr(params),
                                 ptr(opt.exp_avg), ptr(opt.exp_avg_sq), ptr(new_flat), ptr(new_m), ptr(new_v),
                                 stream_of(dev)))
     new_opt = FlatAdam.from_buffers(shapes, new_flat, new_m, new_v, opt.lrs, opt.step_count, opt.betas, opt.eps)

@@ -51,12 +51,13 @@ class FlatAdam:
     and, unless a bucket over the same parameters is given, a GradBucket is made for their gradients.
     step() runs one kernel over all parameters; lrs can change between steps (set_lr).
 
-    tail: zero elements appended to the flat buffer and to the gradient bucket beyond the parameters
-    (not stepped, no moments): room for rows that are rendered, and differentiated, beside the
-    parameters' own (the tile-row split's fetched feature rows)."""
+    head, tail: zero elements placed before and after the parameters in the flat buffer and in the
+    gradient bucket (not stepped, no moments): room for rows that are rendered, and differentiated,
+    beside the parameters' own (the tile-row split's fetched feature rows, which sort before and after
+    the owned block)."""
 
     def __init__(self, params: list[torch.Tensor], lrs: list[float], betas=(0.9, 0.999), eps: float = 1e-15,
-                 bucket: GradBucket | None = None, tail: int = 0):
+                 bucket: GradBucket | None = None, tail: int = 0, head: int = 0):
         if not params or len(params) != len(lrs):
             raise ValueError("one learning rate per parameter")
         if len(params) > MAX_SEGMENTS:
@@ -69,23 +70,25 @@ class FlatAdam:
         self.lrs = [float(x) for x in lrs]
         self.betas = betas
         self.eps = eps
-        if tail and bucket is not None:
-            raise ValueError("a tail needs the optimizer's own bucket")
+        if (head or tail) and bucket is not None:
+            raise ValueError("a head or tail needs the optimizer's own bucket")
         with torch.no_grad():
-            self.flat = torch.cat([p.detach().reshape(-1) for p in params] +
+            self.flat = torch.cat(([torch.zeros(head, dtype=torch.float32, device=dev)] if head else []) +
+                                  [p.detach().reshape(-1) for p in params] +
                                   ([torch.zeros(tail, dtype=torch.float32, device=dev)] if tail else [])).contiguous()
         ends, off = [], 0
         for p in params:
             n = p.numel()
-            p.data = self.flat[off:off + n].view_as(p)
+            p.data = self.flat[head + off:head + off + n].view_as(p)
             off += n
             ends.append(off)
         self.segment_ends = ends
         self.n = off
+        self.head = head
         self.exp_avg = torch.zeros(off, dtype=torch.float32, device=dev)
         self.exp_avg_sq = torch.zeros_like(self.exp_avg)
         if bucket is None:
-            bucket = GradBucket(params, capacity=off + tail)
+            bucket = GradBucket(params, capacity=head + off + tail, offset=head)
         elif bucket.flat.numel() != off or any(a is not b for a, b in zip(bucket.params, params)):
             raise ValueError("the bucket must cover the same parameters in the same order")
         self.bucket = bucket
@@ -98,7 +101,7 @@ class FlatAdam:
         the given shapes as views of `flat`, with their own gradient bucket, and the given moments."""
         self = cls.__new__(cls)
         self.flat, self.exp_avg, self.exp_avg_sq = flat, exp_avg, exp_avg_sq
-        self.n = flat.numel()
+        self.n, self.head = flat.numel(), 0
         self.lrs, self.betas, self.eps, self.step_count = [float(x) for x in lrs], betas, eps, step_count
         params, ends, off = [], [], 0
         for shape in shapes:
@@ -124,9 +127,9 @@ class FlatAdam:
     def step(self) -> None:
         self.bucket.ready()
         self.step_count += 1
-        n = self.n
-        adam_step(self.flat[:n], self.exp_avg, self.exp_avg_sq, self.bucket.flat[:n], self.segment_ends, self.lrs,
-                  self.step_count, self.betas, self.eps)
+        h, n = self.head, self.n
+        adam_step(self.flat[h:h + n], self.exp_avg, self.exp_avg_sq, self.bucket.flat[h:h + n], self.segment_ends,
+                  self.lrs, self.step_count, self.betas, self.eps)
 
 
 def shard_segments(segment_ends, lo: int, length: int) -> list[int]:

@@ -71,14 +71,15 @@ class GradBucket:
     attach() points every parameter's .grad at its slice, so autograd accumulates in place across
     views; all_reduce() then sums all gradients over ranks with a single collective."""
 
-    def __init__(self, params: list[torch.Tensor], capacity: int = 0):
+    def __init__(self, params: list[torch.Tensor], capacity: int = 0, offset: int = 0):
         """capacity: the flat buffer's length when it must exceed the parameters' (zero padding at
-        the end, e.g. to split it evenly across ranks)."""
+        the end, e.g. to split it evenly across ranks); offset: elements before the first parameter's
+        slice (zero padding at the start)."""
         self.params = params
         total = sum(p.numel() for p in params)
-        self.flat = torch.zeros(max(total, capacity), dtype=torch.float32, device=params[0].device)
+        self.flat = torch.zeros(max(offset + total, capacity), dtype=torch.float32, device=params[0].device)
         self.views = []
-        off = 0
+        off = offset
         for p in params:
             self.views.append(self.flat[off:off + p.numel()].view_as(p))
             off += p.numel()

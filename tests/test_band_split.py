@@ -2,7 +2,8 @@
 
 * FeatureShards: rows dispatched from their owners equal the full table's rows; gradients combined
   from every band land summed on the owners -- with contiguous row blocks, and with an owner map
-  (band_owner on a scene's projected centres).
+  (band_owner on a scene's projected centres), and with uneven blocks of a scene put in band order
+  (band_order).
 * HaloExchange + BandSSIM (with the oracle's SSIM): the bands' shares add up to the full image's mean
   SSIM, and the folded band gradients equal the full image's SSIM gradient row for row.
 """
@@ -84,6 +85,16 @@ def _worker(rank, port, queue):
         grads_m = [None] * WORLD
         dist.all_gather_object(grads_m, (mapped.ids_local.numpy().copy(), mapped.rows.grad.numpy().copy()))
 
+        # The scene in band order: uneven blocks, rank r's block holding the gaussians of band r.
+        perm, starts = band_split.band_order(means2D, radii, parallel.row_bands(H, WORLD))
+        ordered = band_split.FeatureShards(N, C, rank, WORLD, "cpu", init=lambda a, b: table_rows(0, N)[perm[a:b]],
+                                           starts=starts)
+        rows_o = ordered.dispatch(ids)
+        ordered_ok = torch.equal(rows_o, table_rows(0, N)[perm[ids]])
+        ordered.combine(ids, torch.full((len(ids), C), float(rank + 1)))
+        grads_o = [None] * WORLD
+        dist.all_gather_object(grads_o, (ordered.start, ordered.rows.grad.numpy().copy()))
+
         img, gt = images()
         bands = parallel.row_bands(H, WORLD)
         y0, y1 = bands[rank]
@@ -95,7 +106,8 @@ def _worker(rank, port, queue):
         shares = [None] * WORLD
         dist.all_gather_object(shares, (float(share), band.grad.numpy().copy()))
         queue.put((rank, {"rows_ok": rows_ok, "grads": grads, "ssim": shares, "mapped_ok": mapped_ok,
-                          "grads_mapped": grads_m, "owner": owner.numpy()}))
+                          "grads_mapped": grads_m, "owner": owner.numpy(), "ordered_ok": ordered_ok,
+                          "grads_ordered": grads_o, "starts": starts}))
     finally:
         dist.destroy_process_group()
 
@@ -137,6 +149,47 @@ def test_feature_shards_with_an_owner_map(results):
         assert np.array_equal(owner[ids_local], np.full(len(ids_local), r))
         got[ids_local] = g
     assert np.array_equal(got, want)  # every row owned exactly once, gradients summed
+
+
+def test_feature_shards_in_band_order(results):
+    assert all(results[r]["ordered_ok"] for r in range(WORLD))
+    want = np.zeros((N, C), np.float32)
+    for r in range(WORLD):
+        want[rank_ids(r).numpy()] += r + 1
+    got = np.full((N, C), np.nan, np.float32)
+    starts = results[0]["starts"]
+    for r, (start, g) in enumerate(results[0]["grads_ordered"]):
+        assert start == starts[r] and len(g) == starts[r + 1] - starts[r]
+        got[start:start + len(g)] = g
+    assert np.array_equal(got, want)
+
+
+def test_band_order_puts_each_band_in_its_block():
+    from hds_b200 import band_split, parallel
+
+    gen = torch.Generator().manual_seed(5)
+    n, world = 2000, 3
+    means2D = torch.rand(n, 2, generator=gen) * torch.tensor([float(W), 1.5 * H]) - torch.tensor([0.0, 0.25 * H])
+    radii = (torch.rand(n, generator=gen) > 0.3).float() * 3.0
+    bands = parallel.row_bands(H, world, [1.0 + 4.0 * (y < H // 4) for y in range((H + 15) // 16)])
+    perm, starts = band_split.band_order(means2D, radii, bands)
+    assert sorted(perm.tolist()) == list(range(n)) and starts[0] == 0 and starts[-1] == n
+    y = means2D[:, 1].clamp(0.0, H - 1.0)
+    for r, (y0, y1) in enumerate(bands):
+        block = perm[starts[r]:starts[r + 1]]
+        assert torch.all(block[1:] > block[:-1])  # ascending within a block
+        vis = block[radii[block] > 0]
+        lo = y0 if r > 0 else -1.0
+        assert torch.all((y[vis] >= lo) & (y[vis] < y1)), r
+        # Every visible gaussian of band r is in block r.
+        in_band = torch.nonzero((radii > 0) & (y >= lo) & (y < y1)).squeeze(1)
+        assert set(in_band.tolist()) <= set(block.tolist())
+    # The hidden gaussians raise the smaller blocks towards n / world before the larger ones grow.
+    sizes = [starts[r + 1] - starts[r] for r in range(world)]
+    vis_sizes = [int(((radii > 0) & (y >= (bands[r][0] if r else -1.0)) & (y < bands[r][1])).sum())
+                 for r in range(world)]
+    assert sum(sizes) == n and all(s >= v for s, v in zip(sizes, vis_sizes))
+    assert max(sizes) == max(max(vis_sizes), -(-n // world))
 
 
 def test_band_ssim_matches_full_image(results):

@@ -118,3 +118,35 @@ def test_sharded_flat_adam_on_one_rank_equals_flat_adam():
             assert torch.equal(p.detach(), q.detach())
     finally:
         dist.destroy_process_group()
+
+
+def test_flat_adam_with_head_and_tail_reserves_steps_only_the_parameters():
+    """FlatAdam(head=, tail=) keeps zero reserves before and after the parameters in the flat buffer
+    and the bucket (the tile-row split renders fetched rows there): the parameters step exactly as
+    without reserves, and the reserves are neither stepped nor touched."""
+    from hds_b200.optim import FlatAdam
+
+    a, b = _leaves(5), _leaves(5)
+    plain = FlatAdam(a, LRS, eps=1e-15)
+    head, tail = 24, 40
+    reserved = FlatAdam(b, LRS, eps=1e-15, head=head, tail=tail)
+    n = plain.n
+    assert reserved.flat.numel() == head + n + tail and reserved.bucket.flat.numel() == head + n + tail
+    assert b[0].data_ptr() == reserved.flat[head:].data_ptr()
+    for step in range(1, 4):
+        grads = _grads(5, step)
+        plain.zero_grad()
+        reserved.zero_grad()
+        for p, q, gr in zip(a, b, grads):
+            p.grad.add_(gr)
+            q.grad.add_(gr)
+        # Whatever lands in the reserves (rows rendered beside the parameters) is not stepped.
+        reserved.bucket.flat[:head] = 1.0
+        reserved.bucket.flat[head + n:] = 1.0
+        reserved.flat[:head] = 7.0
+        plain.step()
+        reserved.step()
+    torch.cuda.synchronize()
+    for p, q in zip(a, b):
+        assert torch.equal(p.detach(), q.detach())
+    assert torch.all(reserved.flat[:head] == 7.0) and torch.all(reserved.flat[head + n:] == 0.0)

@@ -1,7 +1,8 @@
 """The tile-row split end to end on two GPUs (hds_b200.band_split over NCCL): one training step of a
 config-4-like view split into two bands gives the same loss and the same gradients -- geometry and SH
 after their all-reduce, features after the combine at their owners -- as the whole view on one GPU,
-with the feature table split in row blocks or by an owner map.  Needs two GPUs; skipped otherwise."""
+with the feature table split in row blocks, by an owner map, or in uneven blocks of a scene put in
+band order (both runs then render the same reordered scene).  Needs two GPUs; skipped otherwise."""
 import os
 import socket
 
@@ -20,7 +21,7 @@ def free_port():
         return s.getsockname()[1]
 
 
-def _run(rank, world, port, queue, owner_map=False):
+def _run(rank, world, port, queue, mode="blocks"):
     import torch.distributed as dist
 
     from hds_b200 import band_split, optim, scenes
@@ -38,13 +39,27 @@ def _run(rank, world, port, queue, owner_map=False):
                "opacity_logits": torch.log(op / (1 - op)), "sh_dc": s.sh_dc, "sh_rest": s.sh_rest}
         raw = {k: v.to(device).contiguous().requires_grad_(True) for k, v in raw.items()}
         table = torch.randn(N, C, generator=torch.Generator().manual_seed(3))
-        if owner_map and world > 1:
+        starts = None
+        if mode == "band_order":
+            from hds_b200.parallel import row_bands
+            from hds_b200.projection import project_gaussians_raw
+
+            with torch.no_grad():
+                m2, _, rad, _, _ = project_gaussians_raw(raw["means"], raw["log_scales"], raw["quats"],
+                                                         raw["opacity_logits"], cam.world_to_camera, cam.fx, cam.fy,
+                                                         cam.cx, cam.cy, cam.width, cam.height)
+            perm, two_starts = band_split.band_order(m2, rad, row_bands(cam.height, 2))
+            raw = {k: v.detach()[perm].contiguous().requires_grad_(True) for k, v in raw.items()}
+            table = table[perm.cpu()]
+            starts = two_starts if world > 1 else None
+        if mode == "owner_map" and world > 1:
             owner = torch.randint(0, world, (N,), generator=torch.Generator().manual_seed(6))
             feats = band_split.FeatureShards(N, C, rank, world, device, init=lambda ids: table[ids.cpu()].clone(),
                                              owner=owner)
             ids_local = feats.ids_local.cpu().numpy()
         else:
-            feats = band_split.FeatureShards(N, C, rank, world, device, init=lambda a, b: table[a:b].clone())
+            feats = band_split.FeatureShards(N, C, rank, world, device, init=lambda a, b: table[a:b].clone(),
+                                             starts=starts)
             ids_local = np.arange(feats.start, feats.end)
         lrs = [optim.REFERENCE_LRS[k] for k in raw] + [optim.REFERENCE_LRS["features"]]
         trainer = band_split.BandSplitTrainer(raw, feats, cam, lrs, rank, world)
@@ -52,8 +67,9 @@ def _run(rank, world, port, queue, owner_map=False):
         gt = torch.rand(H, W, 3, generator=torch.Generator().manual_seed(4)).to(device)
         fgrad = torch.rand(H, W, C, generator=torch.Generator().manual_seed(5)).to(device) / (H * W)
         loss = trainer.step(gt, fgrad[trainer.y0:trainer.y1])
-        out = {"loss": float(loss), "geometry": trainer.bucket.flat.cpu().numpy(),
-               "features": (ids_local, feats.rows.grad.cpu().numpy()), "bands": trainer.bands}
+        out = {"loss": float(loss), "geometry": trainer.geometry_grad().cpu().numpy(),
+               "features": (ids_local, feats.rows.grad.cpu().numpy()), "bands": trainer.bands,
+               "fetched": trainer.fetched_rows}
         queue.put((rank, out))
     finally:
         if world > 1:
@@ -61,13 +77,13 @@ def _run(rank, world, port, queue, owner_map=False):
             dist.destroy_process_group()
 
 
-def _launch(world, owner_map=False):
+def _launch(world, mode="blocks"):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=_run, args=(r, world, port, queue, owner_map)) for r in range(world)]
+    procs = [ctx.Process(target=_run, args=(r, world, port, queue, mode)) for r in range(world)]
     for p in procs:
         p.start()
     out = dict(queue.get(timeout=600) for _ in range(world))
@@ -77,14 +93,14 @@ def _launch(world, owner_map=False):
     return out
 
 
-@pytest.mark.parametrize("owner_map", [False, True])
-def test_two_band_step_matches_one_gpu(owner_map):
+@pytest.mark.parametrize("mode", ["blocks", "owner_map", "band_order"])
+def test_two_band_step_matches_one_gpu(mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("the tile-row split test needs two GPUs")
     from helpers import assert_grads_close
 
-    one = _launch(1)[0]
-    two = _launch(2, owner_map)
+    one = _launch(1, mode)[0]
+    two = _launch(2, mode)
     assert len(two[0]["bands"]) == 2
     np.testing.assert_allclose(two[0]["loss"], one["loss"], rtol=1e-5)
     assert two[0]["loss"] == two[1]["loss"]
@@ -101,3 +117,6 @@ def test_two_band_step_matches_one_gpu(owner_map):
         ids_local, g = two[r]["features"]
         got[ids_local] = g
     assert_grads_close(got, one["features"][1], "feature gradients, 2 bands vs 1 GPU")
+    if mode == "band_order":
+        # Only gaussians reaching across the band edge are fetched.
+        assert two[0]["fetched"] + two[1]["fetched"] < N // 10
