@@ -196,8 +196,7 @@ __global__ void __cluster_dims__(CLUSTER, 1, 1) __launch_bounds__(THREADS, 1) fe
     } else if (role == Role::Operand) {
         // ------------------------------------------------------------------ operand warps 9-12
         const int otid = tid - OPERAND_WARP0 * 32, ow = otid >> 5;
-        const int q4 = warp & 3;                               // TMEM subpartition of this warp
-        const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;  // its lanes (channels of dF^T)
+        const int q4 = warp & 3;  // TMEM subpartition of this warp
 
         // Stage G (dL/dout of the half tile and this block's slice) as bf16 hi + lo.
         // Two rounds of 2 x CK/16 loads, all of a round issued before its first conversion, so that each
