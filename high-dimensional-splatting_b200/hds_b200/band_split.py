@@ -93,6 +93,7 @@ class FeatureShards:
         self.rows = rows.to(device=device, dtype=torch.float32).contiguous().requires_grad_(True)
         self.rows.grad = torch.zeros_like(self.rows)
         self._plan = None
+        self._side = None  # stream of dispatch_async
 
     def _local(self, ids: torch.Tensor) -> torch.Tensor:
         """Positions in rows of owned global ids."""
@@ -132,6 +133,43 @@ class FeatureShards:
             got = ordered
         self._plan = (send, recv, local, perm)
         return got
+
+    def dispatch_async(self, ids: torch.Tensor):
+        """dispatch(ids) with the fetch queued on a side stream: the counts are exchanged now (a host
+        read), then both all-to-alls and the owners' gather run on the side stream while the caller
+        queues other work.  Returns a callable that makes the current stream wait for the fetch and
+        returns the rows.  CPU tensors, one rank or an owner map: the plain dispatch, done now."""
+        if self.world == 1 or not ids.is_cuda or self.owner is not None:
+            rows = self.dispatch(ids)
+            return lambda: rows
+        own = torch.searchsorted(self._bounds, ids, right=True)
+        send_counts = torch.bincount(own, minlength=self.world)
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        send, recv = send_counts.tolist(), recv_counts.tolist()
+        current = torch.cuda.current_stream(ids.device)
+        if self._side is None:
+            self._side = torch.cuda.Stream(ids.device)
+        side = self._side
+        side.wait_stream(current)
+        with torch.cuda.stream(side):
+            wanted = torch.empty(sum(recv), dtype=ids.dtype, device=ids.device)
+            dist.all_to_all_single(wanted, ids, output_split_sizes=recv, input_split_sizes=send, group=self.group)
+            local = self._local(wanted)
+            served = self.rows.detach()[local].contiguous()
+            got = torch.empty(ids.numel(), self.channels, dtype=served.dtype, device=ids.device)
+            dist.all_to_all_single(got, served, output_split_sizes=send, input_split_sizes=recv, group=self.group)
+        ids.record_stream(side)
+        self._plan = (send, recv, local, None)
+
+        def finish():
+            waiting = torch.cuda.current_stream(ids.device)
+            waiting.wait_stream(side)
+            got.record_stream(waiting)
+            local.record_stream(waiting)
+            return got
+
+        return finish
 
     def combine(self, ids: torch.Tensor, grads: torch.Tensor) -> None:
         """Adds grads ([M, C], rows of the ids of the last dispatch) into the owners' rows.grad."""
@@ -314,19 +352,12 @@ def bin_band(means2D, depths, radii, conics, colors, opacities, width: int, y0: 
         return ids, values_c, ranges, conic[ids].contiguous(), co[ids].contiguous()
 
 
-def bin_band_in_place(means2D, depths, radii, conics, colors, opacities, width: int, y0: int, y1: int, start: int,
-                      end: int):
-    """bin_band for a rank that owns the feature rows [start, end): the band renders over a table of
-    rows in ascending global id -- the a reachable gaussians below start, the owned block (all of it,
-    in place), then the b reachable gaussians from end on.  Only the table's gaussians are binned:
-    every per-gaussian step of the binning is independent of the others and the sorts are stable in
-    table order, which is global-id order, so the lists are the full-scene band's lists with each id
-    replaced by its table row.  Returns (pos_ids [a + n_local + b]: the global id of each table row,
-    values in table rows, ranges, the packed conic / color_opacity rows of the table, remote_ids
-    [a + b]: the sorted ids of the rows to fetch, a).  The reach is band_reach_mask's superset, so a
-    few fetched rows (and unreachable owned rows) hold no pair."""
-    from .gaussian_rasterizer import _bin
-
+def band_table(means2D, radii, y0: int, y1: int, start: int, end: int):
+    """The table a rank that owns the feature rows [start, end) renders the band [y0, y1) over: rows in
+    ascending global id -- the a reachable gaussians below start, the owned block (all of it, in
+    place), then the b reachable gaussians from end on.  Returns (pos_ids [a + n_local + b]: the global
+    id of each table row, remote_ids [a + b]: the sorted ids of the rows to fetch, a).  The reach is
+    band_reach_mask's superset, so a few fetched rows (and unreachable owned rows) hold no pair."""
     with torch.no_grad():
         dev = means2D.device
         reach = band_reach_mask(means2D, radii, y0, y1)
@@ -334,13 +365,33 @@ def bin_band_in_place(means2D, depths, radii, conics, colors, opacities, width: 
         remote_ids = torch.nonzero(reach).squeeze(1)
         a = int(torch.searchsorted(remote_ids, torch.tensor([start], device=dev)).item())
         pos_ids = torch.cat([remote_ids[:a], torch.arange(start, end, device=dev), remote_ids[a:]])
+        return pos_ids, remote_ids, a
 
+
+def bin_table(pos_ids, means2D, depths, radii, conics, colors, opacities, width: int, y0: int, y1: int):
+    """Bins the band [y0, y1) over the table rows pos_ids (ascending global ids).  Every per-gaussian
+    step of the binning is independent of the others and both sorts are stable in table order, which
+    is global-id order, so the lists are the full-scene band's lists with each id replaced by its table
+    row.  Returns (values in table rows, ranges, the packed conic / color_opacity rows of the table)."""
+    from .gaussian_rasterizer import _bin
+
+    with torch.no_grad():
         def rows(t):
             return t.detach()[pos_ids].contiguous()
 
         conic, co, values, ranges, _ = _bin(rows(means2D), rows(depths), rows(radii), rows(conics), rows(colors),
                                             rows(opacities), width, y1 - y0, origin_y=y0)
-        return pos_ids, values, ranges, conic, co, remote_ids, a
+        return values, ranges, conic, co
+
+
+def bin_band_in_place(means2D, depths, radii, conics, colors, opacities, width: int, y0: int, y1: int, start: int,
+                      end: int):
+    """bin_band for a rank that owns the feature rows [start, end): band_table, then bin_table.
+    Returns (pos_ids, values in table rows, ranges, the packed conic / color_opacity rows of the table,
+    remote_ids, a)."""
+    pos_ids, remote_ids, a = band_table(means2D, radii, y0, y1, start, end)
+    values, ranges, conic, co = bin_table(pos_ids, means2D, depths, radii, conics, colors, opacities, width, y0, y1)
+    return pos_ids, values, ranges, conic, co, remote_ids, a
 
 
 class CompactBandRender(torch.autograd.Function):
@@ -494,10 +545,11 @@ class BandSplitTrainer:
             elif self.in_place:
                 t.mark("bin")
                 f = self.features
-                binned = bin_band_in_place(means2D, depths, radii, conics, colors, opacities, W, y0, y1, f.start,
-                                           f.end)
-                remote, a = binned[5], binned[6]
-                self.band_gaussians = binned[0].numel()
+                pos_ids, remote, a = band_table(means2D, radii, y0, y1, f.start, f.end)
+                # The fetch needs only the table: it runs on a side stream while the band is binned.
+                fetched = f.dispatch_async(remote)
+                binned = (pos_ids,) + bin_table(pos_ids, means2D, depths, radii, conics, colors, opacities, W, y0, y1)
+                self.band_gaussians = pos_ids.numel()
                 self.fetched_rows = remote.numel()
                 n_local, Cf = f.end - f.start, f.channels
                 # The table: a fetched rows, the owned block (in place), the other fetched rows -- a
@@ -511,7 +563,7 @@ class BandSplitTrainer:
                 grad_table.zero_()
                 self.feature_opt.bucket.attach()
                 t.mark("dispatch")
-                fetched = f.dispatch(remote)
+                fetched = fetched()
                 table[:a] = fetched[:a]
                 table[a + n_local:] = fetched[a:]
                 t.mark("render")
