@@ -547,7 +547,7 @@ class BandSplitTrainer:
                 f = self.features
                 pos_ids, remote, a = band_table(means2D, radii, y0, y1, f.start, f.end)
                 # The fetch needs only the table: it runs on a side stream while the band is binned.
-                fetched = f.dispatch_async(remote)
+                pending = f.dispatch_async(remote)
                 binned = (pos_ids,) + bin_table(pos_ids, means2D, depths, radii, conics, colors, opacities, W, y0, y1)
                 self.band_gaussians = pos_ids.numel()
                 self.fetched_rows = remote.numel()
@@ -563,7 +563,7 @@ class BandSplitTrainer:
                 grad_table.zero_()
                 self.feature_opt.bucket.attach()
                 t.mark("dispatch")
-                fetched = fetched()
+                fetched = pending()
                 table[:a] = fetched[:a]
                 table[a + n_local:] = fetched[a:]
                 t.mark("render")
