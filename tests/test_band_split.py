@@ -4,6 +4,7 @@
   from every band land summed on the owners -- with contiguous row blocks, and with an owner map
   (band_owner on a scene's projected centres), and with uneven blocks of a scene put in band order
   (band_order).
+* band_table: the rows a band renders over, in global order around the owned block.
 * HaloExchange + BandSSIM (with the oracle's SSIM): the bands' shares add up to the full image's mean
   SSIM, and the folded band gradients equal the full image's SSIM gradient row for row.
 """
@@ -201,3 +202,24 @@ def test_band_ssim_matches_full_image(results):
     np.testing.assert_allclose(total, smap.astype(np.float64).mean(), rtol=1e-6)
     stitched = np.concatenate([g for _, g in shares], axis=0)
     assert_grads_close(stitched, full_grad, "SSIM gradient stitched from bands")
+
+
+def test_band_table_is_in_global_order_around_the_owned_block():
+    """band_table (the rows a rank renders its band over): ascending global ids, the whole owned block
+    in place after the a reachable ids below it, and exactly the reachable ids outside the block as
+    the rows to fetch."""
+    from hds_b200 import band_split
+
+    gen = torch.Generator().manual_seed(8)
+    n = 3000
+    means2D = torch.rand(n, 2, generator=gen) * torch.tensor([float(W), 2.0 * H]) - torch.tensor([0.0, 0.5 * H])
+    radii = (torch.rand(n, generator=gen) > 0.2).float() * (1.0 + 6.0 * torch.rand(n, generator=gen))
+    y0, y1, start, end = 32, 64, 1100, 2100
+    pos_ids, remote, a = band_split.band_table(means2D, radii, y0, y1, start, end)
+    reach = band_split.band_reach_mask(means2D, radii, y0, y1)
+    want_remote = torch.tensor([i for i in range(n) if bool(reach[i]) and not start <= i < end], dtype=torch.int64)
+    assert torch.equal(remote, want_remote)
+    assert a == int((want_remote < start).sum())
+    assert torch.all(pos_ids[1:] > pos_ids[:-1])
+    assert torch.equal(pos_ids[a:a + end - start], torch.arange(start, end))
+    assert pos_ids.numel() == remote.numel() + end - start
