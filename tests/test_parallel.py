@@ -53,6 +53,30 @@ def test_bucket_zero_async_on_cpu_is_zero():
     assert torch.count_nonzero(bucket.flat) == 0
 
 
+def test_flat_adam_reserves_lay_out_around_the_parameters_on_cpu():
+    """FlatAdam(head=, tail=): the parameters become views of the flat buffer after `head` zeros, the
+    gradient bucket puts their slices at the same offsets, and both buffers end with `tail` zeros
+    (the layout only; the step runs the CUDA kernel and is checked on the GPU)."""
+    from hds_b200.optim import FlatAdam
+
+    params = [torch.randn(6, 4, requires_grad=True), torch.randn(5, requires_grad=True)]
+    values = [p.detach().clone() for p in params]
+    head, tail = 12, 20
+    opt = FlatAdam(params, [0.1, 0.2], head=head, tail=tail)
+    n = 6 * 4 + 5
+    assert opt.n == n and opt.head == head and opt.flat.numel() == head + n + tail
+    assert torch.count_nonzero(opt.flat[:head]) == 0 and torch.count_nonzero(opt.flat[head + n:]) == 0
+    assert torch.equal(opt.flat[head:head + 24].view(6, 4), values[0]) and torch.equal(opt.flat[head + 24:head + n],
+                                                                                         values[1])
+    assert params[0].data_ptr() == opt.flat[head:].data_ptr()
+    opt.zero_grad()
+    assert opt.bucket.flat.numel() == head + n + tail
+    assert params[0].grad.data_ptr() == opt.bucket.flat[head:].data_ptr()
+    assert params[1].grad.data_ptr() == opt.bucket.flat[head + 24:].data_ptr()
+    with pytest.raises(ValueError):
+        FlatAdam([torch.randn(3, requires_grad=True)], [0.1], head=4, bucket=parallel.GradBucket(params))
+
+
 def band_render_np(inputs, width, y0, y1, background, features=None):
     """Rows [y0, y1) of the full render: the band is an image of its own whose row 0 lies at row y0
     of the full view (origin_y), with the means in full-image pixels."""
